@@ -1,0 +1,223 @@
+"""Generate the golden fixtures under ``tests/golden/`` by running the
+reference's own, unmodified Python (``mlx_gsplat/rendering.py``,
+``optimizer.py``, ``allocator.py``) on seeded inputs.
+
+MLX is not installable here, so ``tests/golden/mlx_shim`` stands in for
+``mlx.core`` over torch-CPU (see its docstring).  The fixtures are small
+``.npz`` files committed next to this script; they pin the CPU oracle
+(``tests/test_oracle_golden.py``).  Run from the repository root:
+
+    python tests/golden/gen_golden.py [REFERENCE_ROOT]     # default /root/reference
+
+The reference checkout is needed only to regenerate; the tests read the
+committed fixtures.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(HERE, "mlx_shim"))
+sys.path.insert(0, ROOT)
+
+import mlx.core as mx  # noqa: E402  (the shim)
+from mlx_gsplat_b200 import synthetic  # noqa: E402
+
+
+def load_ref(ref_root: str, name: str):
+    path = os.path.join(ref_root, "mlx_gsplat", name + ".py")
+    spec = importlib.util.spec_from_file_location("ref_" + name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def small_scene(n, seed, wl_name="tiny-3k", sh_dim=3):
+    wl = synthetic.WORKLOADS[wl_name]
+    g = synthetic.make_gaussians(wl, seed=seed, n=n)
+    rng = np.random.default_rng(seed + 100)
+    colors = g["sh0"]
+    if sh_dim > 3:
+        colors = np.concatenate([g["sh0"], rng.normal(0, 0.5, (n, sh_dim - 3)).astype(np.float32)], 1)
+    return g, colors.astype(np.float32)
+
+
+def gen_cull(R, out):
+    wl = synthetic.WORKLOADS["tiny-3k"]
+    g = synthetic.make_gaussians(wl, seed=0, n=3000)
+    # widen the spread so that all cull edges are exercised
+    g["means"] = (g["means"] * np.float32(3.0)).astype(np.float32)
+    views, K = synthetic.make_cameras(wl, seed=2, num_views=8)
+    res = {"means": g["means"], "opacities": g["opacities"], "views": views, "K": K,
+           "width": np.int32(wl.width), "height": np.int32(wl.height)}
+    for i, vm in enumerate(views):
+        ids = R.frustum_culling_mlx(mx.array(g["means"]), mx.array(g["quats"]), mx.array(g["scales"]),
+                                    mx.array(vm), mx.array(K), wl.width, wl.height,
+                                    opacities=mx.array(g["opacities"]))
+        res[f"ids_{i}"] = np.array(ids).astype(np.int32)
+    # nothing visible: camera looking away -> the reference returns N entries of -1
+    away = views[0].copy()
+    away[:3, :3] = -away[:3, :3]
+    away[:3, 3] = -away[:3, 3]
+    ids = R.frustum_culling_mlx(mx.array(g["means"]), mx.array(g["quats"]), mx.array(g["scales"]),
+                                mx.array(away), mx.array(K), wl.width, wl.height,
+                                opacities=mx.array(g["opacities"]))
+    res["away_view"] = away
+    res["ids_away"] = np.array(ids).astype(np.int32)
+    np.savez_compressed(os.path.join(out, "cull.npz"), **res)
+
+
+def gen_raster(R, out):
+    cases = [
+        # name, n, sh_dim, W, H, RW, RH, seed
+        ("sh0", 160, 3, 48, 36, 48, 36, 10),
+        ("sh1", 160, 12, 48, 36, 48, 36, 11),
+        ("sh3", 120, 48, 40, 30, 40, 30, 12),
+        ("scaled", 140, 12, 64, 48, 32, 24, 13),
+    ]
+    res = {}
+    wl = synthetic.WORKLOADS["tiny-3k"]
+    for name, n, shd, W, H, RW, RH, seed in cases:
+        g, colors = small_scene(n, seed, sh_dim=shd)
+        views, _ = synthetic.make_cameras(wl, seed=2, num_views=3)
+        vm = views[seed % 3]
+        K = np.array([[W * 0.9, 0, W / 2.0], [0, W * 0.9, H / 2.0], [0, 0, 1]], np.float32)
+        ids = R.frustum_culling_mlx(mx.array(g["means"]), mx.array(g["quats"]), mx.array(g["scales"]),
+                                    mx.array(vm), mx.array(K), W, H, opacities=mx.array(g["opacities"]))
+        ids = mx.array(np.array(ids), dtype=mx.int32)
+        rng = np.random.default_rng(seed + 7)
+        target = rng.uniform(0, 1, (RH, RW, 3)).astype(np.float32)
+        wA = rng.uniform(-1, 1, (RH, RW, 1)).astype(np.float32)
+        tgt = mx.array(target)
+        wa = mx.array(wA)
+
+        # colours one row per visible Gaussian (the trainer's calling form)
+        col_vis = colors[np.array(ids).astype(np.int64)]
+
+        def loss_fn(p):
+            c, a = R.rasterize_gaussians_mlx(p["means"], p["quats"], p["scales"], p["opacities"], p["colors"],
+                                             mx.array(vm), mx.array(K), W, H, ids,
+                                             render_width=RW, render_height=RH, pixel_chunk_size=512)
+            return mx.mean(mx.abs(c - tgt)) + mx.mean(a * wa)
+
+        params = {"means": mx.array(g["means"]), "quats": mx.array(g["quats"]),
+                  "scales": mx.array(g["scales"]), "opacities": mx.array(g["opacities"]),
+                  "colors": mx.array(col_vis)}
+        c, a = R.rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"],
+                                         params["opacities"], params["colors"], mx.array(vm), mx.array(K),
+                                         W, H, ids, render_width=RW, render_height=RH)
+        loss, grads = mx.value_and_grad(loss_fn)(params)
+        pre = f"{name}_"
+        res.update({pre + "means": g["means"], pre + "quats": g["quats"], pre + "scales": g["scales"],
+                    pre + "opacities": g["opacities"], pre + "colors": col_vis, pre + "viewmat": vm,
+                    pre + "K": K, pre + "dims": np.array([W, H, RW, RH], np.int32),
+                    pre + "ids": np.array(ids).astype(np.int32), pre + "target": target, pre + "wA": wA,
+                    pre + "out_colors": np.array(c), pre + "out_alphas": np.array(a),
+                    pre + "loss": np.array(loss)})
+        for k, v in grads.items():
+            res[pre + "grad_" + k] = np.array(v)
+    np.savez_compressed(os.path.join(out, "raster.npz"), **res)
+
+
+def gen_adam(O, out):
+    rng = np.random.default_rng(5)
+    dims = {"means": 3, "scales": 3, "quats": 4, "opacities": 1, "sh0": 3, "shN": 9}
+    n = 50
+    p = {k: rng.normal(0, 1, (n, d)).astype(np.float32) for k, d in dims.items()}
+    m = {k: np.zeros((n, d), np.float32) for k, d in dims.items()}
+    v = {k: np.zeros((n, d), np.float32) for k, d in dims.items()}
+    opt = O.FusedMLXAdam(lr=1e-3, betas=(0.9, 0.999), eps=1e-15)
+    res = {}
+    for k in dims:
+        res["p0_" + k] = p[k]
+    for t in range(1, 4):
+        gr = {k: rng.normal(0, 0.1, (n, d)).astype(np.float32) for k, d in dims.items()}
+        for k in dims:
+            res[f"g{t}_" + k] = gr[k]
+        up, um, uv = opt.step({k: mx.array(x) for k, x in p.items()}, {k: mx.array(x) for k, x in gr.items()},
+                              {k: mx.array(x) for k, x in m.items()}, {k: mx.array(x) for k, x in v.items()},
+                              use_metal_fusion=False)
+        p = {k: np.array(x) for k, x in up.items()}
+        m = {k: np.array(x) for k, x in um.items()}
+        v = {k: np.array(x) for k, x in uv.items()}
+        for k in dims:
+            res[f"p{t}_" + k] = p[k]
+            res[f"m{t}_" + k] = m[k]
+            res[f"v{t}_" + k] = v[k]
+    np.savez_compressed(os.path.join(out, "adam_pure.npz"), **res)
+
+
+def gen_alloc(A, out):
+    rng = np.random.default_rng(9)
+    maxg, sh = 96, 1
+    alloc = A.PointerStableChunkedAllocator(max_gaussians=maxg, sh_degree=sh)
+    n0 = 60
+    dims = {"means": 3, "scales": 3, "quats": 4, "opacities": 1, "sh0": 3, "shN": 9}
+    init = {k: rng.normal(0, 1, (n0, d)).astype(np.float32) for k, d in dims.items()}
+    alloc.set_initial_gaussians({k: mx.array(x) for k, x in init.items()})
+    res = {"init_" + k: x for k, x in init.items()}
+    res["table0"] = alloc.indirection_table.copy()
+    res["free0"] = np.array(alloc.free_slots, np.int32)
+    for r in range(3):
+        n = alloc.num_active
+        prune = rng.uniform(0, 1, n) < 0.15
+        split = rng.uniform(0, 1, n) < 0.25
+        ns = int(split.sum())
+        sp = {}
+        for k, d in dims.items():
+            sp[k + "_child1"] = rng.normal(0, 1, (ns, d)).astype(np.float32)
+            sp[k + "_child2"] = rng.normal(0, 1, (ns, d)).astype(np.float32)
+        for k, x in sp.items():
+            res[f"r{r}_sp_{k}"] = x
+        res[f"r{r}_prune"] = prune
+        res[f"r{r}_split"] = split
+        n_p, n_s = alloc.split_and_prune(prune, split, {k: mx.array(x) for k, x in sp.items()})
+        res[f"r{r}_counts"] = np.array([n_p, n_s], np.int32)
+        res[f"r{r}_table"] = alloc.indirection_table.astype(np.int32).copy()
+        res[f"r{r}_free"] = np.array(alloc.free_slots, np.int32)
+        for k in dims:
+            res[f"r{r}_pool_{k}"] = np.array(alloc.physical_pools[k])
+            res[f"r{r}_m_{k}"] = np.array(alloc.adam_m_pools[k])
+    # capacity error: ask for more splits than free slots
+    n = alloc.num_active
+    split = np.ones(n, bool)
+    prune = np.zeros(n, bool)
+    ns = n
+    sp = {k + s: np.zeros((ns, d), np.float32) for k, d in dims.items() for s in ("_child1", "_child2")}
+    try:
+        alloc.split_and_prune(prune, split, {k: mx.array(x) for k, x in sp.items()})
+        res["oom_raised"] = np.array(False)
+    except MemoryError:
+        res["oom_raised"] = np.array(True)
+    np.savez_compressed(os.path.join(out, "allocator.npz"), **res)
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    torch.manual_seed(0)
+    torch.set_num_threads(1)  # a fixed summation order for the reference's matmuls
+    R = load_ref(ref_root, "rendering")
+    O = load_ref(ref_root, "optimizer")
+    cwd = os.getcwd()
+    tmp = os.path.join(ROOT, "_work", "golden_cwd")
+    os.makedirs(tmp, exist_ok=True)
+    os.chdir(tmp)  # the allocator writes a log next to its own file; keep any stray output out of the repo
+    try:
+        A = load_ref(ref_root, "allocator")
+        gen_cull(R, HERE)
+        gen_raster(R, HERE)
+        gen_adam(O, HERE)
+        gen_alloc(A, HERE)
+    finally:
+        os.chdir(cwd)
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
