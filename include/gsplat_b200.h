@@ -1,0 +1,256 @@
+/* gsplat_b200.h — C ABI of libgsplat_b200.so, the B200 (sm_100a) kernels of the
+ * 3D Gaussian Splatting training step: cull -> project -> depth sort -> tile
+ * binning + tile sort -> compositing forward -> compositing backward ->
+ * projection backward -> fused Adam over the pooled buffers -> densify/prune
+ * over the fixed-capacity pool.
+ *
+ * Conventions (every entry point):
+ *  - plain device pointers, element counts and strides (in floats); no
+ *    framework types.  The library never allocates on these paths, never
+ *    frees caller memory and mutates only the buffers documented as outputs.
+ *  - ``stream`` is a cudaStream_t passed as void*; every kernel is enqueued on
+ *    it asynchronously (NULL = the legacy default stream).  No entry point
+ *    synchronises the device.
+ *  - the return value is a GS_* status; GS_OK is 0.  gs_last_error() gives a
+ *    human-readable message for the calling thread's last failure.
+ *  - not reentrant per buffer set; callable from one host thread per device.
+ *
+ * Replaced reference interface: the pybind11 module ``mlx_gsplat_ext``
+ * (src/mlx_extensions.cpp:238-248) — launch_fused_adam_step and
+ * clear_buffer_cache — plus the pure-Python rasterizer entry points
+ * frustum_culling_mlx / rasterize_gaussians_mlx (mlx_gsplat/rendering.py:41-308),
+ * the allocator's split_and_prune (mlx_gsplat/allocator.py:185-292) and the
+ * trainer's densify policy (mlx_gsplat/trainer.py:421-519).
+ */
+#ifndef GSPLAT_B200_H
+#define GSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define GS_OK 0
+#define GS_ERR_INVALID 1  /* bad argument (null pointer, size, stride, alignment) */
+#define GS_ERR_CUDA 2     /* a CUDA runtime call or kernel launch failed */
+#define GS_ERR_CAPACITY 3 /* a caller buffer or the pool is too small */
+
+typedef void* gs_stream_t; /* cudaStream_t */
+
+const char* gs_last_error(void);
+int gs_abi_version(void);
+/* Number of kernels this library has launched in this process (all threads). */
+unsigned long long gs_kernel_launches(void);
+
+/* ------------------------------------------------------------------ types */
+
+/* Read-only Gaussian parameters.  Row ``r`` of a group lives at
+ * ``ptr + r * stride``.  Rows are addressed by an "active id" ``i``:
+ * ``r = table ? table[i] : i``.  Colours use the same row unless
+ * ``colors_by_visible`` is set, in which case colour row = visible position
+ * (the reference's rule at mlx_gsplat/rendering.py:143-146). */
+typedef struct gs_gaussians {
+    const float* means;  int64_t means_stride;  /* [., 3] world positions */
+    const float* quats;  int64_t quats_stride;  /* [., 4] (w, x, y, z), unnormalised */
+    const float* scales; int64_t scales_stride; /* [., 3] log-scales */
+    const float* opac;   int64_t opac_stride;   /* [., 1] opacity logits */
+    const float* colors; int64_t colors_stride; /* [., colors_dim] SH coefficients, DC first */
+    int32_t colors_dim;                         /* stored colour floats; >= 12 enables the SH degree-1 term */
+    int32_t colors_by_visible;
+    const int32_t* table;                       /* optional active-id -> row map */
+} gs_gaussians;
+
+/* Gradient outputs, one row per active id (never through ``table``). */
+typedef struct gs_gaussian_grads {
+    float* means;  int64_t means_stride;
+    float* quats;  int64_t quats_stride;
+    float* scales; int64_t scales_stride;
+    float* opac;   int64_t opac_stride;
+    float* colors; int64_t colors_stride;
+    int32_t colors_write;     /* colour columns written per row (>= the rasterizer's 3 or 12) */
+    int32_t colors_by_visible;
+    int32_t accumulate;       /* 1: atomically add into the rows; 0: store */
+    float reg;                /* constant added to every written geometry gradient (the trainer's 1e-5 * sum(params)) */
+    int32_t reg_color_cols;   /* the first reg_color_cols colour columns also receive ``reg`` */
+} gs_gaussian_grads;
+
+/* Pinhole camera.  ``viewmat`` is the row-major world-to-camera matrix
+ * (camera point = viewmat @ [x, y, z, 1]); pixel (i, j) of the render grid
+ * is centred at (i*sx + sx/2, j*sy + sy/2), sx = width / render_width. */
+typedef struct gs_camera {
+    float viewmat[16];
+    float fx, fy, cx, cy;
+    int32_t width, height;
+    int32_t render_width, render_height;
+} gs_camera;
+
+/* Rasterizer settings.  The dense reference composites every visible
+ * Gaussian at every pixel; the tiled kernels bin a Gaussian into a 16x16 tile
+ * only when some pixel centre of the tile can see alpha >= alpha_cutoff, and
+ * stop a pixel once its transmittance falls below transmittance_min. */
+typedef struct gs_raster_settings {
+    float alpha_cutoff;      /* e.g. 1e-8 (parity) */
+    float transmittance_min; /* e.g. 1e-6 (parity) */
+} gs_raster_settings;
+
+/* Per-tile [start, end) ranges into the tile-sorted entry list. */
+typedef struct gs_tile_range { int32_t start, end; } gs_tile_range;
+
+/* ------------------------------------------------------------------ Adam */
+
+/* Drop-in for mlx_gsplat_ext.launch_fused_adam_step (src/mlx_extensions.cpp:75-236,
+ * bound at :240-244): in place over contiguous pools ``theta/m/v [max_gaussians, dim]``
+ * with dense gradients ``g [num_active, dim]`` and ``indices [num_active]``
+ * (logical -> physical row).  Semantics of the reference kernel (:102-152):
+ * NaN gradients -> 0, weight decay, NaN/Inf moments and step -> 0, float32
+ * bias corrections, clamp to [a_min, a_max].  Addresses are device pointers
+ * carried as integers, as in the reference. */
+int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, uint64_t m_addr, uint64_t v_addr,
+                              uint64_t indices_addr, size_t max_gaussians, size_t num_active, int dim,
+                              float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                              float a_min, float a_max, gs_stream_t stream);
+
+/* Drop-in for mlx_gsplat_ext.clear_buffer_cache (src/mlx_extensions.cpp:19-36, :245-246).
+ * Device pointers need no wrapping on CUDA, so there is no cache; returns GS_OK. */
+int gs_clear_buffer_cache(void);
+
+#define GS_ADAM_FUSED 0 /* the Metal kernel's semantics (scrub + clamp, float32 bias corrections) */
+#define GS_ADAM_PURE 1  /* mlx_gsplat/optimizer.py:146-175: lr_scale, float64 bias corrections, no scrub/clamp */
+
+/* One parameter group with explicit row strides (pools whose rows are views
+ * into a wider slab).  ``grad_scale`` multiplies g first (1/world_size after
+ * a gradient all-reduce). */
+int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const int32_t* indices,
+                        int64_t num_active, int dim, int64_t pool_stride, int64_t g_stride,
+                        float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                        float a_min, float a_max, float lr_scale, float grad_scale, int mode,
+                        gs_stream_t stream);
+
+/* All groups of a pooled slab in one float4-vectorised launch.  Pools are
+ * ``[max, stride]`` with ``stride % 4 == 0`` and 16-byte-aligned bases;
+ * columns [0, ncols) are parameters, the rest padding (left untouched).
+ * Per column: clamp bounds ``col_lo/col_hi`` and ``col_lr_scale`` (host arrays
+ * of ncols, ncols <= 64).  When ``quat_col >= 0`` (a multiple of 4) the four
+ * columns from quat_col are renormalised after the update,
+ * q / sqrt(sum q^2 + 1e-8) (mlx_gsplat/trainer.py:380-387). */
+int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
+                       int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
+                       const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
+                       float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                       float grad_scale, int mode, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ cull */
+
+/* frustum_culling_mlx (mlx_gsplat/rendering.py:41-94): writes the ascending
+ * active ids i in [0, n) that pass  z > near, z < far, the 50 px tolerance
+ * box around the image and logit >= opacity_threshold (skipped when
+ * g->opac is NULL) into ``out_ids`` and their number into ``*out_count``
+ * (device int32).  Camera-space z and the projected centre are computed in
+ * float32 with every product and sum rounded separately, left to right.
+ * Scratch: ``gs_cull_scratch_bytes(n)`` bytes at ``scratch`` (16-byte aligned). */
+size_t gs_cull_scratch_bytes(int64_t n);
+int gs_cull(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_plane, float far_plane,
+            float opacity_threshold, int32_t* out_ids, int32_t* out_count, void* scratch,
+            size_t scratch_bytes, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ sort / scan */
+
+/* Stable LSD radix sort of (key, value) uint32 pairs on bits [begin_bit, end_bit).
+ * Sorted output lands in keys_out/vals_out.  Scratch: gs_radix_sort_scratch_bytes(n). */
+size_t gs_radix_sort_scratch_bytes(int64_t n);
+int gs_radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
+                        uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, void* scratch,
+                        size_t scratch_bytes, gs_stream_t stream);
+
+/* Exclusive prefix sum of n uint32 values; out[n] (one extra slot) receives the total. */
+size_t gs_scan_scratch_bytes(int64_t n);
+int gs_exclusive_scan_u32(const uint32_t* in, uint32_t* out, int64_t n, void* scratch, size_t scratch_bytes,
+                          gs_stream_t stream);
+
+/* ------------------------------------------------------------------ rasterizer */
+
+/* Per visible Gaussian v (ids[v] is its active id): camera transform, EWA
+ * projection, conic, sigmoid opacity and the SH <= 1 colour of
+ * mlx_gsplat/rendering.py:153-244, written as a 48-byte splat record
+ * ``splats[v]`` = {u, v, conic_a, conic_b}, {conic_c, conic_d, opacity, r},
+ * {g, b, depth, 0}; the sortable depth key ``depth_keys[v]``; and
+ * ``tile_counts[v]``, the number of 16x16 tiles binned for it. */
+int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible, const gs_camera* cam,
+                       const gs_raster_settings* rs, float* splats, uint32_t* depth_keys,
+                       uint32_t* tile_counts, gs_stream_t stream);
+
+/* Offsets of each visible Gaussian's binned entries in depth order:
+ * offsets[r] = sum of tile_counts[order[q]] for q < r, and offsets[n] = the
+ * total number of entries.  Scratch: gs_bin_offsets_scratch_bytes(n). */
+size_t gs_bin_offsets_scratch_bytes(int64_t num_visible);
+int gs_bin_offsets(const uint32_t* order, const uint32_t* tile_counts, int64_t num_visible, uint32_t* offsets,
+                   void* scratch, size_t scratch_bytes, gs_stream_t stream);
+
+/* Writes the tile-binned entries of every visible Gaussian: for depth rank r,
+ * v = order[r], entries [offsets[r], offsets[r] + tile_counts[v]) get the tile
+ * id in ``tile_keys`` and v in ``entry_vals``.  ``capacity`` bounds the
+ * output arrays: a Gaussian whose entries would pass it writes nothing and
+ * sets the device flag ``*overflow_flag = 1`` (the caller zeroes it first and
+ * reads it back when it did not size the arrays from the scan total). */
+int gs_bin_emit(const float* splats, const uint32_t* order, const uint32_t* offsets, const uint32_t* tile_counts,
+                int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, uint32_t* tile_keys,
+                uint32_t* entry_vals, int64_t capacity, int32_t* overflow_flag, gs_stream_t stream);
+
+/* Fills [start, end) per tile from the tile-sorted keys (ranges must hold
+ * num_tiles entries; tiles without entries get {0, 0}). */
+int gs_tile_ranges(const uint32_t* sorted_tile_keys, int64_t num_entries, int32_t num_tiles,
+                   gs_tile_range* ranges, gs_stream_t stream);
+
+#define GS_LOSS_NONE 0       /* no loss: the backward takes dL/dcolor, dL/dalpha buffers */
+#define GS_LOSS_L1_U8 1      /* mean |C - target| with a uint8 HWC target (scaled by 1/255) */
+#define GS_LOSS_L1_F32 2     /* mean |C - target| with a float32 HWC target */
+#define GS_LOSS_MEAN 3       /* mean(C) (the reference trainer's loss without a target) */
+
+/* Front-to-back compositing per 16x16 tile with shared-memory staged splats and
+ * warp-level early termination: colour [RH, RW, 3] and alpha [RH, RW, 1]
+ * (HWC float32), the final transmittance and the number of entries each pixel
+ * consumed (for the backward).  With a loss mode, ``loss_partials[tile]``
+ * receives that tile's sum of |C - target| (or of C).  Entry values at or
+ * beyond ``num_visible`` are never dereferenced (they read splat 0). */
+int gs_render_forward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+                      int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, float* out_color, float* out_alpha,
+                      float* final_T, int32_t* n_contrib, int loss_mode, const void* target, float* loss_partials,
+                      gs_stream_t stream);
+
+/* Back-to-front gradient of the compositing: recomputes transmittance from the
+ * saved final value and accumulates per visible Gaussian, with warp-reduced
+ * atomics, the 12-float record {du, dv, dconic_a, dconic_bc}, {dconic_d,
+ * dopacity, dr, dg}, {db, 0, 0, 0} into ``splat_grads`` (zeroed by the caller).
+ * dL/dcolor comes from ``dL_dcolor`` [RH,RW,3] (+ ``dL_dalpha`` [RH,RW,1],
+ * may be NULL) for GS_LOSS_NONE, or is formed from the loss mode. */
+int gs_render_backward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+                       int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, const float* out_color,
+                       const float* final_T, const int32_t* n_contrib, int loss_mode, const void* target,
+                       const float* dL_dcolor, const float* dL_dalpha, float* splat_grads, gs_stream_t stream);
+
+/* Chains the splat gradients back to the Gaussian parameters (projection,
+ * covariance, quaternion normalisation, sigmoid, SH colour and their clip
+ * rules) and writes one gradient row per visible Gaussian.  When ``grad2d``
+ * is not NULL also adds the densification statistic
+ * sqrt(|dL/dmean|^2 + 1e-8) * |z| / fx to grad2d[table[id]] and 1 to
+ * count[table[id]] (mlx_gsplat/trainer.py:300-318). */
+int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible, const gs_camera* cam,
+                        const float* splat_grads, const gs_gaussian_grads* out, float* grad2d, float* count,
+                        gs_stream_t stream);
+
+/* ------------------------------------------------------------------ pool / densify */
+
+/* Writes ``pattern[0..stride)`` into every row r < n_rows of ``dst`` (row stride ``stride``). */
+int gs_fill_rows(float* dst, int64_t n_rows, int64_t stride, const float* pattern_host, gs_stream_t stream);
+
+/* Sets column ``col`` of rows [0, n_rows) to ``value`` (the periodic opacity
+ * reset, mlx_gsplat/trainer.py:416-419). */
+int gs_fill_column(float* dst, int64_t n_rows, int64_t stride, int col, float value, gs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSPLAT_B200_H */

@@ -1,0 +1,219 @@
+// Fused Adam over pooled parameter/moment buffers (replaces the Metal kernel
+// fused_adam_step, src/mlx_extensions.cpp:102-152, and the pure-MLX step,
+// mlx_gsplat/optimizer.py:146-175).
+//
+// Every element update is written with round-to-nearest intrinsics and no
+// fused multiply-add, in the reference kernel's operation order, so that the
+// result matches the CPU restatement bit for bit.  The slab kernel moves one
+// float4 of theta, m, v and g per thread (16-byte loads and stores), covering
+// all parameter groups of a pooled row in a single launch.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace gs {
+
+struct AdamScalars {
+    float b1, b2, omb1, omb2;  // beta, (1 - beta) as the selected semantics round them
+    float eps, wd, sqrt_bc2, grad_scale;
+    int scrub, clamp;
+};
+
+constexpr int kMaxSlabCols = 64;
+struct SlabCols {
+    float step_size[kMaxSlabCols];
+    float lo[kMaxSlabCols];
+    float hi[kMaxSlabCols];
+};
+
+__device__ __forceinline__ void adam_elem(float& th, float& m, float& v, float g, const AdamScalars& s,
+                                          float step_size, float lo, float hi) {
+    g = __fmul_rn(g, s.grad_scale);
+    if (s.scrub && isnan(g)) g = 0.0f;
+    if (s.wd != 0.0f) g = __fadd_rn(g, __fmul_rn(s.wd, th));
+    float mn = __fadd_rn(__fmul_rn(s.b1, m), __fmul_rn(s.omb1, g));
+    float vn = __fadd_rn(__fmul_rn(s.b2, v), __fmul_rn(s.omb2, __fmul_rn(g, g)));
+    if (s.scrub) {
+        if (!isfinite(mn)) mn = 0.0f;
+        if (!isfinite(vn)) vn = 0.0f;
+    }
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vn), s.sqrt_bc2), s.eps);
+    float delta = __fmul_rn(step_size, __fdiv_rn(mn, denom));
+    if (s.scrub && !isfinite(delta)) delta = 0.0f;
+    float t = __fsub_rn(th, delta);
+    if (s.clamp) t = fminf(fmaxf(t, lo), hi);
+    th = t;
+    m = mn;
+    v = vn;
+}
+
+// One thread per (active row, column) element, as the reference dispatches it.
+__global__ void adam_group_kernel(float* __restrict__ theta, const float* __restrict__ g, float* __restrict__ m,
+                                  float* __restrict__ v, const int32_t* __restrict__ idx, int64_t n_elems, int dim,
+                                  int64_t pool_stride, int64_t g_stride, AdamScalars s, float step_size, float lo,
+                                  float hi) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_elems) return;
+    const int64_t r = t / dim;
+    const int c = (int)(t - r * dim);
+    const int64_t p = (int64_t)__ldg(idx + r) * pool_stride + c;
+    float th = theta[p], mm = m[p], vv = v[p];
+    adam_elem(th, mm, vv, __ldg(g + r * g_stride + c), s, step_size, lo, hi);
+    theta[p] = th;
+    m[p] = mm;
+    v[p] = vv;
+}
+
+// One thread per float4 chunk of a pooled row.
+__global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
+                                                        float4* __restrict__ m, float4* __restrict__ v,
+                                                        const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
+                                                        int g_chunks, int ncols, int quat_chunk, AdamScalars s,
+                                                        SlabCols cols) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_rows * chunks) return;
+    const int64_t r = t / chunks;
+    const int c4 = (int)(t - r * chunks);
+    const int c0 = 4 * c4;
+    if (c0 >= ncols) return;
+    const int64_t off = (int64_t)__ldg(idx + r) * chunks + c4;
+    float4 th = theta[off], mm = m[off], vv = v[off];
+    const float4 gg = __ldg(g + r * g_chunks + c4);
+    if (c0 + 0 < ncols) adam_elem(th.x, mm.x, vv.x, gg.x, s, cols.step_size[c0 + 0], cols.lo[c0 + 0], cols.hi[c0 + 0]);
+    if (c0 + 1 < ncols) adam_elem(th.y, mm.y, vv.y, gg.y, s, cols.step_size[c0 + 1], cols.lo[c0 + 1], cols.hi[c0 + 1]);
+    if (c0 + 2 < ncols) adam_elem(th.z, mm.z, vv.z, gg.z, s, cols.step_size[c0 + 2], cols.lo[c0 + 2], cols.hi[c0 + 2]);
+    if (c0 + 3 < ncols) adam_elem(th.w, mm.w, vv.w, gg.w, s, cols.step_size[c0 + 3], cols.lo[c0 + 3], cols.hi[c0 + 3]);
+    if (c4 == quat_chunk) {
+        float ss = __fmul_rn(th.x, th.x);
+        ss = __fadd_rn(ss, __fmul_rn(th.y, th.y));
+        ss = __fadd_rn(ss, __fmul_rn(th.z, th.z));
+        ss = __fadd_rn(ss, __fmul_rn(th.w, th.w));
+        const float n = __fsqrt_rn(__fadd_rn(ss, 1e-8f));
+        th.x = __fdiv_rn(th.x, n);
+        th.y = __fdiv_rn(th.y, n);
+        th.z = __fdiv_rn(th.z, n);
+        th.w = __fdiv_rn(th.w, n);
+    }
+    theta[off] = th;
+    m[off] = mm;
+    v[off] = vv;
+}
+
+// Host-side scalars for each semantics.
+static AdamScalars make_scalars(int mode, float beta1, float beta2, float eps, float wd, int step, float grad_scale,
+                                double* bc1_out) {
+    AdamScalars s;
+    s.b1 = beta1;
+    s.b2 = beta2;
+    s.eps = eps;
+    s.wd = wd;
+    s.grad_scale = grad_scale;
+    if (mode == GS_ADAM_FUSED) {
+        // float32 everywhere, as the Metal kernel computes them (:131-146)
+        s.omb1 = 1.0f - beta1;
+        s.omb2 = 1.0f - beta2;
+        const float bc1 = 1.0f - powf(beta1, (float)step);
+        const float bc2 = 1.0f - powf(beta2, (float)step);
+        s.sqrt_bc2 = sqrtf(bc2);
+        *bc1_out = bc1;
+        s.scrub = 1;
+        s.clamp = 1;
+    } else {
+        // float64 Python scalars rounded once to float32 (optimizer.py:75-76, 162-167)
+        const double b1 = (double)beta1, b2 = (double)beta2;
+        s.omb1 = (float)(1.0 - b1);
+        s.omb2 = (float)(1.0 - b2);
+        const double bc1 = 1.0 - pow(b1, (double)step);
+        const double bc2 = 1.0 - pow(b2, (double)step);
+        s.sqrt_bc2 = (float)sqrt(bc2);
+        *bc1_out = bc1;
+        s.scrub = 0;
+        s.clamp = 0;
+    }
+    return s;
+}
+
+static float step_size_for(int mode, float lr, float lr_scale, double bc1) {
+    if (mode == GS_ADAM_FUSED) return lr / (float)bc1;  // float32 division, no lr_scales
+    return (float)(((double)lr * (double)lr_scale) / bc1);
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const int32_t* indices,
+                                   int64_t num_active, int dim, int64_t pool_stride, int64_t g_stride, float lr,
+                                   float beta1, float beta2, float eps, float weight_decay, int step, float a_min,
+                                   float a_max, float lr_scale, float grad_scale, int mode, gs_stream_t stream) {
+    GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam: unknown mode %d", mode);
+    GS_REQUIRE(num_active >= 0 && dim > 0 && step >= 1, "adam: bad sizes (num_active=%lld dim=%d step=%d)",
+               (long long)num_active, dim, step);
+    if (num_active == 0) return GS_OK;
+    GS_REQUIRE(theta && g && m && v && indices, "adam: null pointer");
+    GS_REQUIRE(pool_stride >= dim && g_stride >= dim, "adam: stride smaller than dim");
+    double bc1;
+    AdamScalars s = make_scalars(mode, beta1, beta2, eps, weight_decay, step, grad_scale, &bc1);
+    const float ss = step_size_for(mode, lr, lr_scale, bc1);
+    const int64_t n = num_active * (int64_t)dim;
+    adam_group_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(theta, g, m, v, indices, n, dim,
+                                                                          pool_stride, g_stride, s, ss, a_min, a_max);
+    return check_launch("adam_group_kernel");
+}
+
+extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
+                                  int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
+                                  const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
+                                  float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                                  float grad_scale, int mode, gs_stream_t stream) {
+    GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
+    GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
+    GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && g_stride >= ncols,
+               "adam_slab: strides must be multiples of 4 and >= ncols");
+    GS_REQUIRE(step >= 1 && num_active >= 0, "adam_slab: bad step/num_active");
+    GS_REQUIRE(quat_col < 0 || (quat_col % 4 == 0 && quat_col + 4 <= ncols), "adam_slab: bad quat_col");
+    if (num_active == 0) return GS_OK;
+    GS_REQUIRE(theta && g && m && v && indices && col_lo && col_hi, "adam_slab: null pointer");
+    GS_REQUIRE(aligned16(theta) && aligned16(g) && aligned16(m) && aligned16(v), "adam_slab: bases must be 16-byte aligned");
+    double bc1;
+    AdamScalars s = make_scalars(mode, beta1, beta2, eps, weight_decay, step, grad_scale, &bc1);
+    SlabCols cols;
+    for (int c = 0; c < kMaxSlabCols; ++c) {
+        const bool on = c < ncols;
+        cols.lo[c] = on ? col_lo[c] : 0.f;
+        cols.hi[c] = on ? col_hi[c] : 0.f;
+        cols.step_size[c] = on ? step_size_for(mode, lr, col_lr_scale ? col_lr_scale[c] : 1.0f, bc1) : 0.f;
+    }
+    const int chunks = (int)(stride / 4);
+    const int64_t n = num_active * chunks;
+    adam_slab_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
+        reinterpret_cast<float4*>(v), indices, num_active, chunks, (int)(g_stride / 4), ncols,
+        quat_col < 0 ? -1 : quat_col / 4, s, cols);
+    return check_launch("adam_slab_kernel");
+}
+
+extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, uint64_t m_addr, uint64_t v_addr,
+                                         uint64_t indices_addr, size_t max_gaussians, size_t num_active, int dim,
+                                         float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                                         float a_min, float a_max, gs_stream_t stream) {
+    (void)max_gaussians;  // the pools are addressed through the indirection table, as in the reference
+    float* theta = reinterpret_cast<float*>(theta_addr);
+    const float* g = reinterpret_cast<const float*>(g_addr);
+    float* m = reinterpret_cast<float*>(m_addr);
+    float* v = reinterpret_cast<float*>(v_addr);
+    const int32_t* idx = reinterpret_cast<const int32_t*>(indices_addr);
+    if (dim % 4 == 0 && dim <= kMaxSlabCols && aligned16(theta) && aligned16(g) && aligned16(m) && aligned16(v)) {
+        float lo[kMaxSlabCols], hi[kMaxSlabCols];
+        for (int c = 0; c < dim; ++c) {
+            lo[c] = a_min;
+            hi[c] = a_max;
+        }
+        return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
+                                  beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED, stream);
+    }
+    return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
+                               weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);
+}
+
+extern "C" int gs_clear_buffer_cache(void) { return GS_OK; }

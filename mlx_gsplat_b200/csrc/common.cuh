@@ -1,0 +1,81 @@
+// Shared helpers of the sm_100a kernels: status reporting, launch checks,
+// warp primitives and the float32 camera transform shared by cull and projection.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "gsplat_b200.h"
+
+namespace gs {
+
+constexpr int kTile = 16;               // tile edge in pixels
+constexpr int kTileThreads = kTile * kTile;
+constexpr unsigned kFull = 0xffffffffu;
+
+int set_error(int code, const char* fmt, ...);
+void note_launches(int n);  // running count of this library's kernel launches
+
+// Records ``launched`` kernel launches and reports a launch failure.
+inline int check_launch(const char* what, int launched = 1) {
+    note_launches(launched);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return GS_OK;
+}
+
+#define GS_REQUIRE(cond, ...)                                  \
+    do {                                                       \
+        if (!(cond)) return ::gs::set_error(GS_ERR_INVALID, __VA_ARGS__); \
+    } while (0)
+
+#define GS_TRY(expr)                 \
+    do {                             \
+        int _st = (expr);            \
+        if (_st != GS_OK) return _st; \
+    } while (0)
+
+inline unsigned grid_for(int64_t n, int block) { return (unsigned)((n + block - 1) / block); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// Vector reduction into global memory (16-byte aligned address).
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+// Camera-space point of world position m: row i of  viewmat @ [m, 1],
+// summed left to right with each product and sum rounded (no fused
+// multiply-add), the order the CPU oracle uses, so the cull decision
+// is reproducible bit for bit.
+__device__ __forceinline__ float cam_row(const float* vm, int i, float x, float y, float z) {
+    float s = __fmul_rn(x, vm[4 * i + 0]);
+    s = __fadd_rn(s, __fmul_rn(y, vm[4 * i + 1]));
+    s = __fadd_rn(s, __fmul_rn(z, vm[4 * i + 2]));
+    return __fadd_rn(s, vm[4 * i + 3]);
+}
+
+// Sortable unsigned key of a float: ascending float order == ascending key.
+__device__ __forceinline__ uint32_t float_sort_key(float f) {
+    uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+}  // namespace gs

@@ -1,0 +1,165 @@
+// Frustum + opacity cull with order-preserving stream compaction
+// (frustum_culling_mlx, mlx_gsplat/rendering.py:41-94).
+//
+// Pass 1: one bit per active id (warp ballot) and a count per 2048-id chunk.
+// Pass 2: exclusive scan of the chunk counts.
+// Pass 3: each chunk writes its surviving ids in ascending order.
+// Reads 16 bytes per id (means + opacity), writes 4 bytes per survivor.
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace gs {
+
+constexpr int kCullThreads = 256;
+constexpr int kCullItems = 8;
+constexpr int kCullChunk = kCullThreads * kCullItems;  // 2048 ids, 64 mask words
+
+struct CullParams {
+    float vm[16];
+    float fx, fy, cx, cy;
+    float width, height, near_p, far_p, opac_thr;
+};
+
+__device__ __forceinline__ bool cull_test(const gs_gaussians& g, const CullParams& p, int64_t i) {
+    const int64_t r = g.table ? (int64_t)__ldg(g.table + i) : i;
+    const float* mp = g.means + r * g.means_stride;
+    const float x = __ldg(mp + 0), y = __ldg(mp + 1), z = __ldg(mp + 2);
+    const float cx_ = cam_row(p.vm, 0, x, y, z);
+    const float cy_ = cam_row(p.vm, 1, x, y, z);
+    const float cz_ = cam_row(p.vm, 2, x, y, z);
+    const float ds = cz_ > p.near_p ? cz_ : p.near_p;
+    const float x2d = __fadd_rn(__fdiv_rn(__fmul_rn(cx_, p.fx), ds), p.cx);
+    const float y2d = __fadd_rn(__fdiv_rn(__fmul_rn(cy_, p.fy), ds), p.cy);
+    bool ok = (cz_ > p.near_p) && (cz_ < p.far_p) && (__fadd_rn(x2d, 50.0f) >= 0.0f) &&
+              (__fsub_rn(x2d, 50.0f) < p.width) && (__fadd_rn(y2d, 50.0f) >= 0.0f) &&
+              (__fsub_rn(y2d, 50.0f) < p.height);
+    if (g.opac) ok = ok && (__ldg(g.opac + r * g.opac_stride) >= p.opac_thr);
+    return ok;
+}
+
+// mask word w covers ids [32w, 32w + 32)
+__global__ void __launch_bounds__(kCullThreads) cull_flags(gs_gaussians g, int64_t n, CullParams p,
+                                                           uint32_t* __restrict__ words,
+                                                           uint32_t* __restrict__ chunk_counts) {
+    __shared__ uint32_t wsum[kCullThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t base = (int64_t)blockIdx.x * kCullChunk;
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int k = 0; k < kCullItems; ++k) {
+        const int64_t i = base + (int64_t)k * kCullThreads + threadIdx.x;
+        const bool ok = i < n && cull_test(g, p, i);
+        const uint32_t b = __ballot_sync(kFull, ok);
+        const int64_t wi = (base + (int64_t)k * kCullThreads + warp * 32) >> 5;
+        if (lane == 0 && (wi << 5) < n) words[wi] = b;
+        cnt += __popc(b);
+    }
+    if (lane == 0) wsum[warp] = cnt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0;
+#pragma unroll
+        for (int w = 0; w < kCullThreads / 32; ++w) t += wsum[w];
+        chunk_counts[blockIdx.x] = t;
+    }
+}
+
+__global__ void __launch_bounds__(kCullThreads) cull_write(const uint32_t* __restrict__ words, int64_t n,
+                                                           const uint32_t* __restrict__ chunk_offsets,
+                                                           int32_t* __restrict__ out_ids) {
+    __shared__ uint32_t woff[kCullChunk / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t base = (int64_t)blockIdx.x * kCullChunk;
+    const int64_t wbase = base >> 5;
+    const int64_t n_words = (n + 31) >> 5;
+    if (warp == 0) {
+        // exclusive prefix over the chunk's 64 words, two per lane
+        const int64_t w0 = wbase + 2 * lane, w1 = w0 + 1;
+        const uint32_t c0 = w0 < n_words ? __popc(words[w0]) : 0u;
+        const uint32_t c1 = w1 < n_words ? __popc(words[w1]) : 0u;
+        uint32_t inc = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(kFull, inc, o);
+            if (lane >= o) inc += y;
+        }
+        const uint32_t ex = inc - c0 - c1;
+        woff[2 * lane] = ex;
+        woff[2 * lane + 1] = ex + c0;
+    }
+    __syncthreads();
+    const uint32_t off0 = chunk_offsets[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < kCullItems; ++k) {
+        const int local_word = k * (kCullThreads / 32) + warp;
+        const int64_t wi = wbase + local_word;
+        if (wi >= n_words) break;
+        const uint32_t b = words[wi];
+        if ((b >> lane) & 1u) {
+            const uint32_t pos = off0 + woff[local_word] + __popc(b & lanemask_lt());
+            out_ids[pos] = (int32_t)((wi << 5) + lane);
+        }
+    }
+}
+
+static CullParams make_cull_params(const gs_camera& c, float near_p, float far_p, float thr) {
+    CullParams p;
+    for (int i = 0; i < 16; ++i) p.vm[i] = c.viewmat[i];
+    p.fx = c.fx;
+    p.fy = c.fy;
+    p.cx = c.cx;
+    p.cy = c.cy;
+    p.width = (float)c.width;
+    p.height = (float)c.height;
+    p.near_p = near_p;
+    p.far_p = far_p;
+    p.opac_thr = thr;
+    return p;
+}
+
+size_t cull_scratch_bytes(int64_t n) {
+    const int64_t chunks = (n + kCullChunk - 1) / kCullChunk;
+    size_t b = align_up((size_t)((n + 31) / 32 + 1) * 4, 256);
+    b += align_up((size_t)(chunks + 1) * 4, 256);
+    b += align_up(scan_scratch_bytes(chunks), 256);
+    return b + 256;
+}
+
+int cull(const gs_gaussians& g, int64_t n, const gs_camera& cam, float near_p, float far_p, float thr,
+         int32_t* out_ids, int32_t* out_count, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+    GS_REQUIRE(n >= 0 && n < ((int64_t)1 << 31), "cull: n out of range");
+    GS_REQUIRE(g.means != nullptr && out_count != nullptr, "cull: null pointer");
+    GS_REQUIRE(scratch_bytes >= cull_scratch_bytes(n) && scratch != nullptr, "cull: scratch too small");
+    if (n == 0) {
+        cudaMemsetAsync(out_count, 0, sizeof(int32_t), stream);
+        return check_launch("cull(n=0)", 0);
+    }
+    GS_REQUIRE(out_ids != nullptr, "cull: null out_ids");
+    const int64_t chunks = (n + kCullChunk - 1) / kCullChunk;
+    char* p = reinterpret_cast<char*>(align_up(reinterpret_cast<uintptr_t>(scratch), 256));
+    uint32_t* words = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)((n + 31) / 32 + 1) * 4, 256);
+    uint32_t* counts = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)(chunks + 1) * 4, 256);
+    const CullParams cp = make_cull_params(cam, near_p, far_p, thr);
+    cull_flags<<<(unsigned)chunks, kCullThreads, 0, stream>>>(g, n, cp, words, counts);
+    GS_TRY(check_launch("cull_flags"));
+    // counts -> offsets in place; the total lands in counts[chunks]
+    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream));
+    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, out_ids);
+    GS_TRY(check_launch("cull_write"));
+    cudaMemcpyAsync(out_count, counts + chunks, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
+    return check_launch("cull count copy", 0);
+}
+
+}  // namespace gs
+
+extern "C" size_t gs_cull_scratch_bytes(int64_t n) { return gs::cull_scratch_bytes(n); }
+
+extern "C" int gs_cull(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_plane, float far_plane,
+                       float opacity_threshold, int32_t* out_ids, int32_t* out_count, void* scratch,
+                       size_t scratch_bytes, gs_stream_t stream) {
+    GS_REQUIRE(g && cam, "cull: null descriptor");
+    return gs::cull(*g, n, *cam, near_plane, far_plane, opacity_threshold, out_ids, out_count, scratch, scratch_bytes,
+                    (cudaStream_t)stream);
+}

@@ -1,0 +1,236 @@
+// Shared device code of the rasterizer kernels: camera constants, the
+// per-Gaussian projection of mlx_gsplat/rendering.py:153-244, and the
+// splat-versus-tile bound used by binning.
+#pragma once
+
+#include "common.cuh"
+
+namespace gs {
+
+constexpr float kSH_C0 = 0.28209479177387814f;
+constexpr float kSH_C1 = 0.4886025119029199f;
+
+struct RasterParams {
+    float vm[16];
+    float fx, fy, cx, cy;
+    float campos[3];   // -R^T t (rendering.py:221-223)
+    float sx, sy, hsx, hsy;  // pixel scale and half scale (rendering.py:251-255)
+    int rw, rh, tiles_x, tiles_y;
+    float alpha_cut, t_min;
+    float loss_scale;  // 1 / (3 * rw * rh) for the mean-based losses
+};
+
+inline RasterParams make_raster_params(const gs_camera& c, const gs_raster_settings* rs) {
+    RasterParams p;
+    for (int i = 0; i < 16; ++i) p.vm[i] = c.viewmat[i];
+    p.fx = c.fx;
+    p.fy = c.fy;
+    p.cx = c.cx;
+    p.cy = c.cy;
+    for (int i = 0; i < 3; ++i)
+        p.campos[i] = -(c.viewmat[0 * 4 + i] * c.viewmat[3] + c.viewmat[1 * 4 + i] * c.viewmat[7] +
+                        c.viewmat[2 * 4 + i] * c.viewmat[11]);
+    p.sx = (float)c.width / (float)c.render_width;
+    p.sy = (float)c.height / (float)c.render_height;
+    p.hsx = p.sx * 0.5f;
+    p.hsy = p.sy * 0.5f;
+    p.rw = c.render_width;
+    p.rh = c.render_height;
+    p.tiles_x = (c.render_width + kTile - 1) / kTile;
+    p.tiles_y = (c.render_height + kTile - 1) / kTile;
+    p.alpha_cut = rs ? rs->alpha_cutoff : 1e-8f;
+    p.t_min = rs ? rs->transmittance_min : 1e-6f;
+    p.loss_scale = (float)(1.0 / (3.0 * (double)c.render_width * (double)c.render_height));
+    return p;
+}
+
+// Everything the forward computes for one Gaussian (kept for the backward's recompute).
+struct ProjState {
+    float mx, my, mz;          // world mean
+    float tx, ty, tz, z;       // camera point; z = max(tz, 1e-4)
+    float u, v;
+    float qw, qx, qy, qz, qn;  // raw quaternion and its norm sqrt(sum q^2 + 1e-8)
+    float R[9];                // rotation of the normalised quaternion
+    float S[3];                // exp(log-scale)
+    float Sg[9];               // 3-D covariance R S S^T R^T
+    float T[6];                // J W (2 x 3)
+    float a, b, c, d;          // 2-D covariance + 0.3 I
+    float det_raw, det;        // det before / after the 1e-6 floor
+    float ca, cb, cc, cd;      // conic (inverse)
+    float opac;                // sigmoid(logit)
+    float dir[3], dnorm;       // unit view direction and |mean - campos|
+    float pre[3];              // SH colour + 0.5 before the [0, 1] clip
+    float rgb[3];
+};
+
+__device__ __forceinline__ int64_t param_row(const gs_gaussians& g, int32_t id) {
+    return g.table ? (int64_t)__ldg(g.table + id) : (int64_t)id;
+}
+
+// rendering.py:153-244 for one Gaussian.  ``cols`` points at its colour row.
+__device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, const float* cols,
+                                            const RasterParams& p, ProjState& s) {
+    const float* mp = g.means + row * g.means_stride;
+    s.mx = __ldg(mp + 0);
+    s.my = __ldg(mp + 1);
+    s.mz = __ldg(mp + 2);
+    s.tx = cam_row(p.vm, 0, s.mx, s.my, s.mz);
+    s.ty = cam_row(p.vm, 1, s.mx, s.my, s.mz);
+    s.tz = cam_row(p.vm, 2, s.mx, s.my, s.mz);
+    s.z = s.tz > 1e-4f ? s.tz : 1e-4f;
+    s.u = __fadd_rn(__fdiv_rn(__fmul_rn(s.tx, p.fx), s.z), p.cx);
+    s.v = __fadd_rn(__fdiv_rn(__fmul_rn(s.ty, p.fy), s.z), p.cy);
+
+    const float* qp = g.quats + row * g.quats_stride;
+    s.qw = __ldg(qp + 0);
+    s.qx = __ldg(qp + 1);
+    s.qy = __ldg(qp + 2);
+    s.qz = __ldg(qp + 3);
+    s.qn = sqrtf(s.qw * s.qw + s.qx * s.qx + s.qy * s.qy + s.qz * s.qz + 1e-8f);
+    const float r = s.qw / s.qn, x = s.qx / s.qn, y = s.qy / s.qn, z = s.qz / s.qn;
+    s.R[0] = 1.f - 2.f * (y * y + z * z);
+    s.R[1] = 2.f * (x * y - r * z);
+    s.R[2] = 2.f * (x * z + r * y);
+    s.R[3] = 2.f * (x * y + r * z);
+    s.R[4] = 1.f - 2.f * (x * x + z * z);
+    s.R[5] = 2.f * (y * z - r * x);
+    s.R[6] = 2.f * (x * z - r * y);
+    s.R[7] = 2.f * (y * z + r * x);
+    s.R[8] = 1.f - 2.f * (x * x + y * y);
+
+    const float* sp = g.scales + row * g.scales_stride;
+    s.S[0] = expf(__ldg(sp + 0));
+    s.S[1] = expf(__ldg(sp + 1));
+    s.S[2] = expf(__ldg(sp + 2));
+    float M[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) M[3 * i + j] = s.R[3 * i + j] * s.S[j];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            s.Sg[3 * i + j] = M[3 * i + 0] * M[3 * j + 0] + M[3 * i + 1] * M[3 * j + 1] + M[3 * i + 2] * M[3 * j + 2];
+
+    // J (third row zero) times W = viewmat[:3,:3]  (rendering.py:189-199)
+    const float tz2 = s.z * s.z;
+    const float j00 = p.fx / s.z, j02 = -p.fx * s.tx / tz2;
+    const float j11 = p.fy / s.z, j12 = -p.fy * s.ty / tz2;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        s.T[k] = j00 * p.vm[0 * 4 + k] + j02 * p.vm[2 * 4 + k];
+        s.T[3 + k] = j11 * p.vm[1 * 4 + k] + j12 * p.vm[2 * 4 + k];
+    }
+    // X = Sigma3 T^T (3 x 2), Sigma2 = T X   (rendering.py:200)
+    float X0[3], X1[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        X0[k] = s.Sg[3 * k + 0] * s.T[0] + s.Sg[3 * k + 1] * s.T[1] + s.Sg[3 * k + 2] * s.T[2];
+        X1[k] = s.Sg[3 * k + 0] * s.T[3] + s.Sg[3 * k + 1] * s.T[4] + s.Sg[3 * k + 2] * s.T[5];
+    }
+    s.a = s.T[0] * X0[0] + s.T[1] * X0[1] + s.T[2] * X0[2] + 0.3f;
+    s.b = s.T[0] * X1[0] + s.T[1] * X1[1] + s.T[2] * X1[2];
+    s.c = s.T[3] * X0[0] + s.T[4] * X0[1] + s.T[5] * X0[2];
+    s.d = s.T[3] * X1[0] + s.T[4] * X1[1] + s.T[5] * X1[2] + 0.3f;
+    s.det_raw = s.a * s.d - s.b * s.c;
+    s.det = s.det_raw > 1e-6f ? s.det_raw : 1e-6f;
+    s.ca = s.d / s.det;
+    s.cb = -s.b / s.det;
+    s.cc = -s.c / s.det;
+    s.cd = s.a / s.det;
+
+    const float logit = __ldg(g.opac + row * g.opac_stride);
+    s.opac = 1.0f / (1.0f + expf(-logit));
+
+    const float dx = s.mx - p.campos[0], dy = s.my - p.campos[1], dz = s.mz - p.campos[2];
+    s.dnorm = sqrtf(dx * dx + dy * dy + dz * dz);
+    const float inv = 1.0f / (s.dnorm + 1e-8f);
+    s.dir[0] = dx * inv;
+    s.dir[1] = dy * inv;
+    s.dir[2] = dz * inv;
+    float c0 = __ldg(cols + 0) * kSH_C0, c1 = __ldg(cols + 1) * kSH_C0, c2 = __ldg(cols + 2) * kSH_C0;
+    if (g.colors_dim >= 12) {
+        const float xd = s.dir[0], yd = s.dir[1], zd = s.dir[2];
+        c0 += kSH_C1 * (__ldg(cols + 3) * yd + __ldg(cols + 4) * zd + __ldg(cols + 5) * xd);
+        c1 += kSH_C1 * (__ldg(cols + 6) * yd + __ldg(cols + 7) * zd + __ldg(cols + 8) * xd);
+        c2 += kSH_C1 * (__ldg(cols + 9) * yd + __ldg(cols + 10) * zd + __ldg(cols + 11) * xd);
+    }
+    s.pre[0] = c0 + 0.5f;
+    s.pre[1] = c1 + 0.5f;
+    s.pre[2] = c2 + 0.5f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) s.rgb[k] = fminf(fmaxf(s.pre[k], 0.0f), 1.0f);
+}
+
+// ------------------------------------------------------------------ tile binning bound
+// A splat is binned into a tile when some pixel centre of the tile can see
+// alpha >= alpha_cut, i.e. Mahalanobis m <= m_cut = 2 ln(opac / alpha_cut).
+// The bound is evaluated on the continuous rectangle spanned by the tile's
+// pixel centres (a superset of the centres), with a small relative slack.
+struct TileBox {
+    int x0, x1, y0, y1;  // inclusive tile range
+    bool exact;          // false: conic not positive definite -> every tile of the box
+    float m_cut, s;      // cut and symmetric off-diagonal (cb + cc) / 2
+};
+
+__device__ __forceinline__ bool splat_tile_box(float u, float v, float ca, float cb, float cc, float cd, float opac,
+                                               const RasterParams& p, TileBox& tb) {
+    if (!(opac > p.alpha_cut)) return false;
+    if (!(isfinite(u) && isfinite(v) && isfinite(ca) && isfinite(cb) && isfinite(cc) && isfinite(cd))) return false;
+    tb.m_cut = 2.0f * logf(opac / p.alpha_cut);
+    tb.s = 0.5f * (cb + cc);
+    const float det = ca * cd - tb.s * tb.s;
+    if (ca > 0.f && cd > 0.f && det > 0.f) {
+        const float m = tb.m_cut * 1.0002f + 1e-3f;
+        const float ex = sqrtf(m * cd / det) * 1.0002f + 1e-3f;
+        const float ey = sqrtf(m * ca / det) * 1.0002f + 1e-3f;
+        const float i0 = fmaxf(ceilf((u - ex - p.hsx) / p.sx), 0.f);
+        const float i1 = fminf(floorf((u + ex - p.hsx) / p.sx), (float)(p.rw - 1));
+        const float j0 = fmaxf(ceilf((v - ey - p.hsy) / p.sy), 0.f);
+        const float j1 = fminf(floorf((v + ey - p.hsy) / p.sy), (float)(p.rh - 1));
+        if (!(i0 <= i1 && j0 <= j1)) return false;
+        tb.x0 = (int)i0 / kTile;
+        tb.x1 = (int)i1 / kTile;
+        tb.y0 = (int)j0 / kTile;
+        tb.y1 = (int)j1 / kTile;
+        tb.exact = true;
+    } else {
+        tb.x0 = 0;
+        tb.x1 = p.tiles_x - 1;
+        tb.y0 = 0;
+        tb.y1 = p.tiles_y - 1;
+        tb.exact = false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ float quad_form(float ca, float s, float cd, float x, float y) {
+    return ca * x * x + 2.0f * s * x * y + cd * y * y;
+}
+
+// Minimum of the (positive definite) quadratic form over the tile's pixel-centre rectangle.
+__device__ __forceinline__ bool splat_hits_tile(float u, float v, float ca, float cd, const TileBox& tb, int tx,
+                                                int ty, const RasterParams& p) {
+    if (!tb.exact) return true;
+    const int i0 = tx * kTile, i1 = min(i0 + kTile - 1, p.rw - 1);
+    const int j0 = ty * kTile, j1 = min(j0 + kTile - 1, p.rh - 1);
+    const float x0 = (float)i0 * p.sx + p.hsx - u, x1 = (float)i1 * p.sx + p.hsx - u;
+    const float y0 = (float)j0 * p.sy + p.hsy - v, y1 = (float)j1 * p.sy + p.hsy - v;
+    if (x0 <= 0.f && 0.f <= x1 && y0 <= 0.f && 0.f <= y1) return true;
+    const float s = tb.s;
+    float best = 3.4e38f;
+    {
+        const float ya = fminf(fmaxf(-s * x0 / cd, y0), y1);
+        best = fminf(best, quad_form(ca, s, cd, x0, ya));
+        const float yb = fminf(fmaxf(-s * x1 / cd, y0), y1);
+        best = fminf(best, quad_form(ca, s, cd, x1, yb));
+        const float xa = fminf(fmaxf(-s * y0 / ca, x0), x1);
+        best = fminf(best, quad_form(ca, s, cd, xa, y0));
+        const float xb = fminf(fmaxf(-s * y1 / ca, x0), x1);
+        best = fminf(best, quad_form(ca, s, cd, xb, y1));
+    }
+    return best <= tb.m_cut * 1.0002f + 1e-3f;
+}
+
+}  // namespace gs

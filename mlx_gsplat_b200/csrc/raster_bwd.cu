@@ -1,0 +1,360 @@
+// Rasterizer backward: back-to-front compositing gradient with warp-reduced
+// atomics, and the projection backward to the Gaussian parameters (the
+// vector-Jacobian product MLX's autograd forms for mlx_gsplat/rendering.py:153-300).
+#include "raster.cuh"
+
+namespace gs {
+
+constexpr int kGradRec = 12;  // floats per splat gradient record
+
+// For every tile: walk the tile's entries from the last one any pixel used
+// back to the first.  Per pixel the transmittance before entry i is
+// recovered as T_i = T_{i+1} / (1 - alpha_i), and with
+//   val_i = dL/dC . rgb_i + dL/dA,   B_{i-1} = alpha_i val_i + (1 - alpha_i) B_i
+// the alpha gradient is dL/dalpha_i = T_i (val_i - B_i).  The clip of
+// opacity * g to [0, 0.99] passes the gradient only strictly inside
+// (MLX's maximum/minimum rule).  Nine per-splat sums are reduced across the
+// warp and added once per warp with vector reductions.
+__global__ void __launch_bounds__(kTileThreads) render_bwd_kernel(
+    const gs_tile_range* __restrict__ ranges, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
+    int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
+    const int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
+    const float* __restrict__ dL_dcolor, const float* __restrict__ dL_dalpha, float* __restrict__ splat_grads) {
+    __shared__ float4 s0[kTileThreads], s1[kTileThreads], s2[kTileThreads];
+    __shared__ uint32_t sv[kTileThreads];
+    __shared__ int smax;
+    const int tile = blockIdx.x;
+    const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pi = tx * kTile + (warp & 1) * 8 + (lane & 7);
+    const int pj = ty * kTile + (warp >> 1) * 4 + (lane >> 3);
+    const bool inside = pi < p.rw && pj < p.rh;
+    const float px = (float)pi * p.sx + p.hsx;
+    const float py = (float)pj * p.sy + p.hsy;
+    const gs_tile_range rg = ranges[tile];
+
+    float T = 1.f, dr = 0.f, dg = 0.f, db = 0.f, dA = 0.f;
+    int last = 0;
+    if (inside) {
+        const int64_t pix = (int64_t)pj * p.rw + pi;
+        T = final_T[pix];
+        last = n_contrib[pix];
+        if (loss_mode == GS_LOSS_NONE) {
+            dr = dL_dcolor[3 * pix + 0];
+            dg = dL_dcolor[3 * pix + 1];
+            db = dL_dcolor[3 * pix + 2];
+            dA = dL_dalpha ? dL_dalpha[pix] : 0.f;
+        } else if (loss_mode == GS_LOSS_MEAN) {
+            dr = dg = db = p.loss_scale;
+        } else {
+            float t0, t1, t2;
+            if (loss_mode == GS_LOSS_L1_U8) {
+                const uint8_t* t8 = static_cast<const uint8_t*>(target) + 3 * pix;
+                t0 = __fdiv_rn((float)t8[0], 255.0f);
+                t1 = __fdiv_rn((float)t8[1], 255.0f);
+                t2 = __fdiv_rn((float)t8[2], 255.0f);
+            } else {
+                const float* tf = static_cast<const float*>(target) + 3 * pix;
+                t0 = tf[0];
+                t1 = tf[1];
+                t2 = tf[2];
+            }
+            const float e0 = out_color[3 * pix + 0] - t0, e1 = out_color[3 * pix + 1] - t1,
+                        e2 = out_color[3 * pix + 2] - t2;
+            dr = (e0 > 0.f ? 1.f : (e0 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+            dg = (e1 > 0.f ? 1.f : (e1 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+            db = (e2 > 0.f ? 1.f : (e2 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+        }
+    }
+    if (threadIdx.x == 0) smax = 0;
+    __syncthreads();
+    if (last > 0) atomicMax(&smax, last);
+    __syncthreads();
+    const int max_last = smax;
+
+    float Bv = 0.f;
+    for (int bend = rg.start + max_last; bend > rg.start; bend -= kTileThreads) {
+        const int bstart = max(bend - kTileThreads, rg.start);
+        const int cnt = bend - bstart;
+        __syncthreads();
+        if ((int)threadIdx.x < cnt) {
+            const uint32_t vr = vals[bstart + threadIdx.x];
+            const uint32_t vi = vr < (uint64_t)nv ? vr : 0u;
+            sv[threadIdx.x] = vi;
+            s0[threadIdx.x] = splats[3 * vi];
+            s1[threadIdx.x] = splats[3 * vi + 1];
+            s2[threadIdx.x] = splats[3 * vi + 2];
+        }
+        __syncthreads();
+        for (int k = cnt - 1; k >= 0; --k) {
+            const int idx = bstart + k - rg.start;
+            const bool valid = idx < last;
+            if (!__any_sync(kFull, valid)) continue;
+            float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f, g4 = 0.f, g5 = 0.f, g6 = 0.f, g7 = 0.f, g8 = 0.f;
+            if (valid) {
+                const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
+                const float x = px - q0.x, y = py - q0.y;
+                const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
+                const float gv = __expf(-0.5f * m);
+                const float og = q1.z * gv;
+                const float al = fminf(og, 0.99f);
+                T = T / (1.f - al);
+                const float val = dr * q1.w + dg * q2.x + db * q2.y + dA;
+                const float dal = T * (val - Bv);
+                Bv = al * val + (1.f - al) * Bv;
+                const float wT = al * T;
+                g6 = wT * dr;
+                g7 = wT * dg;
+                g8 = wT * db;
+                if (og > 0.f && og < 0.99f) {
+                    g5 = dal * gv;                      // d opacity
+                    const float dm = -0.5f * gv * (dal * q1.z);
+                    const float sbc = q0.w + q1.x;
+                    g0 = -dm * (2.f * q0.z * x + sbc * y);  // d u
+                    g1 = -dm * (sbc * x + 2.f * q1.y * y);  // d v
+                    g2 = dm * x * x;                        // d conic a
+                    g3 = dm * x * y;                        // d conic b (= d conic c)
+                    g4 = dm * y * y;                        // d conic d
+                }
+            }
+            g0 = warp_sum(g0);
+            g1 = warp_sum(g1);
+            g2 = warp_sum(g2);
+            g3 = warp_sum(g3);
+            g4 = warp_sum(g4);
+            g5 = warp_sum(g5);
+            g6 = warp_sum(g6);
+            g7 = warp_sum(g7);
+            g8 = warp_sum(g8);
+            if (lane == 0) {
+                float* rec = splat_grads + (int64_t)sv[k] * kGradRec;
+                red_add_v4(rec, g0, g1, g2, g3);
+                red_add_v4(rec + 4, g4, g5, g6, g7);
+                atomicAdd(rec + 8, g8);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void put(float* base, int64_t off, float v, bool acc) {
+    if (acc)
+        atomicAdd(base + off, v);
+    else
+        base[off] = v;
+}
+
+// Chain rule from the splat gradient record back to means, quaternions,
+// log-scales, opacity logits and SH colour coefficients.
+__global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
+                                                          RasterParams p, const float* __restrict__ splat_grads,
+                                                          gs_gaussian_grads o, float* __restrict__ grad2d,
+                                                          float* __restrict__ count) {
+    const int64_t vi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vi >= nv) return;
+    const int32_t id = ids[vi];
+    const int64_t row = param_row(g, id);
+    const int64_t crow = g.colors_by_visible ? vi : row;
+    const float* cols = g.colors + crow * g.colors_stride;
+    ProjState s;
+    project_one(g, row, cols, p, s);
+    const float* G = splat_grads + vi * kGradRec;
+    const float du = G[0], dv = G[1], dca = G[2], dcbc = G[3], dcd = G[4], dop = G[5];
+    const float drgb[3] = {G[6], G[7], G[8]};
+
+    // ---- conic = adj(Sigma2) / max(det, 1e-6)
+    const float det2 = s.det * s.det;
+    const float ddet = (-dca * s.d + dcbc * s.b + dcbc * s.c - dcd * s.a) / det2;
+    const float mk = s.det_raw > 1e-6f ? 1.f : 0.f;
+    const float dA_ = dcd / s.det + mk * ddet * s.d;
+    const float dD_ = dca / s.det + mk * ddet * s.a;
+    const float dB_ = -dcbc / s.det - mk * ddet * s.c;
+    const float dC_ = -dcbc / s.det - mk * ddet * s.b;
+
+    // ---- Sigma2 = T Sigma3 T^T: dSigma3 = T^T G2 T,  dT = (G2 + G2^T) T Sigma3
+    const float G2[4] = {dA_, dB_, dC_, dD_};
+    const float* Tm = s.T;
+    float dS3[9];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int l = 0; l < 3; ++l)
+            dS3[3 * k + l] = Tm[k] * (G2[0] * Tm[l] + G2[1] * Tm[3 + l]) + Tm[3 + k] * (G2[2] * Tm[l] + G2[3] * Tm[3 + l]);
+    const float Gs00 = 2.f * G2[0], Gs01 = G2[1] + G2[2], Gs11 = 2.f * G2[3];
+    float TS[6];  // T Sigma3
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int l = 0; l < 3; ++l)
+            TS[3 * i + l] = Tm[3 * i + 0] * s.Sg[0 * 3 + l] + Tm[3 * i + 1] * s.Sg[1 * 3 + l] + Tm[3 * i + 2] * s.Sg[2 * 3 + l];
+    float dT[6];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+        dT[l] = Gs00 * TS[l] + Gs01 * TS[3 + l];
+        dT[3 + l] = Gs01 * TS[l] + Gs11 * TS[3 + l];
+    }
+    // ---- T = J W: dJ = dT W^T (only J00, J02, J11, J12 are non-zero)
+    const float* W = p.vm;
+    const float dJ00 = dT[0] * W[0] + dT[1] * W[1] + dT[2] * W[2];
+    const float dJ02 = dT[0] * W[8] + dT[1] * W[9] + dT[2] * W[10];
+    const float dJ11 = dT[3] * W[4] + dT[4] * W[5] + dT[5] * W[6];
+    const float dJ12 = dT[3] * W[8] + dT[4] * W[9] + dT[5] * W[10];
+    const float z = s.z, z2 = z * z, z3 = z2 * z;
+    float dtx = dJ02 * (-p.fx / z2) + du * p.fx / z;
+    float dty = dJ12 * (-p.fy / z2) + dv * p.fy / z;
+    float dz = dJ00 * (-p.fx / z2) + dJ02 * (2.f * p.fx * s.tx / z3) + dJ11 * (-p.fy / z2) +
+               dJ12 * (2.f * p.fy * s.ty / z3) - du * p.fx * s.tx / z2 - dv * p.fy * s.ty / z2;
+    const float dtz = s.tz > 1e-4f ? dz : 0.f;
+    // ---- camera point = W mean + t
+    float dm[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dm[k] = W[0 * 4 + k] * dtx + W[1 * 4 + k] * dty + W[2 * 4 + k] * dtz;
+
+    // ---- Sigma3 = M M^T, M = R diag(S)
+    float M[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) M[3 * i + j] = s.R[3 * i + j] * s.S[j];
+    float dM[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) acc += (dS3[3 * i + k] + dS3[3 * k + i]) * M[3 * k + j];
+            dM[3 * i + j] = acc;
+        }
+    float dscale[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+        dscale[j] = (dM[0 * 3 + j] * s.R[0 * 3 + j] + dM[1 * 3 + j] * s.R[1 * 3 + j] + dM[2 * 3 + j] * s.R[2 * 3 + j]) * s.S[j];
+    float dR[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) dR[3 * i + j] = dM[3 * i + j] * s.S[j];
+    // ---- R(q), q = quat / |quat|
+    const float r = s.qw / s.qn, x = s.qx / s.qn, y = s.qy / s.qn, zq = s.qz / s.qn;
+    const float dqr = 2.f * (-zq * dR[1] + y * dR[2] + zq * dR[3] - x * dR[5] - y * dR[6] + x * dR[7]);
+    const float dqx = 2.f * (y * dR[1] + zq * dR[2] + y * dR[3] - 2.f * x * dR[4] - r * dR[5] + zq * dR[6] + r * dR[7] -
+                             2.f * x * dR[8]);
+    const float dqy = 2.f * (-2.f * y * dR[0] + x * dR[1] + r * dR[2] + x * dR[3] + zq * dR[5] - r * dR[6] + zq * dR[7] -
+                             2.f * y * dR[8]);
+    const float dqz = 2.f * (-2.f * zq * dR[0] - r * dR[1] + x * dR[2] + r * dR[3] - 2.f * zq * dR[4] + y * dR[5] +
+                             x * dR[6] + y * dR[7]);
+    const float qdot = (dqr * s.qw + dqx * s.qx + dqy * s.qy + dqz * s.qz) / (s.qn * s.qn * s.qn);
+    float dquat[4] = {dqr / s.qn - s.qw * qdot, dqx / s.qn - s.qx * qdot, dqy / s.qn - s.qy * qdot,
+                      dqz / s.qn - s.qz * qdot};
+
+    // ---- opacity
+    const float dlogit = dop * s.opac * (1.f - s.opac);
+
+    // ---- colour: clip mask, SH0, SH1 and the direction's dependence on the mean
+    float dpre[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dpre[k] = (s.pre[k] > 0.f && s.pre[k] < 1.f) ? drgb[k] : 0.f;
+    float dcol[12];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dcol[k] = dpre[k] * kSH_C0;
+    const bool sh1 = g.colors_dim >= 12;
+    if (sh1) {
+        const float xd = s.dir[0], yd = s.dir[1], zd = s.dir[2];
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            const float e = kSH_C1 * dpre[ch];
+            dcol[3 + 3 * ch + 0] = e * yd;
+            dcol[3 + 3 * ch + 1] = e * zd;
+            dcol[3 + 3 * ch + 2] = e * xd;
+        }
+        float ddir[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            const float e = kSH_C1 * dpre[ch];
+            ddir[1] += e * __ldg(cols + 3 + 3 * ch + 0);
+            ddir[2] += e * __ldg(cols + 3 + 3 * ch + 1);
+            ddir[0] += e * __ldg(cols + 3 + 3 * ch + 2);
+        }
+        const float n = s.dnorm, ne = n + 1e-8f;
+        const float dx = s.mx - p.campos[0], dy = s.my - p.campos[1], dzz = s.mz - p.campos[2];
+        const float proj = (ddir[0] * dx + ddir[1] * dy + ddir[2] * dzz) / (n * ne * ne);
+        dm[0] += ddir[0] / ne - dx * proj;
+        dm[1] += ddir[1] / ne - dy * proj;
+        dm[2] += ddir[2] / ne - dzz * proj;
+    } else {
+#pragma unroll
+        for (int k = 3; k < 12; ++k) dcol[k] = 0.f;
+    }
+
+    // ---- outputs
+    const bool acc = o.accumulate != 0;
+    const float reg = o.reg;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dm[k] += reg;
+    if (o.means) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) put(o.means, (int64_t)id * o.means_stride + k, dm[k], acc);
+    }
+    if (o.quats) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) put(o.quats, (int64_t)id * o.quats_stride + k, dquat[k] + reg, acc);
+    }
+    if (o.scales) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) put(o.scales, (int64_t)id * o.scales_stride + k, dscale[k] + reg, acc);
+    }
+    if (o.opac) put(o.opac, (int64_t)id * o.opac_stride, dlogit + reg, acc);
+    if (o.colors) {
+        const int64_t orow = o.colors_by_visible ? vi : (int64_t)id;
+        float* dst = o.colors + orow * o.colors_stride;
+        for (int k = 0; k < o.colors_write; ++k) {
+            float val = k < 12 ? dcol[k] : 0.f;
+            if (k < o.reg_color_cols) val += reg;
+            put(dst, k, val, acc);
+        }
+    }
+    if (grad2d) {
+        const int64_t prow = param_row(g, id);
+        const float gn = sqrtf(dm[0] * dm[0] + dm[1] * dm[1] + dm[2] * dm[2] + 1e-8f);
+        atomicAdd(grad2d + prow, gn * fabsf(s.tz) / p.fx);
+        atomicAdd(count + prow, 1.0f);
+    }
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_render_backward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+                                  int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs,
+                                  const float* out_color,
+                                  const float* final_T, const int32_t* n_contrib, int loss_mode, const void* target,
+                                  const float* dL_dcolor, const float* dL_dalpha, float* splat_grads,
+                                  gs_stream_t stream) {
+    GS_REQUIRE(cam && ranges && final_T && n_contrib && splat_grads, "render_backward: null pointer");
+    GS_REQUIRE(loss_mode >= GS_LOSS_NONE && loss_mode <= GS_LOSS_MEAN, "render_backward: bad loss mode");
+    GS_REQUIRE(loss_mode != GS_LOSS_NONE || dL_dcolor, "render_backward: dL_dcolor required");
+    GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || (target && out_color),
+               "render_backward: target and out_color required");
+    GS_REQUIRE(aligned16(splat_grads) && aligned16(splats), "render_backward: records must be 16-byte aligned");
+    const RasterParams p = make_raster_params(*cam, rs);
+    const int tiles = p.tiles_x * p.tiles_y;
+    render_bwd_kernel<<<tiles, kTileThreads, 0, (cudaStream_t)stream>>>(
+        ranges, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T, n_contrib, loss_mode,
+        target, dL_dcolor, dL_dalpha, splat_grads);
+    return check_launch("render_bwd_kernel");
+}
+
+extern "C" int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible,
+                                   const gs_camera* cam, const float* splat_grads, const gs_gaussian_grads* out,
+                                   float* grad2d, float* count, gs_stream_t stream) {
+    GS_REQUIRE(g && cam && out, "project_backward: null descriptor");
+    if (num_visible == 0) return GS_OK;
+    GS_REQUIRE(ids && splat_grads, "project_backward: null pointer");
+    GS_REQUIRE(!grad2d || count, "project_backward: grad2d needs count");
+    GS_REQUIRE(out->colors == nullptr || out->colors_write >= 0, "project_backward: bad colors_write");
+    const RasterParams p = make_raster_params(*cam, nullptr);
+    project_bwd_kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p,
+                                                                                     splat_grads, *out, grad2d, count);
+    return check_launch("project_bwd_kernel");
+}

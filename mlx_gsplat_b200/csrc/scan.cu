@@ -1,0 +1,119 @@
+// Device-wide exclusive prefix sum of uint32 values (reduce, then scan):
+//   1. per 2048-element tile: tile sums
+//   2. one CTA: exclusive scan of the tile sums (loops when there are many)
+//   3. per tile: block scan plus the tile's offset.
+// No inter-CTA waiting, so nothing can spin.
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace gs {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* smem_warp, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) smem_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < (int)(blockDim.x >> 5) ? smem_warp[lane] : 0u;
+        uint32_t wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(kFull, wi, o);
+            if (lane >= o) wi += y;
+        }
+        if (lane < (int)(blockDim.x >> 5)) smem_warp[lane] = wi - w;
+        if (lane == (int)(blockDim.x >> 5) - 1) smem_warp[32] = wi;
+    }
+    __syncthreads();
+    const uint32_t res = smem_warp[warp] + inc - x;
+    if (total) *total = smem_warp[32];
+    __syncthreads();
+    return res;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tile_sums(const uint32_t* __restrict__ in, int64_t n,
+                                                               uint32_t* __restrict__ tile_sums) {
+    __shared__ uint32_t sw[33];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile + (int64_t)threadIdx.x * kScanItems;
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n) s += in[base + k];
+    uint32_t tot;
+    block_exclusive_scan(s, sw, &tot);
+    if (threadIdx.x == 0) tile_sums[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tile_offsets(uint32_t* __restrict__ sums, int64_t n_tiles,
+                                                                  uint32_t* __restrict__ total_out) {
+    __shared__ uint32_t sw[33];
+    uint32_t carry = 0;
+    for (int64_t base = 0; base < n_tiles; base += kScanThreads) {
+        const int64_t i = base + threadIdx.x;
+        const uint32_t x = i < n_tiles ? sums[i] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_exclusive_scan(x, sw, &tot);
+        if (i < n_tiles) sums[i] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0 && total_out) *total_out = carry;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tiles(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
+                                                           int64_t n, const uint32_t* __restrict__ tile_offsets) {
+    __shared__ uint32_t sw[33];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile + (int64_t)threadIdx.x * kScanItems;
+    uint32_t v[kScanItems];
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        v[k] = base + k < n ? in[base + k] : 0u;
+        s += v[k];
+    }
+    uint32_t run = block_exclusive_scan(s, sw, nullptr) + tile_offsets[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        if (base + k < n) out[base + k] = run;
+        run += v[k];
+    }
+}
+
+size_t scan_scratch_bytes(int64_t n) {
+    const int64_t tiles = (n + kScanTile - 1) / kScanTile;
+    return (size_t)((tiles + 4) * sizeof(uint32_t) + 256);
+}
+
+int scan_exclusive(const uint32_t* in, uint32_t* out, int64_t n, void* scratch, size_t scratch_bytes,
+                   cudaStream_t stream) {
+    GS_REQUIRE(n >= 0, "scan: negative n");
+    GS_REQUIRE(scratch_bytes >= scan_scratch_bytes(n), "scan: scratch too small");
+    if (n == 0) {
+        cudaMemsetAsync(out, 0, sizeof(uint32_t), stream);
+        return check_launch("scan(n=0)", 0);
+    }
+    const int64_t tiles = (n + kScanTile - 1) / kScanTile;
+    uint32_t* sums = reinterpret_cast<uint32_t*>(scratch);
+    scan_tile_sums<<<(unsigned)tiles, kScanThreads, 0, stream>>>(in, n, sums);
+    scan_tile_offsets<<<1, kScanThreads, 0, stream>>>(sums, tiles, out + n);
+    scan_tiles<<<(unsigned)tiles, kScanThreads, 0, stream>>>(in, out, n, sums);
+    return check_launch("scan_exclusive", 3);
+}
+
+}  // namespace gs
+
+extern "C" size_t gs_scan_scratch_bytes(int64_t n) { return gs::scan_scratch_bytes(n); }
+
+extern "C" int gs_exclusive_scan_u32(const uint32_t* in, uint32_t* out, int64_t n, void* scratch,
+                                     size_t scratch_bytes, gs_stream_t stream) {
+    GS_REQUIRE(in && out && scratch, "scan: null pointer");
+    return gs::scan_exclusive(in, out, n, scratch, scratch_bytes, (cudaStream_t)stream);
+}

@@ -1,0 +1,161 @@
+// Stable LSD radix sort of (uint32 key, uint32 value) pairs, 8 bits per pass.
+//
+// Each pass: (1) per 2048-key tile, a 256-bin digit histogram written
+// digit-major; (2) a device-wide exclusive scan of those counts, which gives
+// every (digit, tile) its global output offset; (3) per tile, a stable local
+// rank of each key within its digit — warps own contiguous runs of keys and
+// rank them 32 at a time with __match_any_sync plus per-warp digit counters in
+// shared memory, then a cross-warp prefix — and a scatter to offset + rank.
+// There is no inter-CTA waiting (reduce-then-scan), so no kernel can spin.
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace gs {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortItems = 8;
+constexpr int kSortTile = kSortThreads * kSortItems;  // 2048 keys
+constexpr int kBins = 256;
+
+__global__ void __launch_bounds__(kSortThreads) radix_upsweep(const uint32_t* __restrict__ keys, int64_t n, int shift,
+                                                              uint32_t mask, uint32_t* __restrict__ counts,
+                                                              int64_t n_tiles) {
+    __shared__ uint32_t hist[kBins];
+    hist[threadIdx.x] = 0;
+    __syncthreads();
+    const int64_t base = (int64_t)blockIdx.x * kSortTile;
+#pragma unroll
+    for (int k = 0; k < kSortItems; ++k) {
+        const int64_t i = base + (int64_t)k * kSortThreads + threadIdx.x;
+        if (i < n) atomicAdd(&hist[(__ldg(keys + i) >> shift) & mask], 1u);
+    }
+    __syncthreads();
+    counts[(int64_t)threadIdx.x * n_tiles + blockIdx.x] = hist[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* __restrict__ keys_in,
+                                                                const uint32_t* __restrict__ vals_in,
+                                                                uint32_t* __restrict__ keys_out,
+                                                                uint32_t* __restrict__ vals_out, int64_t n, int shift,
+                                                                uint32_t mask, const uint32_t* __restrict__ offsets,
+                                                                int64_t n_tiles) {
+    __shared__ uint32_t goff[kBins];
+    __shared__ uint32_t wcnt[kSortWarps][kBins];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    goff[threadIdx.x] = offsets[(int64_t)threadIdx.x * n_tiles + blockIdx.x];
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) wcnt[w][threadIdx.x] = 0;
+    __syncthreads();
+
+    const int64_t wbase = (int64_t)blockIdx.x * kSortTile + (int64_t)warp * (32 * kSortItems);
+    const unsigned lt = lanemask_lt();
+    uint32_t key[kSortItems], val[kSortItems], rank[kSortItems];
+    int dig[kSortItems];
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+        const int64_t i = wbase + r * 32 + lane;
+        const bool valid = i < n;
+        key[r] = valid ? keys_in[i] : 0u;
+        val[r] = valid ? vals_in[i] : 0u;
+        const int d = valid ? (int)((key[r] >> shift) & mask) : kBins;  // invalid lanes form their own group
+        dig[r] = d;
+        const unsigned peers = __match_any_sync(kFull, d);
+        const uint32_t before = __popc(peers & lt);
+        const uint32_t prior = valid ? wcnt[warp][d] : 0u;
+        __syncwarp();
+        if (valid && before == 0) wcnt[warp][d] = prior + __popc(peers);
+        __syncwarp();
+        rank[r] = prior + before;
+    }
+    __syncthreads();
+    {
+        uint32_t run = 0;
+#pragma unroll
+        for (int w = 0; w < kSortWarps; ++w) {
+            const uint32_t c = wcnt[w][threadIdx.x];
+            wcnt[w][threadIdx.x] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+        const int d = dig[r];
+        if (d < kBins) {
+            const uint32_t pos = goff[d] + wcnt[warp][d] + rank[r];
+            keys_out[pos] = key[r];
+            vals_out[pos] = val[r];
+        }
+    }
+}
+
+static int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+size_t radix_sort_scratch_bytes(int64_t n) {
+    const int64_t tiles = sort_tiles(n);
+    const int64_t nc = tiles * kBins;
+    size_t b = 0;
+    b += align_up((size_t)n * 4, 256) * 2;          // alternate keys + values
+    b += align_up((size_t)(nc + 1) * 4, 256);       // counts -> offsets (+ total)
+    b += align_up(scan_scratch_bytes(nc), 256);
+    return b + 256;
+}
+
+int radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out, uint32_t* vals_out,
+                     int64_t n, int begin_bit, int end_bit, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+    GS_REQUIRE(n >= 0 && n < (int64_t)1 << 31, "radix_sort: n out of range");
+    GS_REQUIRE(0 <= begin_bit && begin_bit <= end_bit && end_bit <= 32, "radix_sort: bad bit range");
+    GS_REQUIRE(keys_out != keys_in && vals_out != vals_in, "radix_sort: output must not alias input");
+    GS_REQUIRE(scratch_bytes >= radix_sort_scratch_bytes(n), "radix_sort: scratch too small");
+    if (n == 0) return GS_OK;
+    const int passes = (end_bit - begin_bit + 7) / 8;
+    if (passes == 0) {
+        cudaMemcpyAsync(keys_out, keys_in, n * 4, cudaMemcpyDeviceToDevice, stream);
+        cudaMemcpyAsync(vals_out, vals_in, n * 4, cudaMemcpyDeviceToDevice, stream);
+        return check_launch("radix_sort copy", 0);
+    }
+    const int64_t tiles = sort_tiles(n);
+    const int64_t nc = tiles * kBins;
+    char* p = static_cast<char*>(scratch);
+    p = reinterpret_cast<char*>(align_up(reinterpret_cast<uintptr_t>(p), 256));
+    uint32_t* alt_k = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)n * 4, 256);
+    uint32_t* alt_v = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)n * 4, 256);
+    uint32_t* counts = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)(nc + 1) * 4, 256);
+    void* scan_scratch = p;
+    const size_t scan_bytes = scan_scratch_bytes(nc);
+
+    const uint32_t* src_k = keys_in;
+    const uint32_t* src_v = vals_in;
+    for (int pass = 0; pass < passes; ++pass) {
+        const int shift = begin_bit + 8 * pass;
+        const int bits = end_bit - shift < 8 ? end_bit - shift : 8;
+        const uint32_t mask = (1u << bits) - 1u;
+        const bool to_out = ((passes - 1 - pass) % 2) == 0;
+        uint32_t* dk = to_out ? keys_out : alt_k;
+        uint32_t* dv = to_out ? vals_out : alt_v;
+        radix_upsweep<<<(unsigned)tiles, kSortThreads, 0, stream>>>(src_k, n, shift, mask, counts, tiles);
+        GS_TRY(scan_exclusive(counts, counts, nc, scan_scratch, scan_bytes, stream));
+        radix_downsweep<<<(unsigned)tiles, kSortThreads, 0, stream>>>(src_k, src_v, dk, dv, n, shift, mask, counts,
+                                                                      tiles);
+        GS_TRY(check_launch("radix pass", 2));
+        src_k = dk;
+        src_v = dv;
+    }
+    return GS_OK;
+}
+
+}  // namespace gs
+
+extern "C" size_t gs_radix_sort_scratch_bytes(int64_t n) { return gs::radix_sort_scratch_bytes(n); }
+
+extern "C" int gs_radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
+                                   uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, void* scratch,
+                                   size_t scratch_bytes, gs_stream_t stream) {
+    GS_REQUIRE(keys_in && vals_in && keys_out && vals_out && scratch, "radix_sort: null pointer");
+    return gs::radix_sort_pairs(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, scratch, scratch_bytes,
+                                (cudaStream_t)stream);
+}

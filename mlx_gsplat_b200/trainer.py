@@ -1,0 +1,259 @@
+"""Trainer loop (``MLXConfig`` / ``RunnerMLX``, mlx_gsplat/trainer.py:24-631) on B200.
+
+One training step on one view (``train_step``) runs entirely on the GPU over
+the pooled slab — no per-step gather of the active parameters:
+
+    cull over the active ids (through the indirection table)
+    -> tile rasterizer forward with the L1 loss fused into its epilogue
+    -> gradient rows of unseen Gaussians filled with the regulariser pattern
+    -> rasterizer backward writing one gradient row per visible Gaussian and
+       accumulating the densification statistic (grad2d, count)
+    -> [views data-parallel: NCCL all-reduce of the gradient rows]
+    -> one fused Adam launch over the slab (+ quaternion renormalisation)
+    -> periodic opacity reset and densify/prune (``densify``).
+
+Loss: ``loss="l1"`` is mean |render - target| (the benchmark workloads);
+``loss="mean"`` is the reference's target-less ``mean(render)``.  The
+reference's ``1e-5 * sum(active params)`` term (trainer.py:283-292) is kept as
+``param_reg``: +1e-5 on every means/quats/scales/opacities gradient of every
+active Gaussian and on the gathered colour coefficients of visible ones.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib, synthetic
+from .allocator import PointerStableChunkedAllocator
+from .optimizer import FusedMLXAdam
+from .rendering import (DEFAULT_SETTINGS, RasterSettings, camera_struct, cull_ids, gaussians_struct, grads_struct,
+                        render_backward, render_forward)
+
+
+@dataclass
+class MLXConfig:
+    max_gaussians: int = 500000
+    init_gaussians: Optional[int] = None
+    max_steps: int = 300
+    lr: float = 1.6e-4
+    sh_degree: int = 3
+    sh_degree_interval: int = 500
+    refine_every: int = 100
+    data_dir: str = "data/garden"
+    data_factor: int = 8
+    width: int = 800
+    height: int = 600
+    use_real_data: bool = True
+    render_width: int = 200
+    render_height: int = 150
+    pixel_chunk_size: int = 1024
+    preload_images: bool = True
+    # B200 additions
+    betas: Tuple[float, float] = (0.9, 0.999)
+    eps: float = 1e-8
+    loss: str = "l1"
+    param_reg: float = 1e-5
+    densify: bool = True
+    opacity_reset: bool = True
+    alpha_cutoff: float = DEFAULT_SETTINGS.alpha_cutoff
+    transmittance_min: float = DEFAULT_SETTINGS.transmittance_min
+    near_plane: float = 0.01
+    far_plane: float = 1e10
+    opacity_threshold: float = -5.3
+
+
+def lr_at(lr: float, step: int, max_steps: int) -> float:
+    return lr * (0.01 ** (step / max_steps))
+
+
+def sh_cols_for(step: int, cfg: MLXConfig) -> int:
+    """Colour columns the rasterizer sees at ``step`` (trainer.py:242-250)."""
+    d = min(step // cfg.sh_degree_interval, cfg.sh_degree)
+    return 3 + 3 * ((d + 1) ** 2 - 1)
+
+
+class StepTimer:
+    """CUDA events between the phases of a step, on the step's stream."""
+
+    PHASES = ("cull", "project_fwd", "depth_sort+offsets", "bin+tile_sort", "render_fwd", "grad_init",
+              "render_bwd", "project_bwd", "allreduce", "adam")
+
+    def __init__(self):
+        self.events: List[Tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events.append((name, e))
+
+    def durations(self) -> Dict[str, float]:
+        out: Dict[str, float] = {}
+        for (n0, e0), (n1, e1) in zip(self.events[:-1], self.events[1:]):
+            out[n1] = out.get(n1, 0.0) + e0.elapsed_time(e1)
+        return out
+
+
+class RunnerMLX:
+    def __init__(self, cfg: MLXConfig, init_params: Dict[str, np.ndarray], viewmats: np.ndarray, K: np.ndarray,
+                 targets: Optional[torch.Tensor] = None, device: Optional[torch.device] = None,
+                 scene_scale: float = 1.0, process_group=None):
+        self.cfg = cfg
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.allocator = PointerStableChunkedAllocator(cfg.max_gaussians, cfg.sh_degree, device=self.device)
+        self.allocator.set_initial_gaussians(init_params)
+        self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
+        L = self.allocator.layout
+        self.layout = L
+        self.grad = torch.zeros((cfg.max_gaussians, L.stride), dtype=torch.float32, device=self.device)
+        lo, hi = L.col_bounds()
+        self.col_lo, self.col_hi = lo.tolist(), hi.tolist()
+        self.viewmats = np.asarray(viewmats, np.float32)
+        self.K = np.asarray(K, np.float32)
+        self.cams = [camera_struct(vm, self.K, cfg.width, cfg.height, cfg.render_width, cfg.render_height)
+                     for vm in self.viewmats]
+        self.targets = targets
+        self.settings = RasterSettings(cfg.alpha_cutoff, cfg.transmittance_min)
+        self.scene_scale = scene_scale
+        self.pg = process_group
+        self.world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(process_group)
+        self.last_frame = None
+        self.step_count = 0
+
+    # ------------------------------------------------------------------ helpers
+    def _reg_pattern(self) -> List[float]:
+        L = self.layout
+        pat = [0.0] * L.stride
+        for name in ("quats", "means", "opacities", "scales"):
+            o = L.offsets[name]
+            for c in range(o, o + L.dims[name]):
+                pat[c] = self.cfg.param_reg
+        return pat
+
+    def _gaussians(self, step: int):
+        L = self.layout
+        th = self.allocator.theta
+        pools = self.allocator.physical_pools
+        return gaussians_struct(pools["means"], pools["quats"], pools["scales"], pools["opacities"],
+                                th[:, L.color_col:], colors_dim=sh_cols_for(step, self.cfg),
+                                table=self.allocator.indirection_table)
+
+    def _grad_out(self, step: int):
+        L = self.layout
+        gb = self.grad
+        o = L.offsets
+        return grads_struct(gb[:, o["means"]:o["means"] + 3], gb[:, o["quats"]:o["quats"] + 4],
+                            gb[:, o["scales"]:o["scales"] + 3], gb[:, o["opacities"]:o["opacities"] + 1],
+                            gb[:, L.color_col:], colors_write=L.color_cols, colors_by_visible=False,
+                            accumulate=False, reg=self.cfg.param_reg, reg_color_cols=sh_cols_for(step, self.cfg))
+
+    # ------------------------------------------------------------------ one step
+    def train_step(self, view_idx: int, step: int, target: Optional[torch.Tensor] = None,
+                   timer: Optional[StepTimer] = None):
+        """One view: forward, backward, (all-reduce), Adam.  ``target`` is a
+        device uint8 HWC image (defaults to ``targets[view_idx]``)."""
+        cfg = self.cfg
+        lib = _lib.lib()
+        st = _lib.stream_ptr(self.device)
+        self.optimizer.lr = lr_at(cfg.lr, step, cfg.max_steps)
+        N = self.allocator.num_active
+        cam = self.cams[view_idx % len(self.cams)]
+        if target is None and self.targets is not None:
+            target = self.targets[view_idx % self.targets.shape[0]]
+        loss_mode = _lib.GS_LOSS_MEAN if (cfg.loss == "mean" or target is None) else (
+            _lib.GS_LOSS_L1_U8 if target.dtype == torch.uint8 else _lib.GS_LOSS_L1_F32)
+        g = self._gaussians(step)
+        if timer:
+            timer.mark("start")
+        ids, _, V = cull_ids(g, N, cam, self.device, cfg.near_plane, cfg.far_plane, cfg.opacity_threshold)
+        if timer:
+            timer.mark("cull")
+        frame = render_forward(g, ids, V, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
+                               timer=timer)
+        _lib.check(lib.gs_fill_rows(self.grad.data_ptr(), N, self.layout.stride, _lib.fptr(self._reg_pattern()), st),
+                   "grad init")
+        if timer:
+            timer.mark("grad_init")
+        render_backward(frame, g, self._grad_out(step), self.device, grad2d=self.allocator.grad2d,
+                        count=self.allocator.count, timer=timer)
+        scale = 1.0
+        if self.pg is not None and self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.grad[:N], group=self.pg)
+            scale = 1.0 / self.world
+            if timer:
+                timer.mark("allreduce")
+        self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
+                                 self.allocator.indirection_table, N, self.layout.ncols, self.col_lo, self.col_hi,
+                                 quat_col=self.layout.quat_col, grad_scale=scale)
+        if timer:
+            timer.mark("adam")
+        self.last_frame = frame
+        self.step_count += 1
+        return frame
+
+    def loss_value(self, frame=None) -> torch.Tensor:
+        f = frame or self.last_frame
+        P = f.cam.render_width * f.cam.render_height
+        return f.loss_partials.sum() / (3.0 * P)
+
+    # ------------------------------------------------------------------ full loop
+    def train(self, log_every: int = 20):
+        cfg = self.cfg
+        t0 = time.time()
+        for step in range(1, cfg.max_steps + 1):
+            v = (step - 1) % len(self.cams)
+            self.train_step(v, step)
+            if cfg.opacity_reset:
+                interval = 1000 if cfg.max_steps <= 3000 else 3000
+                if step % interval == 0:
+                    self.allocator.reset_opacities(-4.59)
+            if log_every and (step % log_every == 0 or step == 1):
+                print(f"Step {step:5d} | Active: {self.allocator.num_active} | loss {float(self.loss_value()):.5f}")
+        torch.cuda.synchronize(self.device)
+        return time.time() - t0
+
+
+def runner_for_workload(name: str, max_steps: int = 100, num_views: Optional[int] = None, device=None,
+                        n: Optional[int] = None, lr: float = 1e-3, eps: float = 1e-15, seed: int = 0,
+                        loss: str = "l1", upload_targets: bool = True, **overrides) -> RunnerMLX:
+    """A runner for one of the synthetic workloads (``synthetic.WORKLOADS``)."""
+    wl = synthetic.WORKLOADS[name]
+    g = synthetic.make_gaussians(wl, seed=seed, n=n)
+    views, K = synthetic.make_cameras(wl, seed=2, num_views=num_views)
+    cap = wl.capacity or g["means"].shape[0]
+    cfg = MLXConfig(max_gaussians=cap, max_steps=max_steps, lr=lr, sh_degree=wl.sh_degree, sh_degree_interval=1,
+                    width=wl.width, height=wl.height, render_width=wl.width, render_height=wl.height, eps=eps,
+                    loss=loss)
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    targets = None
+    if upload_targets and wl.target_kind == "uint8":
+        targets = torch.from_numpy(synthetic.make_uint8_targets(wl, min(len(views), 8), seed=1)).to(dev)
+    elif upload_targets and wl.target_kind == "render":
+        targets = render_targets(wl, views, K, dev, seed=1, n=n)
+    return RunnerMLX(cfg, g, views, K, targets=targets, device=dev)
+
+
+def render_targets(wl: synthetic.Workload, views: np.ndarray, K: np.ndarray, device, seed: int = 1,
+                   n: Optional[int] = None) -> torch.Tensor:
+    """Target images rendered from a second seeded Gaussian set (float32 HWC per view)."""
+    from .rendering import frustum_culling_mlx, rasterize_gaussians_mlx
+    g = synthetic.make_gaussians(wl, seed=seed, n=n)
+    t = {k: torch.from_numpy(v).to(device) for k, v in g.items()}
+    cols = torch.cat([t["sh0"], t["shN"]], 1)
+    out = []
+    with torch.no_grad():
+        for vm in views:
+            ids = frustum_culling_mlx(t["means"], None, None, vm, K, wl.width, wl.height, opacities=t["opacities"])
+            C, _ = rasterize_gaussians_mlx(t["means"], t["quats"], t["scales"], t["opacities"], cols, vm, K,
+                                           wl.width, wl.height, ids, render_width=wl.width, render_height=wl.height)
+            out.append(C.contiguous())
+    return torch.stack(out)

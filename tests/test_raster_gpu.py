@@ -1,0 +1,199 @@
+"""Tile rasterizer (forward + backward) against the dense oracle and the
+reference-generated golden vectors.  Tolerances: ``tests/gsutil.py``
+(images 1e-4 absolute, gradients 1e-3 relative)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gsutil import assert_grad_close, assert_image_close
+from mlx_gsplat_b200 import _lib, frustum_culling_mlx, rasterize_gaussians_mlx, synthetic
+from mlx_gsplat_b200.rendering import (DEFAULT_SETTINGS, camera_struct, gaussians_struct, grads_struct,
+                                       render_backward, render_forward)
+from oracle import rendering as orend
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+NAMES = ("means", "quats", "scales", "opacities", "colors")
+
+
+def _t(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+
+
+def _scene(wl_name, n, seed=0, sh_dim=None):
+    wl = synthetic.WORKLOADS[wl_name]
+    g = synthetic.make_gaussians(wl, seed=seed, n=n)
+    cols = np.concatenate([g["sh0"], g["shN"]], 1)
+    if sh_dim is not None:
+        cols = cols[:, :sh_dim]
+    return wl, g, cols.astype(np.float32)
+
+
+@pytest.mark.parametrize("case", ["sh0", "sh1", "sh3", "scaled"])
+def test_matches_reference_golden(golden_dir, case):
+    d = np.load(os.path.join(golden_dir, "raster.npz"))
+    p = lambda k: d[f"{case}_{k}"]  # noqa: E731
+    W, H, RW, RH = [int(x) for x in p("dims")]
+    params = {k: _t(p(k)).requires_grad_(True) for k in NAMES}
+    ids = _t(p("ids"))
+    C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                   params["colors"], p("viewmat"), p("K"), W, H, ids, render_width=RW,
+                                   render_height=RH)
+    assert_image_close(C.detach().cpu().numpy(), p("out_colors"), what="colors")
+    assert_image_close(A.detach().cpu().numpy(), p("out_alphas"), what="alphas")
+    loss = torch.mean(torch.abs(C - _t(p("target")))) + torch.mean(A * _t(p("wA")))
+    loss.backward()
+    assert abs(float(loss) - float(p("loss"))) < 1e-5
+    for k in NAMES:
+        assert_grad_close(params[k].grad.cpu().numpy(), p("grad_" + k), what=f"{case} grad {k}")
+
+
+def _oracle_grads(g, cols_vis, ids, vm, K, W, H, dC, dA=None, pixel_ids=None):
+    ids64 = ids.astype(np.int64)
+    C, A, gr = orend.rasterize_dense_vjp(g["means"][ids64], g["quats"][ids64], g["scales"][ids64],
+                                         g["opacities"][ids64], cols_vis, vm, K, W, H, W, H, dL_dC=dC, dL_dA=dA,
+                                         pixel_ids=pixel_ids, chunk=256 if pixel_ids is None else 16)
+    full = {}
+    for k in ("means", "quats", "scales", "opacities"):
+        z = np.zeros_like(g[k], dtype=np.float64)
+        z[ids64] = gr[k]
+        full[k] = z
+    full["colors"] = gr["colors"]
+    return C, A, full
+
+
+@pytest.mark.parametrize("sh_dim", [3, 12])
+def test_tiny_full_image_forward_backward_vs_oracle(sh_dim):
+    wl, g, cols = _scene("tiny-3k", 3000, seed=0, sh_dim=sh_dim)
+    views, K = synthetic.make_cameras(wl, seed=2)
+    rng = np.random.default_rng(1)
+    P = wl.pixels
+    for vi in (0, 3):
+        vm = views[vi]
+        params = {"means": _t(g["means"]), "quats": _t(g["quats"]), "scales": _t(g["scales"]),
+                  "opacities": _t(g["opacities"])}
+        ids = frustum_culling_mlx(params["means"], None, None, vm, K, wl.width, wl.height,
+                                  opacities=params["opacities"])
+        idn = ids.cpu().numpy()
+        cols_vis = cols[idn.astype(np.int64)]
+        for k in params:
+            params[k].requires_grad_(True)
+        params["colors"] = _t(cols_vis).requires_grad_(True)
+        C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                       params["colors"], vm, K, wl.width, wl.height, ids, render_width=wl.width,
+                                       render_height=wl.height)
+        wC = rng.uniform(-1, 1, (wl.height, wl.width, 3)).astype(np.float32) / P
+        wA = rng.uniform(-1, 1, (wl.height, wl.width, 1)).astype(np.float32) / P
+        (torch.sum(C * _t(wC)) + torch.sum(A * _t(wA))).backward()
+        Cr, Ar, gr = _oracle_grads(g, cols_vis, idn, vm, K, wl.width, wl.height, wC, wA)
+        assert_image_close(C.detach().cpu().numpy(), Cr, what=f"view {vi} colors")
+        assert_image_close(A.detach().cpu().numpy(), Ar, what=f"view {vi} alphas")
+        for k in NAMES:
+            assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what=f"view {vi} grad {k}")
+
+
+def _subset(wl, n_pix, seed):
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(wl.pixels, n_pix, replace=False))
+
+
+@pytest.mark.parametrize("wl_name,n,n_pix", [("mid-200k", 200_000, 512), ("outdoor-1m", 1_000_000, 96)])
+def test_full_size_pixel_subset_vs_oracle(wl_name, n, n_pix):
+    """Full-size scenes: the oracle evaluates only a pixel subset (dense over every
+    visible Gaussian); the cotangent is non-zero only there."""
+    wl, g, cols = _scene(wl_name, n, seed=0, sh_dim=12 if wl_name == "outdoor-1m" else 3)
+    views, K = synthetic.make_cameras(wl, seed=2, num_views=8)
+    vm = views[1]
+    params = {"means": _t(g["means"]), "quats": _t(g["quats"]), "scales": _t(g["scales"]),
+              "opacities": _t(g["opacities"])}
+    ids = frustum_culling_mlx(params["means"], None, None, vm, K, wl.width, wl.height,
+                              opacities=params["opacities"])
+    idn = ids.cpu().numpy()
+    cols_vis = cols[idn.astype(np.int64)]
+    for k in params:
+        params[k].requires_grad_(True)
+    params["colors"] = _t(cols_vis).requires_grad_(True)
+    C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                   params["colors"], vm, K, wl.width, wl.height, ids, render_width=wl.width,
+                                   render_height=wl.height)
+    pix = _subset(wl, n_pix, seed=5)
+    rng = np.random.default_rng(2)
+    wsub = rng.uniform(-1, 1, (n_pix, 3)).astype(np.float32)
+    wC = np.zeros((wl.pixels, 3), np.float32)
+    wC[pix] = wsub
+    (torch.sum(C * _t(wC.reshape(wl.height, wl.width, 3)))).backward()
+    Cr, Ar, gr = _oracle_grads(g, cols_vis, idn, vm, K, wl.width, wl.height, wsub, None, pixel_ids=pix)
+    Cg = C.detach().cpu().numpy().reshape(-1, 3)[pix]
+    Ag = A.detach().cpu().numpy().reshape(-1, 1)[pix]
+    assert_image_close(Cg, Cr, what="colors at subset")
+    assert_image_close(Ag, Ar, what="alphas at subset")
+    for k in NAMES:
+        assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what=f"{wl_name} grad {k}")
+
+
+def test_fused_l1_loss_matches_autograd_path():
+    wl, g, cols = _scene("mid-200k", 50_000, seed=1)
+    views, K = synthetic.make_cameras(wl, seed=2, num_views=4)
+    vm = views[2]
+    target = synthetic.make_uint8_targets(wl, 1, seed=1)[0]
+    gs = {k: _t(g[k]) for k in ("means", "quats", "scales", "opacities")}
+    colors = _t(cols)
+    ids = frustum_culling_mlx(gs["means"], None, None, vm, K, wl.width, wl.height, opacities=gs["opacities"])
+    V = int(ids.numel())
+    cam = camera_struct(vm, K, wl.width, wl.height, wl.width, wl.height)
+    st = gaussians_struct(gs["means"], gs["quats"], gs["scales"], gs["opacities"], colors)
+    T8 = _t(target)
+    f = render_forward(st, ids, V, cam, DEFAULT_SETTINGS, torch.device(DEV), loss_mode=_lib.GS_LOSS_L1_U8,
+                       target=T8)
+    loss = float(f.loss_partials.sum()) / (3 * wl.pixels)
+    Cn = f.color.cpu().numpy().astype(np.float64)
+    ref_loss = np.mean(np.abs(Cn - target.astype(np.float32) / np.float32(255.0)))
+    assert abs(loss - ref_loss) < 1e-6
+    grads = {k: torch.zeros_like(v) for k, v in gs.items()}
+    gcol = torch.zeros_like(colors)
+    out = grads_struct(grads["means"], grads["quats"], grads["scales"], grads["opacities"], gcol, colors_write=3)
+    render_backward(f, st, out, torch.device(DEV))
+    # same thing through autograd with an explicit cotangent sign(C - t) / (3P)
+    p2 = {k: v.clone().requires_grad_(True) for k, v in gs.items()}
+    c2 = colors.clone().requires_grad_(True)
+    C, A = rasterize_gaussians_mlx(p2["means"], p2["quats"], p2["scales"], p2["opacities"], c2, vm, K, wl.width,
+                                   wl.height, ids, render_width=wl.width, render_height=wl.height)
+    tf = T8.float() / 255.0
+    torch.mean(torch.abs(C - tf)).backward()
+    for k in gs:
+        assert_grad_close(grads[k].cpu().numpy(), p2[k].grad.cpu().numpy(), rtol=1e-5, what=k)
+    assert_grad_close(gcol.cpu().numpy(), c2.grad.cpu().numpy(), rtol=1e-5, what="colors")
+
+
+def test_empty_and_degenerate_inputs():
+    wl, g, cols = _scene("tiny-3k", 200, seed=4)
+    views, K = synthetic.make_cameras(wl, seed=2)
+    m = _t(g["means"])
+    C, A = rasterize_gaussians_mlx(m, _t(g["quats"]), _t(g["scales"]), _t(g["opacities"]), _t(cols), views[0], K,
+                                   wl.width, wl.height, torch.zeros(0, dtype=torch.int32, device=DEV),
+                                   render_width=wl.width, render_height=wl.height)
+    assert float(C.abs().sum()) == 0.0 and float(A.abs().sum()) == 0.0
+    # one huge Gaussian just in front of the camera covering every tile, plus zero quats
+    g2 = {k: v[:20].copy() for k, v in g.items()}
+    cam_c = -(views[0][:3, :3].T @ views[0][:3, 3])
+    fwd = -cam_c / np.linalg.norm(cam_c)
+    g2["means"][0] = (cam_c + 0.05 * fwd).astype(np.float32)
+    g2["scales"][0] = -2.0
+    g2["quats"][1] = 0.0
+    c2 = cols[:20]
+    ids = np.arange(20, dtype=np.int32)
+    params = {k: _t(g2[k]).requires_grad_(True) for k in ("means", "quats", "scales", "opacities")}
+    params["colors"] = _t(c2).requires_grad_(True)
+    C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                   params["colors"], views[0], K, wl.width, wl.height, _t(ids),
+                                   render_width=wl.width, render_height=wl.height)
+    rng = np.random.default_rng(0)
+    wC = rng.uniform(-1, 1, C.shape).astype(np.float32) / wl.pixels
+    torch.sum(C * _t(wC)).backward()
+    Cr, Ar, gr = _oracle_grads(g2, c2, ids, views[0], K, wl.width, wl.height, wC.reshape(-1, 3))
+    assert_image_close(C.detach().cpu().numpy(), Cr)
+    assert_image_close(A.detach().cpu().numpy(), Ar)
+    for k in NAMES:
+        assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what="degenerate grad " + k)
