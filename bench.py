@@ -44,6 +44,13 @@ def peaks():
     return {"hbm_gbs": PEAKS_FALLBACK["hbm_gbs"], "src": "fallback"}
 
 
+def metric_name(workload: str) -> str:
+    from mlx_gsplat_b200 import synthetic
+    wl = synthetic.WORKLOADS[workload]
+    return (f"train steps/s (1 view per GPU per step, fwd+bwd+Adam) @ {workload} "
+            f"{wl.num_gaussians} Gaussians {wl.width}x{wl.height}")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -207,11 +214,11 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     base = cpu_baseline(args.workload, max(5.0, min(args.cpu_seconds, 60.0)))
-    line = {"metric": "train steps/s (1 view per GPU per step) @ outdoor-1m 1297x840",
+    line = {"metric": metric_name(args.workload),
             "value": base["value"], "unit": "train steps/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": args.workload, "gaussians": 1_000_000, "image": "1297x840", "sh_degree": 3},
+            "config": {"workload": args.workload},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "train steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -328,7 +335,7 @@ def main():
         base = cpu_baseline(args.workload, args.cpu_seconds)
 
     if rank == 0:
-        line = {"metric": "train steps/s (1 view per GPU per step) @ outdoor-1m 1297x840", "value": value,
+        line = {"metric": metric_name(args.workload), "value": value,
                 "unit": "train steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic",

@@ -122,10 +122,13 @@ int gs_clear_buffer_cache(void);
 
 /* One parameter group with explicit row strides (pools whose rows are views
  * into a wider slab).  ``grad_scale`` multiplies g first (1/world_size after
- * a gradient all-reduce). */
+ * a gradient all-reduce).  ``lr``/``beta1``/``beta2`` are the caller's float64
+ * values: GS_ADAM_FUSED rounds them to float32 as the Metal kernel's
+ * arguments are; GS_ADAM_PURE forms 1 - beta and the bias corrections in
+ * float64 first, as the pure-MLX step does with Python floats. */
 int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                         int64_t num_active, int dim, int64_t pool_stride, int64_t g_stride,
-                        float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                        double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                         float a_min, float a_max, float lr_scale, float grad_scale, int mode,
                         gs_stream_t stream);
 
@@ -139,7 +142,7 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
-                       float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                       double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                        float grad_scale, int mode, gs_stream_t stream);
 
 /* ------------------------------------------------------------------ cull */

@@ -64,16 +64,17 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
     v[p] = vv;
 }
 
-// One thread per float4 chunk of a pooled row.
+// One thread per float4 chunk of a pooled row; 2^lane_shift consecutive
+// threads own one row (the smallest power of two >= the row's chunk count).
 __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
                                                         float4* __restrict__ m, float4* __restrict__ v,
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
-                                                        int g_chunks, int ncols, int quat_chunk, AdamScalars s,
-                                                        SlabCols cols) {
+                                                        int lane_shift, int g_chunks, int ncols, int quat_chunk,
+                                                        AdamScalars s, SlabCols cols) {
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= n_rows * chunks) return;
-    const int64_t r = t / chunks;
-    const int c4 = (int)(t - r * chunks);
+    const int64_t r = t >> lane_shift;
+    const int c4 = (int)(t & ((1 << lane_shift) - 1));
+    if (r >= n_rows || c4 >= chunks) return;
     const int c0 = 4 * c4;
     if (c0 >= ncols) return;
     const int64_t off = (int64_t)__ldg(idx + r) * chunks + c4;
@@ -99,32 +100,34 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
     v[off] = vv;
 }
 
-// Host-side scalars for each semantics.
-static AdamScalars make_scalars(int mode, float beta1, float beta2, float eps, float wd, int step, float grad_scale,
-                                double* bc1_out) {
+// Host-side scalars for each semantics.  ``lr``/``beta1``/``beta2`` arrive in
+// float64 (the Python values): the fused mode rounds them to float32 first, as
+// the Metal kernel receives them (src/mlx_extensions.cpp:259-263); the pure
+// mode forms 1 - beta and the bias corrections in float64 and rounds each
+// scalar once, as MLX does with Python floats (optimizer.py:75-76, 162-167).
+static AdamScalars make_scalars(int mode, double beta1, double beta2, float eps, float wd, int step,
+                                float grad_scale, double* bc1_out) {
     AdamScalars s;
-    s.b1 = beta1;
-    s.b2 = beta2;
+    s.b1 = (float)beta1;
+    s.b2 = (float)beta2;
     s.eps = eps;
     s.wd = wd;
     s.grad_scale = grad_scale;
     if (mode == GS_ADAM_FUSED) {
-        // float32 everywhere, as the Metal kernel computes them (:131-146)
-        s.omb1 = 1.0f - beta1;
-        s.omb2 = 1.0f - beta2;
-        const float bc1 = 1.0f - powf(beta1, (float)step);
-        const float bc2 = 1.0f - powf(beta2, (float)step);
+        const float b1 = (float)beta1, b2 = (float)beta2;
+        s.omb1 = 1.0f - b1;
+        s.omb2 = 1.0f - b2;
+        const float bc1 = 1.0f - powf(b1, (float)step);
+        const float bc2 = 1.0f - powf(b2, (float)step);
         s.sqrt_bc2 = sqrtf(bc2);
         *bc1_out = bc1;
         s.scrub = 1;
         s.clamp = 1;
     } else {
-        // float64 Python scalars rounded once to float32 (optimizer.py:75-76, 162-167)
-        const double b1 = (double)beta1, b2 = (double)beta2;
-        s.omb1 = (float)(1.0 - b1);
-        s.omb2 = (float)(1.0 - b2);
-        const double bc1 = 1.0 - pow(b1, (double)step);
-        const double bc2 = 1.0 - pow(b2, (double)step);
+        s.omb1 = (float)(1.0 - beta1);
+        s.omb2 = (float)(1.0 - beta2);
+        const double bc1 = 1.0 - pow(beta1, (double)step);
+        const double bc2 = 1.0 - pow(beta2, (double)step);
         s.sqrt_bc2 = (float)sqrt(bc2);
         *bc1_out = bc1;
         s.scrub = 0;
@@ -133,9 +136,9 @@ static AdamScalars make_scalars(int mode, float beta1, float beta2, float eps, f
     return s;
 }
 
-static float step_size_for(int mode, float lr, float lr_scale, double bc1) {
-    if (mode == GS_ADAM_FUSED) return lr / (float)bc1;  // float32 division, no lr_scales
-    return (float)(((double)lr * (double)lr_scale) / bc1);
+static float step_size_for(int mode, double lr, double lr_scale, double bc1) {
+    if (mode == GS_ADAM_FUSED) return (float)lr / (float)bc1;  // float32 division, no lr_scales
+    return (float)((lr * lr_scale) / bc1);
 }
 
 }  // namespace gs
@@ -143,8 +146,8 @@ static float step_size_for(int mode, float lr, float lr_scale, double bc1) {
 using namespace gs;
 
 extern "C" int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const int32_t* indices,
-                                   int64_t num_active, int dim, int64_t pool_stride, int64_t g_stride, float lr,
-                                   float beta1, float beta2, float eps, float weight_decay, int step, float a_min,
+                                   int64_t num_active, int dim, int64_t pool_stride, int64_t g_stride, double lr,
+                                   double beta1, double beta2, float eps, float weight_decay, int step, float a_min,
                                    float a_max, float lr_scale, float grad_scale, int mode, gs_stream_t stream) {
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam: unknown mode %d", mode);
     GS_REQUIRE(num_active >= 0 && dim > 0 && step >= 1, "adam: bad sizes (num_active=%lld dim=%d step=%d)",
@@ -164,7 +167,7 @@ extern "C" int gs_fused_adam_group(float* theta, const float* g, float* m, float
 extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                                   int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                                   const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
-                                  float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                                  double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                                   float grad_scale, int mode, gs_stream_t stream) {
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
@@ -185,10 +188,12 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         cols.step_size[c] = on ? step_size_for(mode, lr, col_lr_scale ? col_lr_scale[c] : 1.0f, bc1) : 0.f;
     }
     const int chunks = (int)(stride / 4);
-    const int64_t n = num_active * chunks;
+    int shift = 0;
+    while ((1 << shift) < chunks) ++shift;
+    const int64_t n = num_active << shift;
     adam_slab_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
-        reinterpret_cast<float4*>(v), indices, num_active, chunks, (int)(g_stride / 4), ncols,
+        reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
         quat_col < 0 ? -1 : quat_col / 4, s, cols);
     return check_launch("adam_slab_kernel");
 }

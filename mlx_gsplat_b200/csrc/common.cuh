@@ -49,6 +49,27 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Sums eight per-lane values over the warp with 9 shuffles (a butterfly that
+// halves the number of values carried at each of the first three steps).  On
+// return lane l holds the warp total of value index (l >> 2) & 7.
+__device__ __forceinline__ float warp_sum8(float v0, float v1, float v2, float v3, float v4, float v5, float v6,
+                                           float v7, int lane) {
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    // offset 16: keep values 0-3 (bit4 = 0) or 4-7 (bit4 = 1)
+    float w0 = (b4 ? v4 : v0) + __shfl_xor_sync(kFull, b4 ? v0 : v4, 16);
+    float w1 = (b4 ? v5 : v1) + __shfl_xor_sync(kFull, b4 ? v1 : v5, 16);
+    float w2 = (b4 ? v6 : v2) + __shfl_xor_sync(kFull, b4 ? v2 : v6, 16);
+    float w3 = (b4 ? v7 : v3) + __shfl_xor_sync(kFull, b4 ? v3 : v7, 16);
+    // offset 8: keep (w0, w1) or (w2, w3)
+    float x0 = (b3 ? w2 : w0) + __shfl_xor_sync(kFull, b3 ? w0 : w2, 8);
+    float x1 = (b3 ? w3 : w1) + __shfl_xor_sync(kFull, b3 ? w1 : w3, 8);
+    // offset 4: keep x0 or x1
+    float y = (b2 ? x1 : x0) + __shfl_xor_sync(kFull, b2 ? x0 : x1, 4);
+    y += __shfl_xor_sync(kFull, y, 2);
+    y += __shfl_xor_sync(kFull, y, 1);
+    return y;
+}
+
 __device__ __forceinline__ unsigned lanemask_lt() {
     unsigned m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

@@ -163,6 +163,16 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     for (int k = 0; k < 3; ++k) s.rgb[k] = fminf(fmaxf(s.pre[k], 0.0f), 1.0f);
 }
 
+// ------------------------------------------------------------------ per-pixel contribution rule
+// A (pixel, splat) pair contributes iff its Mahalanobis distance m satisfies
+// m <= 2 ln(opacity / alpha_cutoff), i.e. alpha = opacity * exp(-m/2) >=
+// alpha_cutoff.  The bound is stored in the splat record; forward and backward
+// apply the same test to the same floats, so they see the same pairs.  A
+// splat too faint to reach alpha_cutoff anywhere gets -1 (never contributes).
+__device__ __forceinline__ float pair_cut(float opac, const RasterParams& p) {
+    return opac > p.alpha_cut ? 2.0f * logf(opac / p.alpha_cut) : -1.0f;
+}
+
 // ------------------------------------------------------------------ tile binning bound
 // A splat is binned into a tile when some pixel centre of the tile can see
 // alpha >= alpha_cut, i.e. Mahalanobis m <= m_cut = 2 ln(opac / alpha_cut).
@@ -178,7 +188,7 @@ __device__ __forceinline__ bool splat_tile_box(float u, float v, float ca, float
                                                const RasterParams& p, TileBox& tb) {
     if (!(opac > p.alpha_cut)) return false;
     if (!(isfinite(u) && isfinite(v) && isfinite(ca) && isfinite(cb) && isfinite(cc) && isfinite(cd))) return false;
-    tb.m_cut = 2.0f * logf(opac / p.alpha_cut);
+    tb.m_cut = pair_cut(opac, p);
     tb.s = 0.5f * (cb + cc);
     const float det = ca * cd - tb.s * tb.s;
     if (ca > 0.f && cd > 0.f && det > 0.f) {

@@ -22,7 +22,10 @@ __global__ void __launch_bounds__(kTileThreads) render_bwd_kernel(
     const float* __restrict__ dL_dcolor, const float* __restrict__ dL_dalpha, float* __restrict__ splat_grads) {
     __shared__ float4 s0[kTileThreads], s1[kTileThreads], s2[kTileThreads];
     __shared__ uint32_t sv[kTileThreads];
+    __shared__ float acc[kTileThreads][9];  // per-batch CTA sums of the splat gradients
     __shared__ int smax;
+#pragma unroll
+    for (int j = 0; j < 9; ++j) acc[threadIdx.x][j] = 0.f;
     const int tile = blockIdx.x;
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -88,13 +91,13 @@ __global__ void __launch_bounds__(kTileThreads) render_bwd_kernel(
         __syncthreads();
         for (int k = cnt - 1; k >= 0; --k) {
             const int idx = bstart + k - rg.start;
-            const bool valid = idx < last;
+            const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
+            const float x = px - q0.x, y = py - q0.y;
+            const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
+            const bool valid = idx < last && m <= q2.z;
             if (!__any_sync(kFull, valid)) continue;
             float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f, g4 = 0.f, g5 = 0.f, g6 = 0.f, g7 = 0.f, g8 = 0.f;
             if (valid) {
-                const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-                const float x = px - q0.x, y = py - q0.y;
-                const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
                 const float gv = __expf(-0.5f * m);
                 const float og = q1.z * gv;
                 const float al = fminf(og, 0.99f);
@@ -117,21 +120,28 @@ __global__ void __launch_bounds__(kTileThreads) render_bwd_kernel(
                     g4 = dm * y * y;                        // d conic d
                 }
             }
-            g0 = warp_sum(g0);
-            g1 = warp_sum(g1);
-            g2 = warp_sum(g2);
-            g3 = warp_sum(g3);
-            g4 = warp_sum(g4);
-            g5 = warp_sum(g5);
-            g6 = warp_sum(g6);
-            g7 = warp_sum(g7);
+            // warp totals: lane l ends with the total of value (l >> 2) & 7; g8 by butterfly
+            const float t8 = warp_sum8(g0, g1, g2, g3, g4, g5, g6, g7, lane);
             g8 = warp_sum(g8);
-            if (lane == 0) {
-                float* rec = splat_grads + (int64_t)sv[k] * kGradRec;
-                red_add_v4(rec, g0, g1, g2, g3);
-                red_add_v4(rec + 4, g4, g5, g6, g7);
-                atomicAdd(rec + 8, g8);
+            if ((lane & 3) == 0) atomicAdd(&acc[k][lane >> 2], t8);
+            if (lane == 0) atomicAdd(&acc[k][8], g8);
+        }
+        __syncthreads();
+        // one global vector reduction per (tile, splat) with a non-zero gradient
+        if ((int)threadIdx.x < cnt) {
+            float* a = acc[threadIdx.x];
+            const float4 lo = make_float4(a[0], a[1], a[2], a[3]);
+            const float4 hi = make_float4(a[4], a[5], a[6], a[7]);
+            const float b8 = a[8];
+            if (lo.x != 0.f || lo.y != 0.f || lo.z != 0.f || lo.w != 0.f || hi.x != 0.f || hi.y != 0.f ||
+                hi.z != 0.f || hi.w != 0.f || b8 != 0.f) {
+                float* rec = splat_grads + (int64_t)sv[threadIdx.x] * kGradRec;
+                red_add_v4(rec, lo.x, lo.y, lo.z, lo.w);
+                red_add_v4(rec + 4, hi.x, hi.y, hi.z, hi.w);
+                atomicAdd(rec + 8, b8);
             }
+#pragma unroll
+            for (int j = 0; j < 9; ++j) a[j] = 0.f;
         }
     }
 }

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const 
     project_one(g, row, g.colors + crow * g.colors_stride, p, s);
     splats[3 * vi + 0] = make_float4(s.u, s.v, s.ca, s.cb);
     splats[3 * vi + 1] = make_float4(s.cc, s.cd, s.opac, s.rgb[0]);
-    splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], s.tz, 0.f);
+    splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], pair_cut(s.opac, p), s.tz);
     depth_keys[vi] = float_sort_key(s.tz);
     uint32_t cnt = 0;
     TileBox tb;
@@ -128,10 +128,10 @@ __global__ void __launch_bounds__(kTileThreads) render_fwd_kernel(
         const int cnt = min(kTileThreads, rg.end - b);
         for (int k = 0; k < cnt; ++k) {
             if (__all_sync(kFull, done)) break;
-            if (!done) {
-                const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-                const float x = px - q0.x, y = py - q0.y;
-                const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
+            const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
+            const float x = px - q0.x, y = py - q0.y;
+            const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
+            if (!done && m <= q2.z) {
                 const float gv = __expf(-0.5f * m);
                 const float al = fminf(q1.z * gv, 0.99f);
                 const float w = al * T;
