@@ -64,27 +64,17 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
     v[p] = vv;
 }
 
-// One thread per float4 chunk of a pooled row; 2^lane_shift consecutive
-// threads own one row (the smallest power of two >= the row's chunk count).
-__global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
-                                                        float4* __restrict__ m, float4* __restrict__ v,
-                                                        const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
-                                                        int lane_shift, int g_chunks, int ncols, int quat_chunk,
-                                                        AdamScalars s, SlabCols cols) {
-    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t r = t >> lane_shift;
-    const int c4 = (int)(t & ((1 << lane_shift) - 1));
-    if (r >= n_rows || c4 >= chunks) return;
-    const int c0 = 4 * c4;
-    if (c0 >= ncols) return;
-    const int64_t off = (int64_t)__ldg(idx + r) * chunks + c4;
-    float4 th = theta[off], mm = m[off], vv = v[off];
-    const float4 gg = __ldg(g + r * g_chunks + c4);
+// One float4 chunk of a pooled row per work item; 2^lane_shift consecutive
+// items own one row (the smallest power of two >= the row's chunk count).
+// Each thread takes two items, ``half`` apart, and issues all eight 16-byte
+// loads before any arithmetic so that more bytes are in flight per thread.
+__device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, const float4& gg, int c0, int ncols,
+                                            bool renorm, const AdamScalars& s, const SlabCols& cols) {
     if (c0 + 0 < ncols) adam_elem(th.x, mm.x, vv.x, gg.x, s, cols.step_size[c0 + 0], cols.lo[c0 + 0], cols.hi[c0 + 0]);
     if (c0 + 1 < ncols) adam_elem(th.y, mm.y, vv.y, gg.y, s, cols.step_size[c0 + 1], cols.lo[c0 + 1], cols.hi[c0 + 1]);
     if (c0 + 2 < ncols) adam_elem(th.z, mm.z, vv.z, gg.z, s, cols.step_size[c0 + 2], cols.lo[c0 + 2], cols.hi[c0 + 2]);
     if (c0 + 3 < ncols) adam_elem(th.w, mm.w, vv.w, gg.w, s, cols.step_size[c0 + 3], cols.lo[c0 + 3], cols.hi[c0 + 3]);
-    if (c4 == quat_chunk) {
+    if (renorm) {
         float ss = __fmul_rn(th.x, th.x);
         ss = __fadd_rn(ss, __fmul_rn(th.y, th.y));
         ss = __fadd_rn(ss, __fmul_rn(th.z, th.z));
@@ -95,9 +85,48 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         th.z = __fdiv_rn(th.z, n);
         th.w = __fdiv_rn(th.w, n);
     }
-    theta[off] = th;
-    m[off] = mm;
-    v[off] = vv;
+}
+
+__global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
+                                                        float4* __restrict__ m, float4* __restrict__ v,
+                                                        const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
+                                                        int lane_shift, int g_chunks, int ncols, int quat_chunk,
+                                                        int64_t half, AdamScalars s, SlabCols cols) {
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int mask = (1 << lane_shift) - 1;
+    const int c4 = (int)(t0 & mask);  // half is a multiple of 2^lane_shift: both items share the chunk
+    if (c4 >= chunks || 4 * c4 >= ncols) return;
+    const int64_t ra = t0 >> lane_shift, rb = (t0 + half) >> lane_shift;
+    const bool va = ra < n_rows, vb = rb < n_rows;
+    float4 tha, ma, vva, ga, thb, mb, vvb, gb;
+    int64_t offa = 0, offb = 0;
+    if (va) {
+        offa = (int64_t)__ldg(idx + ra) * chunks + c4;
+        tha = theta[offa];
+        ma = m[offa];
+        vva = v[offa];
+        ga = __ldg(g + ra * g_chunks + c4);
+    }
+    if (vb) {
+        offb = (int64_t)__ldg(idx + rb) * chunks + c4;
+        thb = theta[offb];
+        mb = m[offb];
+        vvb = v[offb];
+        gb = __ldg(g + rb * g_chunks + c4);
+    }
+    const bool renorm = c4 == quat_chunk;
+    if (va) {
+        slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cols);
+        theta[offa] = tha;
+        m[offa] = ma;
+        v[offa] = vva;
+    }
+    if (vb) {
+        slab_update(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cols);
+        theta[offb] = thb;
+        m[offb] = mb;
+        v[offb] = vvb;
+    }
 }
 
 // Host-side scalars for each semantics.  ``lr``/``beta1``/``beta2`` arrive in
@@ -190,11 +219,14 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
     const int chunks = (int)(stride / 4);
     int shift = 0;
     while ((1 << shift) < chunks) ++shift;
+    // two items per thread: the second half of the items starts ``half`` (a
+    // multiple of 256, hence of 2^shift) after the first
     const int64_t n = num_active << shift;
-    adam_slab_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+    const int64_t half = (n + 511) / 512 * 256;
+    adam_slab_kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
-        quat_col < 0 ? -1 : quat_col / 4, s, cols);
+        quat_col < 0 ? -1 : quat_col / 4, half, s, cols);
     return check_launch("adam_slab_kernel");
 }
 

@@ -13,135 +13,163 @@ constexpr int kGradRec = 12;  // floats per splat gradient record
 //   val_i = dL/dC . rgb_i + dL/dA,   B_{i-1} = alpha_i val_i + (1 - alpha_i) B_i
 // the alpha gradient is dL/dalpha_i = T_i (val_i - B_i).  The clip of
 // opacity * g to [0, 0.99] passes the gradient only strictly inside
-// (MLX's maximum/minimum rule).  Nine per-splat sums are reduced across the
-// warp and added once per warp with vector reductions.
-__global__ void __launch_bounds__(kTileThreads) render_bwd_kernel(
+// (MLX's maximum/minimum rule).  Thread layout as in the forward (two pixels
+// of one column per thread, 128 threads per tile).  The nine per-splat sums
+// of a warp's 64 pixels are reduced with 14 shuffles, added into per-batch
+// shared-memory accumulators, and flushed with one global vector reduction
+// per (tile, splat).
+struct PixelBwd {
+    float T, dr, dg, db, dA, Bv;
+    int last;
+};
+
+__device__ __forceinline__ void pixel_bwd_init(PixelBwd& s, bool inside, int64_t pix, const RasterParams& p,
+                                               const float* out_color, const float* final_T, const int32_t* n_contrib,
+                                               int loss_mode, const void* target, const float* dL_dcolor,
+                                               const float* dL_dalpha) {
+    s.T = 1.f;
+    s.dr = s.dg = s.db = s.dA = s.Bv = 0.f;
+    s.last = 0;
+    if (!inside) return;
+    s.T = final_T[pix];
+    s.last = n_contrib[pix];
+    if (loss_mode == GS_LOSS_NONE) {
+        s.dr = dL_dcolor[3 * pix + 0];
+        s.dg = dL_dcolor[3 * pix + 1];
+        s.db = dL_dcolor[3 * pix + 2];
+        s.dA = dL_dalpha ? dL_dalpha[pix] : 0.f;
+    } else if (loss_mode == GS_LOSS_MEAN) {
+        s.dr = s.dg = s.db = p.loss_scale;
+    } else {
+        float t0, t1, t2;
+        if (loss_mode == GS_LOSS_L1_U8) {
+            const uint8_t* t8 = static_cast<const uint8_t*>(target) + 3 * pix;
+            t0 = __fdiv_rn((float)t8[0], 255.0f);
+            t1 = __fdiv_rn((float)t8[1], 255.0f);
+            t2 = __fdiv_rn((float)t8[2], 255.0f);
+        } else {
+            const float* tf = static_cast<const float*>(target) + 3 * pix;
+            t0 = tf[0];
+            t1 = tf[1];
+            t2 = tf[2];
+        }
+        const float e0 = out_color[3 * pix + 0] - t0, e1 = out_color[3 * pix + 1] - t1,
+                    e2 = out_color[3 * pix + 2] - t2;
+        s.dr = (e0 > 0.f ? 1.f : (e0 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+        s.dg = (e1 > 0.f ? 1.f : (e1 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+        s.db = (e2 > 0.f ? 1.f : (e2 < 0.f ? -1.f : 0.f)) * p.loss_scale;
+    }
+}
+
+// Adds one pixel's contribution of one splat to the nine running sums.
+__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, float x, float y, float m, float4 q0, float4 q1,
+                                               float4 q2, float* g) {
+    const float gv = __expf(-0.5f * m);
+    const float og = q1.z * gv;
+    const float al = fminf(og, 0.99f);
+    s.T = __fdividef(s.T, 1.f - al);
+    const float val = s.dr * q1.w + s.dg * q2.x + s.db * q2.y + s.dA;
+    const float dal = s.T * (val - s.Bv);
+    s.Bv = al * val + (1.f - al) * s.Bv;
+    const float wT = al * s.T;
+    g[6] += wT * s.dr;
+    g[7] += wT * s.dg;
+    g[8] += wT * s.db;
+    if (og > 0.f && og < 0.99f) {
+        g[5] += dal * gv;                       // d opacity
+        const float dm = -0.5f * gv * (dal * q1.z);
+        const float sbc = q0.w + q1.x;
+        g[0] -= dm * (2.f * q0.z * x + sbc * y);  // d u
+        g[1] -= dm * (sbc * x + 2.f * q1.y * y);  // d v
+        g[2] += dm * x * x;                       // d conic a
+        g[3] += dm * x * y;                       // d conic b (= d conic c)
+        g[4] += dm * y * y;                       // d conic d
+    }
+}
+
+__global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
     const gs_tile_range* __restrict__ ranges, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
     const float* __restrict__ dL_dcolor, const float* __restrict__ dL_dalpha, float* __restrict__ splat_grads) {
-    __shared__ float4 s0[kTileThreads], s1[kTileThreads], s2[kTileThreads];
-    __shared__ uint32_t sv[kTileThreads];
-    __shared__ float acc[kTileThreads][9];  // per-batch CTA sums of the splat gradients
+    __shared__ float4 s0[kBatch], s1[kBatch], s2[kBatch];
+    __shared__ uint32_t sv[kBatch];
+    __shared__ float acc[kBatch][9];  // per-batch CTA sums of the splat gradients
     __shared__ int smax;
-#pragma unroll
-    for (int j = 0; j < 9; ++j) acc[threadIdx.x][j] = 0.f;
     const int tile = blockIdx.x;
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pi = tx * kTile + (warp & 1) * 8 + (lane & 7);
-    const int pj = ty * kTile + (warp >> 1) * 4 + (lane >> 3);
-    const bool inside = pi < p.rw && pj < p.rh;
+    const int pj0 = ty * kTile + (warp >> 1) * 8 + (lane >> 3);
+    const int pj1 = pj0 + 4;
+    const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
     const float px = (float)pi * p.sx + p.hsx;
-    const float py = (float)pj * p.sy + p.hsy;
+    const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
     const gs_tile_range rg = ranges[tile];
+    for (int j = threadIdx.x; j < kBatch; j += kRenderThreads)
+#pragma unroll
+        for (int c = 0; c < 9; ++c) acc[j][c] = 0.f;
 
-    float T = 1.f, dr = 0.f, dg = 0.f, db = 0.f, dA = 0.f;
-    int last = 0;
-    if (inside) {
-        const int64_t pix = (int64_t)pj * p.rw + pi;
-        T = final_T[pix];
-        last = n_contrib[pix];
-        if (loss_mode == GS_LOSS_NONE) {
-            dr = dL_dcolor[3 * pix + 0];
-            dg = dL_dcolor[3 * pix + 1];
-            db = dL_dcolor[3 * pix + 2];
-            dA = dL_dalpha ? dL_dalpha[pix] : 0.f;
-        } else if (loss_mode == GS_LOSS_MEAN) {
-            dr = dg = db = p.loss_scale;
-        } else {
-            float t0, t1, t2;
-            if (loss_mode == GS_LOSS_L1_U8) {
-                const uint8_t* t8 = static_cast<const uint8_t*>(target) + 3 * pix;
-                t0 = __fdiv_rn((float)t8[0], 255.0f);
-                t1 = __fdiv_rn((float)t8[1], 255.0f);
-                t2 = __fdiv_rn((float)t8[2], 255.0f);
-            } else {
-                const float* tf = static_cast<const float*>(target) + 3 * pix;
-                t0 = tf[0];
-                t1 = tf[1];
-                t2 = tf[2];
-            }
-            const float e0 = out_color[3 * pix + 0] - t0, e1 = out_color[3 * pix + 1] - t1,
-                        e2 = out_color[3 * pix + 2] - t2;
-            dr = (e0 > 0.f ? 1.f : (e0 < 0.f ? -1.f : 0.f)) * p.loss_scale;
-            dg = (e1 > 0.f ? 1.f : (e1 < 0.f ? -1.f : 0.f)) * p.loss_scale;
-            db = (e2 > 0.f ? 1.f : (e2 < 0.f ? -1.f : 0.f)) * p.loss_scale;
-        }
-    }
+    PixelBwd a, b;
+    pixel_bwd_init(a, in0, (int64_t)pj0 * p.rw + pi, p, out_color, final_T, n_contrib, loss_mode, target, dL_dcolor,
+                   dL_dalpha);
+    pixel_bwd_init(b, in1, (int64_t)pj1 * p.rw + pi, p, out_color, final_T, n_contrib, loss_mode, target, dL_dcolor,
+                   dL_dalpha);
     if (threadIdx.x == 0) smax = 0;
     __syncthreads();
-    if (last > 0) atomicMax(&smax, last);
+    const int mylast = max(a.last, b.last);
+    if (mylast > 0) atomicMax(&smax, mylast);
     __syncthreads();
     const int max_last = smax;
 
-    float Bv = 0.f;
-    for (int bend = rg.start + max_last; bend > rg.start; bend -= kTileThreads) {
-        const int bstart = max(bend - kTileThreads, rg.start);
+    for (int bend = rg.start + max_last; bend > rg.start; bend -= kBatch) {
+        const int bstart = max(bend - kBatch, rg.start);
         const int cnt = bend - bstart;
         __syncthreads();
-        if ((int)threadIdx.x < cnt) {
-            const uint32_t vr = vals[bstart + threadIdx.x];
+        for (int j = threadIdx.x; j < cnt; j += kRenderThreads) {
+            const uint32_t vr = vals[bstart + j];
             const uint32_t vi = vr < (uint64_t)nv ? vr : 0u;
-            sv[threadIdx.x] = vi;
-            s0[threadIdx.x] = splats[3 * vi];
-            s1[threadIdx.x] = splats[3 * vi + 1];
-            s2[threadIdx.x] = splats[3 * vi + 2];
+            sv[j] = vi;
+            s0[j] = splats[3 * vi];
+            s1[j] = splats[3 * vi + 1];
+            s2[j] = splats[3 * vi + 2];
         }
         __syncthreads();
         for (int k = cnt - 1; k >= 0; --k) {
             const int idx = bstart + k - rg.start;
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-            const float x = px - q0.x, y = py - q0.y;
-            const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
-            const bool valid = idx < last && m <= q2.z;
-            if (!__any_sync(kFull, valid)) continue;
-            float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f, g4 = 0.f, g5 = 0.f, g6 = 0.f, g7 = 0.f, g8 = 0.f;
-            if (valid) {
-                const float gv = __expf(-0.5f * m);
-                const float og = q1.z * gv;
-                const float al = fminf(og, 0.99f);
-                T = T / (1.f - al);
-                const float val = dr * q1.w + dg * q2.x + db * q2.y + dA;
-                const float dal = T * (val - Bv);
-                Bv = al * val + (1.f - al) * Bv;
-                const float wT = al * T;
-                g6 = wT * dr;
-                g7 = wT * dg;
-                g8 = wT * db;
-                if (og > 0.f && og < 0.99f) {
-                    g5 = dal * gv;                      // d opacity
-                    const float dm = -0.5f * gv * (dal * q1.z);
-                    const float sbc = q0.w + q1.x;
-                    g0 = -dm * (2.f * q0.z * x + sbc * y);  // d u
-                    g1 = -dm * (sbc * x + 2.f * q1.y * y);  // d v
-                    g2 = dm * x * x;                        // d conic a
-                    g3 = dm * x * y;                        // d conic b (= d conic c)
-                    g4 = dm * y * y;                        // d conic d
-                }
-            }
-            // warp totals: lane l ends with the total of value (l >> 2) & 7; g8 by butterfly
-            const float t8 = warp_sum8(g0, g1, g2, g3, g4, g5, g6, g7, lane);
-            g8 = warp_sum(g8);
+            const float x = px - q0.x;
+            const float ax = q0.z * x, cx = q1.x * x;
+            const float y0 = py0 - q0.y, y1 = py1 - q0.y;
+            const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
+            const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
+            const bool v0 = idx < a.last && m0 <= q2.z;
+            const bool v1 = idx < b.last && m1 <= q2.z;
+            if (!__any_sync(kFull, v0 || v1)) continue;
+            float g[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (v0) pixel_bwd_step(a, x, y0, m0, q0, q1, q2, g);
+            if (v1) pixel_bwd_step(b, x, y1, m1, q0, q1, q2, g);
+            // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
+            const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
+            const float t9 = warp_sum(g[8]);
             if ((lane & 3) == 0) atomicAdd(&acc[k][lane >> 2], t8);
-            if (lane == 0) atomicAdd(&acc[k][8], g8);
+            if (lane == 0) atomicAdd(&acc[k][8], t9);
         }
         __syncthreads();
         // one global vector reduction per (tile, splat) with a non-zero gradient
-        if ((int)threadIdx.x < cnt) {
-            float* a = acc[threadIdx.x];
-            const float4 lo = make_float4(a[0], a[1], a[2], a[3]);
-            const float4 hi = make_float4(a[4], a[5], a[6], a[7]);
-            const float b8 = a[8];
-            if (lo.x != 0.f || lo.y != 0.f || lo.z != 0.f || lo.w != 0.f || hi.x != 0.f || hi.y != 0.f ||
-                hi.z != 0.f || hi.w != 0.f || b8 != 0.f) {
-                float* rec = splat_grads + (int64_t)sv[threadIdx.x] * kGradRec;
-                red_add_v4(rec, lo.x, lo.y, lo.z, lo.w);
-                red_add_v4(rec + 4, hi.x, hi.y, hi.z, hi.w);
-                atomicAdd(rec + 8, b8);
+        for (int j = threadIdx.x; j < cnt; j += kRenderThreads) {
+            float* r = acc[j];
+            bool any = false;
+#pragma unroll
+            for (int c = 0; c < 9; ++c) any |= r[c] != 0.f;
+            if (any) {
+                float* rec = splat_grads + (int64_t)sv[j] * kGradRec;
+                red_add_v4(rec, r[0], r[1], r[2], r[3]);
+                red_add_v4(rec + 4, r[4], r[5], r[6], r[7]);
+                atomicAdd(rec + 8, r[8]);
             }
 #pragma unroll
-            for (int j = 0; j < 9; ++j) a[j] = 0.f;
+            for (int c = 0; c < 9; ++c) r[c] = 0.f;
         }
     }
 }
@@ -349,7 +377,7 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const uint32_t* e
     GS_REQUIRE(aligned16(splat_grads) && aligned16(splats), "render_backward: records must be 16-byte aligned");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_bwd_kernel<<<tiles, kTileThreads, 0, (cudaStream_t)stream>>>(
+    render_bwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T, n_contrib, loss_mode,
         target, dL_dcolor, dL_dalpha, splat_grads);
     return check_launch("render_bwd_kernel");

@@ -6,33 +6,105 @@
 
 namespace gs {
 
+// ---------------------------------------------------------------- warp-cooperative binning
+// Each lane holds one splat's tile box.  The warp visits the boxes of its
+// lanes one after another and tests 32 tiles of the current box at a time
+// (ballot + popcount give the output positions), so a splat covering
+// thousands of tiles costs thousands / 32 warp steps rather than serialising
+// one thread.  Counting and emission run the same code on the same floats, so
+// they agree tile for tile.
+template <bool kEmit>
+__device__ __forceinline__ uint32_t warp_bin(bool has, const TileBox& tb, float u, float v, float ca, float cd,
+                                             const RasterParams& p, uint32_t base, uint32_t expected, uint32_t vi,
+                                             uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = lanemask_lt();
+    uint32_t mine = 0;
+    unsigned todo = __ballot_sync(kFull, has);
+    while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int x0 = __shfl_sync(kFull, tb.x0, j), x1 = __shfl_sync(kFull, tb.x1, j);
+        const int y0 = __shfl_sync(kFull, tb.y0, j), y1 = __shfl_sync(kFull, tb.y1, j);
+        TileBox b;
+        b.exact = __shfl_sync(kFull, (int)tb.exact, j) != 0;
+        b.m_cut = __shfl_sync(kFull, tb.m_cut, j);
+        b.s = __shfl_sync(kFull, tb.s, j);
+        const float uj = __shfl_sync(kFull, u, j), vj = __shfl_sync(kFull, v, j);
+        const float caj = __shfl_sync(kFull, ca, j), cdj = __shfl_sync(kFull, cd, j);
+        uint32_t basej = 0, expj = 0, vij = 0;
+        if (kEmit) {
+            basej = __shfl_sync(kFull, base, j);
+            expj = __shfl_sync(kFull, expected, j);
+            vij = __shfl_sync(kFull, vi, j);
+        }
+        const int w = x1 - x0 + 1;
+        const int area = w * (y1 - y0 + 1);
+        uint32_t cnt = 0;
+        for (int t0 = 0; t0 < area; t0 += 32) {
+            const int t = t0 + lane;
+            bool hit = false;
+            int tile_id = 0;
+            if (t < area) {
+                const int r = t / w;
+                const int tx = x0 + (t - r * w), ty = y0 + r;
+                hit = splat_hits_tile(uj, vj, caj, cdj, b, tx, ty, p);
+                tile_id = ty * p.tiles_x + tx;
+            }
+            const unsigned bal = __ballot_sync(kFull, hit);
+            if (kEmit && hit) {
+                const uint32_t k = cnt + __popc(bal & lt);
+                if (k < expj) {
+                    keys[basej + k] = (uint32_t)tile_id;
+                    vals[basej + k] = vij;
+                }
+            }
+            cnt += __popc(bal);
+        }
+        if (kEmit) {
+            // the counting pass gave expj == cnt; any shortfall becomes sentinel
+            // entries that sort past every tile and are ignored
+            for (uint32_t k = cnt + lane; k < expj; k += 32) {
+                keys[basej + k] = 0xffffffffu;
+                vals[basej + k] = 0u;
+            }
+        }
+        if (lane == j) mine = cnt;
+    }
+    return mine;
+}
+
 // ---------------------------------------------------------------- projection + tile count
 __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids,
                                                           int64_t nv, RasterParams p, float4* __restrict__ splats,
                                                           uint32_t* __restrict__ depth_keys,
                                                           uint32_t* __restrict__ tile_counts) {
     const int64_t vi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (vi >= nv) return;
-    const int32_t id = ids[vi];
-    const int64_t row = param_row(g, id);
-    const int64_t crow = g.colors_by_visible ? vi : row;
-    ProjState s;
-    project_one(g, row, g.colors + crow * g.colors_stride, p, s);
-    splats[3 * vi + 0] = make_float4(s.u, s.v, s.ca, s.cb);
-    splats[3 * vi + 1] = make_float4(s.cc, s.cd, s.opac, s.rgb[0]);
-    splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], pair_cut(s.opac, p), s.tz);
-    depth_keys[vi] = float_sort_key(s.tz);
-    uint32_t cnt = 0;
+    const bool active = vi < nv;
+    bool has = false;
     TileBox tb;
-    if (splat_tile_box(s.u, s.v, s.ca, s.cb, s.cc, s.cd, s.opac, p, tb)) {
-        if (!tb.exact) {
-            cnt = (uint32_t)((tb.x1 - tb.x0 + 1) * (tb.y1 - tb.y0 + 1));
-        } else {
-            for (int ty = tb.y0; ty <= tb.y1; ++ty)
-                for (int tx = tb.x0; tx <= tb.x1; ++tx) cnt += splat_hits_tile(s.u, s.v, s.ca, s.cd, tb, tx, ty, p);
-        }
+    tb.x0 = tb.x1 = tb.y0 = tb.y1 = 0;
+    tb.exact = true;
+    tb.m_cut = tb.s = 0.f;
+    float u = 0.f, v = 0.f, ca = 0.f, cd = 0.f;
+    if (active) {
+        const int32_t id = ids[vi];
+        const int64_t row = param_row(g, id);
+        const int64_t crow = g.colors_by_visible ? vi : row;
+        ProjState s;
+        project_one(g, row, g.colors + crow * g.colors_stride, p, s);
+        splats[3 * vi + 0] = make_float4(s.u, s.v, s.ca, s.cb);
+        splats[3 * vi + 1] = make_float4(s.cc, s.cd, s.opac, s.rgb[0]);
+        splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], pair_cut(s.opac, p), s.tz);
+        depth_keys[vi] = float_sort_key(s.tz);
+        has = splat_tile_box(s.u, s.v, s.ca, s.cb, s.cc, s.cd, s.opac, p, tb);
+        u = s.u;
+        v = s.v;
+        ca = s.ca;
+        cd = s.cd;
     }
-    tile_counts[vi] = cnt;
+    const uint32_t cnt = warp_bin<false>(has, tb, u, v, ca, cd, p, 0u, 0u, 0u, nullptr, nullptr);
+    if (active) tile_counts[vi] = cnt;
 }
 
 // counts in depth order: out[r] = tile_counts[order[r]]
@@ -50,33 +122,35 @@ __global__ void __launch_bounds__(128) bin_emit_kernel(const float4* __restrict_
                                                        uint32_t* __restrict__ vals, int64_t capacity,
                                                        int32_t* __restrict__ overflow) {
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= nv) return;
-    const uint32_t vi = order[r];
-    const uint32_t cnt = tile_counts[vi];
-    if (cnt == 0) return;
-    const int64_t base = offsets[r];
-    if (base + cnt > capacity) {
-        atomicExch(overflow, 1);
-        return;
-    }
-    const float4 a = splats[3 * vi], b = splats[3 * vi + 1];
+    bool has = false;
     TileBox tb;
-    uint32_t k = 0;
-    if (splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb)) {
-        for (int ty = tb.y0; ty <= tb.y1 && k < cnt; ++ty)
-            for (int tx = tb.x0; tx <= tb.x1 && k < cnt; ++tx)
-                if (splat_hits_tile(a.x, a.y, a.z, b.y, tb, tx, ty, p)) {
-                    tile_keys[base + k] = (uint32_t)(ty * p.tiles_x + tx);
-                    vals[base + k] = vi;
-                    ++k;
+    tb.x0 = tb.x1 = tb.y0 = tb.y1 = 0;
+    tb.exact = true;
+    tb.m_cut = tb.s = 0.f;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    uint32_t vi = 0, cnt = 0, base = 0;
+    if (r < nv) {
+        vi = order[r];
+        cnt = tile_counts[vi];
+        base = offsets[r];
+        if (cnt > 0) {
+            if ((int64_t)base + cnt > capacity) {
+                atomicExch(overflow, 1);
+            } else {
+                a = splats[3 * vi];
+                b = splats[3 * vi + 1];
+                has = splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb);
+                if (!has) {
+                    // cannot happen (the count pass found tiles); keep the sorted list well formed
+                    for (uint32_t k = 0; k < cnt; ++k) {
+                        tile_keys[base + k] = 0xffffffffu;
+                        vals[base + k] = 0u;
+                    }
                 }
+            }
+        }
     }
-    // The counting pass ran the same test on the same floats, so k == cnt; any
-    // shortfall becomes sentinel entries that sort past every tile and are ignored.
-    for (; k < cnt; ++k) {
-        tile_keys[base + k] = 0xffffffffu;
-        vals[base + k] = 0u;
-    }
+    warp_bin<true>(has, tb, a.x, a.y, a.z, b.y, p, base, cnt, vi, tile_keys, vals);
 }
 
 __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n, int32_t num_tiles,
@@ -90,82 +164,116 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
 }
 
 // ---------------------------------------------------------------- compositing
-// One CTA per 16x16 tile, one thread per pixel.  Warp w owns the 8x4 pixel
-// block ((w & 1) * 8, (w >> 1) * 4) of the tile.  Splats are staged 256 at a
-// time in shared memory; a warp skips the rest of a batch once all its pixels
-// are saturated (T < t_min) and the CTA stops when all 256 are.
-__global__ void __launch_bounds__(kTileThreads) render_fwd_kernel(
+// One CTA of 128 threads per 16x16 tile; each thread owns two pixels of one
+// column, 4 rows apart.  Warp w owns the 8x8 block ((w & 1) * 8, (w >> 1) * 8):
+// lane l has column l & 7 and rows (l >> 3) and (l >> 3) + 4.  Splats are
+// staged 256 at a time in shared memory (two per thread) and read back as
+// broadcasts; a warp skips the rest of a batch once all its 64 pixels are
+// saturated (T < t_min) and the CTA stops when all 256 are.
+__device__ __forceinline__ void composite_pixel(float m, float4 q1, float4 q2, float& T, float& cr, float& cg,
+                                                float& cb, float& A, int& last, bool& done, int idx1, float t_min) {
+    if (!done && m <= q2.z) {
+        const float gv = __expf(-0.5f * m);
+        const float al = fminf(q1.z * gv, 0.99f);
+        const float w = al * T;
+        cr += w * q1.w;
+        cg += w * q2.x;
+        cb += w * q2.y;
+        A += w;
+        T *= (1.f - al);
+        last = idx1;
+        if (T < t_min) done = true;
+    }
+}
+
+__device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, int64_t pix, float cr, float cg,
+                                            float cb) {
+    if (loss_mode == GS_LOSS_L1_U8) {
+        const uint8_t* t8 = static_cast<const uint8_t*>(target) + 3 * pix;
+        return fabsf(cr - __fdiv_rn((float)t8[0], 255.0f)) + fabsf(cg - __fdiv_rn((float)t8[1], 255.0f)) +
+               fabsf(cb - __fdiv_rn((float)t8[2], 255.0f));
+    }
+    if (loss_mode == GS_LOSS_L1_F32) {
+        const float* tf = static_cast<const float*>(target) + 3 * pix;
+        return fabsf(cr - tf[0]) + fabsf(cg - tf[1]) + fabsf(cb - tf[2]);
+    }
+    if (loss_mode == GS_LOSS_MEAN) return cr + cg + cb;
+    return 0.f;
+}
+
+__global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
     const gs_tile_range* __restrict__ ranges, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, float* __restrict__ out_color, float* __restrict__ out_alpha, float* __restrict__ final_T,
     int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
     float* __restrict__ loss_partials) {
-    __shared__ float4 s0[kTileThreads], s1[kTileThreads], s2[kTileThreads];
-    __shared__ float red[kTileThreads / 32];
+    __shared__ float4 s0[kBatch], s1[kBatch], s2[kBatch];
+    __shared__ float red[kRenderThreads / 32];
     const int tile = blockIdx.x;
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pi = tx * kTile + (warp & 1) * 8 + (lane & 7);
-    const int pj = ty * kTile + (warp >> 1) * 4 + (lane >> 3);
-    const bool inside = pi < p.rw && pj < p.rh;
+    const int pj0 = ty * kTile + (warp >> 1) * 8 + (lane >> 3);
+    const int pj1 = pj0 + 4;
+    const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
     const float px = (float)pi * p.sx + p.hsx;
-    const float py = (float)pj * p.sy + p.hsy;
+    const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
     const gs_tile_range rg = ranges[tile];
 
-    float T = 1.f, cr = 0.f, cg = 0.f, cb = 0.f, A = 0.f;
-    int last = 0;
-    bool done = !inside;
-    for (int b = rg.start; b < rg.end; b += kTileThreads) {
-        if (__syncthreads_count(done) == kTileThreads) break;
-        const int e = b + threadIdx.x;
-        if (e < rg.end) {
-            const uint32_t vr = vals[e];
-            const uint32_t vi = vr < (uint64_t)nv ? vr : 0u;
-            s0[threadIdx.x] = splats[3 * vi];
-            s1[threadIdx.x] = splats[3 * vi + 1];
-            s2[threadIdx.x] = splats[3 * vi + 2];
+    float T0 = 1.f, r0 = 0.f, g0 = 0.f, b0 = 0.f, A0 = 0.f;
+    float T1 = 1.f, r1 = 0.f, g1 = 0.f, b1 = 0.f, A1 = 0.f;
+    int last0 = 0, last1 = 0;
+    bool done0 = !in0, done1 = !in1;
+    for (int b = rg.start; b < rg.end; b += kBatch) {
+        if (__syncthreads_count(done0 && done1) == kRenderThreads) break;
+#pragma unroll
+        for (int h = 0; h < kBatch / kRenderThreads; ++h) {
+            const int j = threadIdx.x + h * kRenderThreads;
+            const int e = b + j;
+            if (e < rg.end) {
+                const uint32_t vr = vals[e];
+                const uint32_t vi = vr < (uint64_t)nv ? vr : 0u;
+                s0[j] = splats[3 * vi];
+                s1[j] = splats[3 * vi + 1];
+                s2[j] = splats[3 * vi + 2];
+            }
         }
         __syncthreads();
-        const int cnt = min(kTileThreads, rg.end - b);
+        const int cnt = min(kBatch, rg.end - b);
+        const int base1 = b - rg.start + 1;
         for (int k = 0; k < cnt; ++k) {
-            if (__all_sync(kFull, done)) break;
+            if (__all_sync(kFull, done0 && done1)) break;
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-            const float x = px - q0.x, y = py - q0.y;
-            const float m = x * (q0.z * x + q0.w * y) + y * (q1.x * x + q1.y * y);
-            if (!done && m <= q2.z) {
-                const float gv = __expf(-0.5f * m);
-                const float al = fminf(q1.z * gv, 0.99f);
-                const float w = al * T;
-                cr += w * q1.w;
-                cg += w * q2.x;
-                cb += w * q2.y;
-                A += w;
-                T *= (1.f - al);
-                last = b - rg.start + k + 1;
-                if (T < p.t_min) done = true;
-            }
+            const float x = px - q0.x;
+            const float ax = q0.z * x, cx = q1.x * x;
+            const float y0 = py0 - q0.y, y1 = py1 - q0.y;
+            const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
+            const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
+            composite_pixel(m0, q1, q2, T0, r0, g0, b0, A0, last0, done0, base1 + k, p.t_min);
+            composite_pixel(m1, q1, q2, T1, r1, g1, b1, A1, last1, done1, base1 + k, p.t_min);
         }
         __syncthreads();
     }
 
     float lsum = 0.f;
-    if (inside) {
-        const int64_t pix = (int64_t)pj * p.rw + pi;
-        out_color[3 * pix + 0] = cr;
-        out_color[3 * pix + 1] = cg;
-        out_color[3 * pix + 2] = cb;
-        out_alpha[pix] = A;
-        final_T[pix] = T;
-        n_contrib[pix] = last;
-        if (loss_mode == GS_LOSS_L1_U8) {
-            const uint8_t* t8 = static_cast<const uint8_t*>(target) + 3 * pix;
-            lsum = fabsf(cr - __fdiv_rn((float)t8[0], 255.0f)) + fabsf(cg - __fdiv_rn((float)t8[1], 255.0f)) +
-                   fabsf(cb - __fdiv_rn((float)t8[2], 255.0f));
-        } else if (loss_mode == GS_LOSS_L1_F32) {
-            const float* tf = static_cast<const float*>(target) + 3 * pix;
-            lsum = fabsf(cr - tf[0]) + fabsf(cg - tf[1]) + fabsf(cb - tf[2]);
-        } else if (loss_mode == GS_LOSS_MEAN) {
-            lsum = cr + cg + cb;
-        }
+    if (in0) {
+        const int64_t pix = (int64_t)pj0 * p.rw + pi;
+        out_color[3 * pix + 0] = r0;
+        out_color[3 * pix + 1] = g0;
+        out_color[3 * pix + 2] = b0;
+        out_alpha[pix] = A0;
+        final_T[pix] = T0;
+        n_contrib[pix] = last0;
+        lsum += pixel_loss(loss_mode, target, pix, r0, g0, b0);
+    }
+    if (in1) {
+        const int64_t pix = (int64_t)pj1 * p.rw + pi;
+        out_color[3 * pix + 0] = r1;
+        out_color[3 * pix + 1] = g1;
+        out_color[3 * pix + 2] = b1;
+        out_alpha[pix] = A1;
+        final_T[pix] = T1;
+        n_contrib[pix] = last1;
+        lsum += pixel_loss(loss_mode, target, pix, r1, g1, b1);
     }
     if (loss_mode != GS_LOSS_NONE) {
         lsum = warp_sum(lsum);
@@ -174,7 +282,7 @@ __global__ void __launch_bounds__(kTileThreads) render_fwd_kernel(
         if (threadIdx.x == 0) {
             float t = 0.f;
 #pragma unroll
-            for (int w = 0; w < kTileThreads / 32; ++w) t += red[w];
+            for (int w = 0; w < kRenderThreads / 32; ++w) t += red[w];
             loss_partials[tile] = t;
         }
     }
@@ -259,7 +367,7 @@ extern "C" int gs_render_forward(const gs_tile_range* ranges, const uint32_t* en
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || target, "render_forward: target required");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_fwd_kernel<<<tiles, kTileThreads, 0, (cudaStream_t)stream>>>(
+    render_fwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, out_alpha, final_T, n_contrib,
         loss_mode, target, loss_partials);
     return check_launch("render_fwd_kernel");
