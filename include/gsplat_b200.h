@@ -246,6 +246,53 @@ int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_v
 
 /* ------------------------------------------------------------------ pool / densify */
 
+/* Row flags of the densify step. */
+#define GS_FLAG_PRUNE 1  /* the row is pruned */
+#define GS_FLAG_REFINE 2 /* the row is cloned or split into two children */
+#define GS_FLAG_SPLIT 4  /* the refinement shrinks the scales by log(1.6) (split, not clone) */
+
+/* Ordered stream compaction: for every r < n with (flags[r] & mask) == value,
+ * in ascending r, writes gather ? gather[r] : r to out and the number of rows
+ * to *out_count (device int32).  Scratch: gs_cull_scratch_bytes(n).  Used for
+ * the pruned slots (allocator.py:200-204), the refined rows and the kept
+ * indirection entries (allocator.py:276-277). */
+int gs_compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, const int32_t* gather,
+                     int32_t* out, int32_t* out_count, void* scratch, size_t scratch_bytes, gs_stream_t stream);
+
+/* The densify policy per active row (trainer.py:428-477): refine when the
+ * average view-space gradient grad2d/max(count,1) > grad_threshold, split when
+ * also max(exp(scale)) > small_threshold (else clone); prune on non-finite
+ * parameters or | |q| - 1 | > quat_tolerance, and — when prune_geometry —
+ * sigmoid(opacity) < dim_threshold or max(exp(scale)) > large_threshold.
+ * ``g`` addresses the pooled rows through its table; grad2d/count are
+ * indexed by physical slot.  Writes GS_FLAG_* bits to flags[num_active]. */
+int gs_densify_masks(const gs_gaussians* g, const float* grad2d, const float* count, int64_t num_active,
+                     float grad_threshold, float small_threshold, float large_threshold, float dim_threshold,
+                     float quat_tolerance, int prune_geometry, uint8_t* flags, gs_stream_t stream);
+
+/* Child rows of the refined Gaussians (trainer.py:479-507): for child j, whose
+ * parent row is theta[parent_slots[j]] and logical row refine_rows[j], writes
+ * child1[j] and child2[j] (``stride`` floats each): means + 0.02 * noise
+ * (noise_means1 / noise_means2, [n, 3]), scales - log(1.6) when split,
+ * opacity logit * 0.95, quaternion / sqrt(|q|^2 + 1e-8) (child 2 after
+ * + 0.01 * noise_quats2, [n, 4]), every other column copied. */
+int gs_densify_children(const float* theta, int64_t stride, int ncols, const int32_t* parent_slots,
+                        const int32_t* refine_rows, const uint8_t* flags, const float* noise_means1,
+                        const float* noise_means2, const float* noise_quats2, int64_t num_children, int col_means,
+                        int col_scales, int col_quats, int col_opac, float* child1, float* child2,
+                        gs_stream_t stream);
+
+/* theta[slots[j]] = vals[j] (row stride vals_stride), or the host row
+ * ``reset_row_host`` when vals is NULL; m[slots[j]] and v[slots[j]] zeroed
+ * (when given) and grad2d/count[slots[j]] zeroed (when given).  The split,
+ * child and prune writes of allocator.py:229-273. */
+int gs_pool_write_rows(float* theta, float* m, float* v, int64_t stride, const int32_t* slots, int64_t n,
+                       const float* vals, int64_t vals_stride, const float* reset_row_host, float* grad2d,
+                       float* count, gs_stream_t stream);
+
+/* out[j] = stack[top - 1 - j] for j < n: the LIFO pops of allocator.py:219. */
+int gs_free_pop_reversed(const int32_t* stack, int64_t top, int64_t n, int32_t* out, gs_stream_t stream);
+
 /* Writes ``pattern[0..stride)`` into every row r < n_rows of ``dst`` (row stride ``stride``). */
 int gs_fill_rows(float* dst, int64_t n_rows, int64_t stride, const float* pattern_host, gs_stream_t stream);
 

@@ -90,6 +90,14 @@ _SIGS = {
                                           c_vp, c_vp, c_vp, c_vp]),
     "gs_project_backward": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, i64, ctypes.POINTER(GsCamera), c_vp,
                                            ctypes.POINTER(GsGaussianGrads), c_vp, c_vp, c_vp]),
+    "gs_compact_flags": (ctypes.c_int, [c_vp, i64, ctypes.c_uint8, ctypes.c_uint8, c_vp, c_vp, c_vp, c_vp,
+                                        ctypes.c_size_t, c_vp]),
+    "gs_densify_masks": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, c_vp, i64] + [ctypes.c_float] * 5 +
+                         [ctypes.c_int, c_vp, c_vp]),
+    "gs_densify_children": (ctypes.c_int, [c_vp, i64, ctypes.c_int] + [c_vp] * 6 + [i64] + [ctypes.c_int] * 4 +
+                            [c_vp, c_vp, c_vp]),
+    "gs_pool_write_rows": (ctypes.c_int, [c_vp, c_vp, c_vp, i64, c_vp, i64, c_vp, i64, c_float_p, c_vp, c_vp, c_vp]),
+    "gs_free_pop_reversed": (ctypes.c_int, [c_vp, i64, i64, c_vp, c_vp]),
     "gs_fill_rows": (ctypes.c_int, [c_vp, i64, i64, c_float_p, c_vp]),
     "gs_fill_column": (ctypes.c_int, [c_vp, i64, i64, ctypes.c_int, ctypes.c_float, c_vp]),
 }

@@ -177,6 +177,96 @@ class PointerStableChunkedAllocator:
             self.adam_m_pools[n].index_copy_(0, idx, m_dict[n])
             self.adam_v_pools[n].index_copy_(0, idx, v_dict[n])
 
+    # ------------------------------------------------------------------ split / prune
+    FLAG_PRUNE, FLAG_REFINE, FLAG_SPLIT = 1, 2, 4
+
+    def _compact(self, flags: torch.Tensor, n: int, mask: int, value: int, gather: Optional[torch.Tensor]):
+        lib = _lib.lib()
+        out = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
+        cnt = torch.empty(1, dtype=torch.int32, device=self.device)
+        sb = torch.empty(max(lib.gs_cull_scratch_bytes(n), 16), dtype=torch.uint8, device=self.device)
+        _lib.check(lib.gs_compact_flags(flags.data_ptr(), n, mask, value, None if gather is None else gather.data_ptr(),
+                                        out.data_ptr(), cnt.data_ptr(), sb.data_ptr(), sb.numel(),
+                                        _lib.stream_ptr(self.device)), "gs_compact_flags")
+        return out, cnt
+
+    def apply_flags(self, flags: torch.Tensor, make_children) -> Tuple[int, int]:
+        """The realloc-free density step of allocator.py:185-292 driven by
+        per-row GS flags (bit 0 prune, bit 1 refine).  ``make_children(split_slots,
+        refine_rows, n)`` returns the child rows ``(child1, child2)`` as
+        ``[n, stride]`` tensors.  Slot order is the reference's: pruned slots are
+        pushed in ascending logical order and children pop from the same end, so
+        a child can land in a just-pruned slot and is then reset by the prune."""
+        start = time.perf_counter()
+        lib = _lib.lib()
+        st = _lib.stream_ptr(self.device)
+        L = self.layout
+        n = self.num_active
+        table = self.indirection_table
+        P, R = self.FLAG_PRUNE, self.FLAG_REFINE
+        prune_slots, c_p = self._compact(flags, n, P, P, table)
+        split_slots, c_s = self._compact(flags, n, R, R, table)
+        refine_rows, _ = self._compact(flags, n, R, R, None)
+        keep_slots, c_k = self._compact(flags, n, P, 0, table)
+        n_p, n_s, n_keep = [int(x) for x in torch.cat([c_p, c_s, c_k]).tolist()]
+        # 1. prune: slots go back on the free list (allocator.py:209-211)
+        if n_p:
+            self.free_stack[self.free_top:self.free_top + n_p].copy_(prune_slots[:n_p])
+            self.active_mask[prune_slots[:n_p].long()] = 0
+        self.free_top += n_p
+        # 2. children pop from the same end (allocator.py:213-220)
+        if self.free_top < n_s:
+            raise MemoryError(f"pool capacity reached: {self.free_top} free slots, {n_s} children requested")
+        children = torch.empty(max(n_s, 1), dtype=torch.int32, device=self.device)
+        _lib.check(lib.gs_free_pop_reversed(self.free_stack.data_ptr(), self.free_top, n_s, children.data_ptr(), st),
+                   "free list pop")
+        self.free_top -= n_s
+        children = children[:n_s]
+        if n_s:
+            self.active_mask[children.long()] = 1
+        # 3. rows: child 1 -> parent slot, child 2 -> popped slot, then the prune reset (allocator.py:229-273)
+        if n_s:
+            child1, child2 = make_children(split_slots[:n_s], refine_rows[:n_s], n_s)
+            for slots, vals in ((split_slots, child1), (children, child2)):
+                _lib.check(lib.gs_pool_write_rows(self.theta.data_ptr(), self.adam_m.data_ptr(),
+                                                  self.adam_v.data_ptr(), L.stride, slots.data_ptr(), n_s,
+                                                  vals.data_ptr(), vals.stride(0), None, self.grad2d.data_ptr(),
+                                                  self.count.data_ptr(), st), "child rows")
+        if n_p:
+            _lib.check(lib.gs_pool_write_rows(self.theta.data_ptr(), self.adam_m.data_ptr(), self.adam_v.data_ptr(),
+                                              L.stride, prune_slots.data_ptr(), n_p, None, 0,
+                                              _lib.fptr(L.reset_row()), self.grad2d.data_ptr(),
+                                              self.count.data_ptr(), st), "prune reset")
+        # 4. indirection table: kept entries in order, then the children (allocator.py:275-281)
+        self.indirection_table = torch.cat([keep_slots[:n_keep], children]).contiguous()
+        self.allocation_latency_ms = (time.perf_counter() - start) * 1000.0
+        self.update_metrics()
+        self.update_cached_pointers()
+        return n_p, n_s
+
+    def split_and_prune(self, prune_mask, split_mask, split_params: Dict[str, torch.Tensor]) -> Tuple[int, int]:
+        """allocator.py:185-292 with the reference's arguments: boolean masks over
+        the active rows and ``{name}_child1`` / ``{name}_child2`` values per group."""
+        pm = torch.as_tensor(np.asarray(prune_mask) if not isinstance(prune_mask, torch.Tensor) else prune_mask,
+                             device=self.device).to(torch.uint8)
+        sm = torch.as_tensor(np.asarray(split_mask) if not isinstance(split_mask, torch.Tensor) else split_mask,
+                             device=self.device).to(torch.uint8)
+        flags = (pm * self.FLAG_PRUNE + sm * self.FLAG_REFINE).to(torch.uint8).contiguous()
+        L = self.layout
+
+        def make_children(split_slots, refine_rows, n):
+            rows = []
+            for suffix in ("_child1", "_child2"):
+                buf = torch.zeros((n, L.stride), dtype=torch.float32, device=self.device)
+                for name, off in L.offsets.items():
+                    val = split_params[name + suffix]
+                    val = torch.as_tensor(np.asarray(val) if not isinstance(val, torch.Tensor) else val)
+                    buf[:, off:off + L.dims[name]] = val.to(self.device, torch.float32).reshape(n, -1)
+                rows.append(buf)
+            return rows[0], rows[1]
+
+        return self.apply_flags(flags, make_children)
+
     # ------------------------------------------------------------------ opacity reset
     def reset_opacities(self, value: float = -4.59) -> None:
         """trainer.py:416-419: every slot's opacity logit set to ``value``."""

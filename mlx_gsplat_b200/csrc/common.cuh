@@ -12,6 +12,9 @@
 
 namespace gs {
 
+int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, const int32_t* gather, int32_t* out,
+                  int32_t* out_count, void* scratch, size_t scratch_bytes, cudaStream_t stream);
+
 constexpr int kTile = 16;               // tile edge in pixels
 constexpr int kTileThreads = kTile * kTile;
 constexpr int kRenderThreads = 128;     // compositing CTA: two pixels per thread

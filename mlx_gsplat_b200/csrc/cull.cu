@@ -64,8 +64,11 @@ __global__ void __launch_bounds__(kCullThreads) cull_flags(gs_gaussians g, int64
     }
 }
 
+// Ordered write of the set bits: id r lands at its rank among the set bits;
+// the value written is gather[r] when a gather map is given, else r.
 __global__ void __launch_bounds__(kCullThreads) cull_write(const uint32_t* __restrict__ words, int64_t n,
                                                            const uint32_t* __restrict__ chunk_offsets,
+                                                           const int32_t* __restrict__ gather,
                                                            int32_t* __restrict__ out_ids) {
     __shared__ uint32_t woff[kCullChunk / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -97,7 +100,8 @@ __global__ void __launch_bounds__(kCullThreads) cull_write(const uint32_t* __res
         const uint32_t b = words[wi];
         if ((b >> lane) & 1u) {
             const uint32_t pos = off0 + woff[local_word] + __popc(b & lanemask_lt());
-            out_ids[pos] = (int32_t)((wi << 5) + lane);
+            const int64_t r = (wi << 5) + lane;
+            out_ids[pos] = gather ? __ldg(gather + r) : (int32_t)r;
         }
     }
 }
@@ -146,15 +150,73 @@ int cull(const gs_gaussians& g, int64_t n, const gs_camera& cam, float near_p, f
     GS_TRY(check_launch("cull_flags"));
     // counts -> offsets in place; the total lands in counts[chunks]
     GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream));
-    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, out_ids);
+    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, nullptr, out_ids);
     GS_TRY(check_launch("cull_write"));
     cudaMemcpyAsync(out_count, counts + chunks, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
     return check_launch("cull count copy", 0);
 }
 
+// One bit per row: (flags[r] & mask) == value.
+__global__ void __launch_bounds__(kCullThreads) flag_words(const uint8_t* __restrict__ flags, int64_t n, uint8_t mask,
+                                                           uint8_t value, uint32_t* __restrict__ words,
+                                                           uint32_t* __restrict__ chunk_counts) {
+    __shared__ uint32_t wsum[kCullThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t base = (int64_t)blockIdx.x * kCullChunk;
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int k = 0; k < kCullItems; ++k) {
+        const int64_t i = base + (int64_t)k * kCullThreads + threadIdx.x;
+        const bool ok = i < n && (flags[i] & mask) == value;
+        const uint32_t b = __ballot_sync(kFull, ok);
+        const int64_t wi = (base + (int64_t)k * kCullThreads + warp * 32) >> 5;
+        if (lane == 0 && (wi << 5) < n) words[wi] = b;
+        cnt += __popc(b);
+    }
+    if (lane == 0) wsum[warp] = cnt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0;
+#pragma unroll
+        for (int w = 0; w < kCullThreads / 32; ++w) t += wsum[w];
+        chunk_counts[blockIdx.x] = t;
+    }
+}
+
+int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, const int32_t* gather, int32_t* out,
+                  int32_t* out_count, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+    GS_REQUIRE(n >= 0 && n < ((int64_t)1 << 31), "compact: n out of range");
+    GS_REQUIRE(out_count && scratch && scratch_bytes >= cull_scratch_bytes(n), "compact: bad scratch/count");
+    if (n == 0) {
+        cudaMemsetAsync(out_count, 0, sizeof(int32_t), stream);
+        return check_launch("compact(n=0)", 0);
+    }
+    GS_REQUIRE(flags && out, "compact: null pointer");
+    const int64_t chunks = (n + kCullChunk - 1) / kCullChunk;
+    char* p = reinterpret_cast<char*>(align_up(reinterpret_cast<uintptr_t>(scratch), 256));
+    uint32_t* words = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)((n + 31) / 32 + 1) * 4, 256);
+    uint32_t* counts = reinterpret_cast<uint32_t*>(p);
+    p += align_up((size_t)(chunks + 1) * 4, 256);
+    flag_words<<<(unsigned)chunks, kCullThreads, 0, stream>>>(flags, n, mask, value, words, counts);
+    GS_TRY(check_launch("flag_words"));
+    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream));
+    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, gather, out);
+    GS_TRY(check_launch("compact write"));
+    cudaMemcpyAsync(out_count, counts + chunks, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
+    return check_launch("compact count copy", 0);
+}
+
 }  // namespace gs
 
 extern "C" size_t gs_cull_scratch_bytes(int64_t n) { return gs::cull_scratch_bytes(n); }
+
+extern "C" int gs_compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, const int32_t* gather,
+                                int32_t* out, int32_t* out_count, void* scratch, size_t scratch_bytes,
+                                gs_stream_t stream) {
+    return gs::compact_flags(flags, n, mask, value, gather, out, out_count, scratch, scratch_bytes,
+                             (cudaStream_t)stream);
+}
 
 extern "C" int gs_cull(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_plane, float far_plane,
                        float opacity_threshold, int32_t* out_ids, int32_t* out_count, void* scratch,

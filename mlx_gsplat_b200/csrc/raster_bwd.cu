@@ -62,28 +62,31 @@ __device__ __forceinline__ void pixel_bwd_init(PixelBwd& s, bool inside, int64_t
 }
 
 // Adds one pixel's contribution of one splat to the nine running sums.
-__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, float x, float y, float m, float4 q0, float4 q1,
-                                               float4 q2, float* g) {
+// ``a2 = 2 conic_a``, ``sbc = conic_b + conic_c``, ``d2 = 2 conic_d`` are per splat.
+__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, float x, float y, float m, float opac, float4 q1,
+                                               float4 q2, float a2, float sbc, float d2, float* g) {
     const float gv = __expf(-0.5f * m);
-    const float og = q1.z * gv;
+    const float og = opac * gv;
     const float al = fminf(og, 0.99f);
     s.T = __fdividef(s.T, 1.f - al);
     const float val = s.dr * q1.w + s.dg * q2.x + s.db * q2.y + s.dA;
-    const float dal = s.T * (val - s.Bv);
-    s.Bv = al * val + (1.f - al) * s.Bv;
+    const float d = val - s.Bv;
+    const float dal = s.T * d;
+    s.Bv += al * d;  // = al * val + (1 - al) * B
     const float wT = al * s.T;
     g[6] += wT * s.dr;
     g[7] += wT * s.dg;
     g[8] += wT * s.db;
     if (og > 0.f && og < 0.99f) {
-        g[5] += dal * gv;                       // d opacity
-        const float dm = -0.5f * gv * (dal * q1.z);
-        const float sbc = q0.w + q1.x;
-        g[0] -= dm * (2.f * q0.z * x + sbc * y);  // d u
-        g[1] -= dm * (sbc * x + 2.f * q1.y * y);  // d v
-        g[2] += dm * x * x;                       // d conic a
-        g[3] += dm * x * y;                       // d conic b (= d conic c)
-        g[4] += dm * y * y;                       // d conic d
+        const float dog = dal * gv;
+        g[5] += dog;                            // d opacity
+        const float dm = -0.5f * opac * dog;    // dL/dm
+        const float dmx = dm * x, dmy = dm * y;
+        g[0] -= a2 * dmx + sbc * dmy;           // d u
+        g[1] -= sbc * dmx + d2 * dmy;           // d v
+        g[2] += dmx * x;                        // d conic a
+        g[3] += dmx * y;                        // d conic b (= d conic c)
+        g[4] += dmy * y;                        // d conic d
     }
 }
 
@@ -147,8 +150,9 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const bool v1 = idx < b.last && m1 <= q2.z;
             if (!__any_sync(kFull, v0 || v1)) continue;
             float g[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (v0) pixel_bwd_step(a, x, y0, m0, q0, q1, q2, g);
-            if (v1) pixel_bwd_step(b, x, y1, m1, q0, q1, q2, g);
+            const float a2 = 2.f * q0.z, sbc = q0.w + q1.x, d2 = 2.f * q1.y;
+            if (v0) pixel_bwd_step(a, x, y0, m0, q1.z, q1, q2, a2, sbc, d2, g);
+            if (v1) pixel_bwd_step(b, x, y1, m1, q1.z, q1, q2, a2, sbc, d2, g);
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
             const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
             const float t9 = warp_sum(g[8]);

@@ -143,6 +143,14 @@ def make_cameras(wl: Workload, seed: int = 2, num_views: Optional[int] = None):
     return views.astype(np.float32), K
 
 
+def scene_scale(viewmats: np.ndarray) -> float:
+    """Scene extent from the cameras (mlx_gsplat/dataset.py:404-408): the largest
+    distance of a camera centre from the mean centre."""
+    v = np.asarray(viewmats, np.float64)
+    centres = np.stack([-(m[:3, :3].T @ m[:3, 3]) for m in v])
+    return float(np.max(np.linalg.norm(centres - centres.mean(0), axis=1)))
+
+
 def make_uint8_targets(wl: Workload, num: int, seed: int = 1) -> np.ndarray:
     """Seeded random uint8 RGB images ``[num, H, W, 3]``."""
     rng = np.random.default_rng(seed)

@@ -198,6 +198,57 @@ class RunnerMLX:
         self.step_count += 1
         return frame
 
+    # ------------------------------------------------------------------ densify / prune
+    def densify(self, step: int, noise: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[int, int]:
+        """trainer.py:425-519 on the GPU: decisions from the pooled rows and the
+        accumulated statistics, children built from the parents and seeded
+        normal noise, the pool updated in place, then grad2d/count cleared.
+        With views data-parallel the statistics are all-reduced first, and every
+        rank draws the same noise (a generator seeded by the step), so every
+        replica takes identical decisions."""
+        cfg = self.cfg
+        lib = _lib.lib()
+        st = _lib.stream_ptr(self.device)
+        al = self.allocator
+        L = self.layout
+        N = al.num_active
+        if self.pg is not None and self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(al.grad2d, group=self.pg)
+            dist.all_reduce(al.count, group=self.pg)
+        g = self._gaussians(step)
+        flags = torch.empty(max(N, 1), dtype=torch.uint8, device=self.device)
+        f32 = np.float32
+        _lib.check(lib.gs_densify_masks(g, al.grad2d.data_ptr(), al.count.data_ptr(), N, 0.0002,
+                                        float(f32(0.01 * self.scene_scale)), float(f32(0.1 * self.scene_scale)),
+                                        0.005, 5e-2, int(N >= 80000), flags.data_ptr(), st), "densify masks")
+        self.last_densify = {"flags": flags[:N]}
+
+        def make_children(split_slots, refine_rows, n):
+            if noise is not None:
+                nz = noise
+            else:
+                gen = torch.Generator(device=self.device)
+                gen.manual_seed(1_000_003 * int(step) + 17)
+                nz = {"means1": torch.randn((n, 3), generator=gen, device=self.device),
+                      "means2": torch.randn((n, 3), generator=gen, device=self.device),
+                      "quats2": torch.randn((n, 4), generator=gen, device=self.device)}
+            self.last_densify["noise"] = nz
+            c1 = torch.empty((n, L.stride), dtype=torch.float32, device=self.device)
+            c2 = torch.empty_like(c1)
+            o = L.offsets
+            _lib.check(lib.gs_densify_children(al.theta.data_ptr(), L.stride, L.ncols, split_slots.data_ptr(),
+                                               refine_rows.data_ptr(), flags.data_ptr(), nz["means1"].data_ptr(),
+                                               nz["means2"].data_ptr(), nz["quats2"].data_ptr(), n, o["means"],
+                                               o["scales"], o["quats"], o["opacities"], c1.data_ptr(), c2.data_ptr(),
+                                               st), "densify children")
+            return c1, c2
+
+        n_p, n_s = al.apply_flags(flags, make_children)
+        al.grad2d.zero_()
+        al.count.zero_()
+        return n_p, n_s
+
     def loss_value(self, frame=None) -> torch.Tensor:
         f = frame or self.last_frame
         P = f.cam.render_width * f.cam.render_height
@@ -214,6 +265,14 @@ class RunnerMLX:
                 interval = 1000 if cfg.max_steps <= 3000 else 3000
                 if step % interval == 0:
                     self.allocator.reset_opacities(-4.59)
+            if cfg.densify:
+                d0 = 300 if cfg.max_steps <= 3000 else 500
+                d1 = 15000 if cfg.max_steps >= 30000 else int(cfg.max_steps * 0.7)
+                if d0 <= step <= d1 and step % cfg.refine_every == 0:
+                    n_p, n_s = self.densify(step)
+                    if log_every:
+                        print(f"[Step {step:4d} - Densification] Pruned: {n_p} | Split/Duplicated: {n_s} | "
+                              f"Active GS: {self.allocator.num_active}")
             if log_every and (step % log_every == 0 or step == 1):
                 print(f"Step {step:5d} | Active: {self.allocator.num_active} | loss {float(self.loss_value()):.5f}")
         torch.cuda.synchronize(self.device)
@@ -239,7 +298,7 @@ def runner_for_workload(name: str, max_steps: int = 100, num_views: Optional[int
         targets = torch.from_numpy(synthetic.make_uint8_targets(wl, min(len(views), 8), seed=1)).to(dev)
     elif upload_targets and wl.target_kind == "render":
         targets = render_targets(wl, views, K, dev, seed=1, n=n)
-    return RunnerMLX(cfg, g, views, K, targets=targets, device=dev)
+    return RunnerMLX(cfg, g, views, K, targets=targets, device=dev, scene_scale=synthetic.scene_scale(views))
 
 
 def render_targets(wl: synthetic.Workload, views: np.ndarray, K: np.ndarray, device, seed: int = 1,

@@ -1,0 +1,117 @@
+"""Allocator split/prune and the densify step on the GPU, bit-exact against the
+oracle (which is itself pinned to the reference's allocator, see
+tests/test_oracle_golden.py), given identical statistics and noise."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from mlx_gsplat_b200 import PointerStableChunkedAllocator
+from mlx_gsplat_b200.trainer import runner_for_workload
+from oracle import allocator as oalloc
+from oracle import densify as odens
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def snapshot(al) -> oalloc.PoolOracle:
+    o = oalloc.PoolOracle(al.max_gaussians, al.sh_degree)
+    th, m, v = al.theta.cpu().numpy(), al.adam_m.cpu().numpy(), al.adam_v.cpu().numpy()
+    for name, off in al.layout.offsets.items():
+        d = al.layout.dims[name]
+        o.pools[name] = th[:, off:off + d].copy()
+        o.m[name] = m[:, off:off + d].copy()
+        o.v[name] = v[:, off:off + d].copy()
+    o.table = al.indirection_table.cpu().numpy().astype(np.int32)
+    o.free_slots = al.free_slots
+    o.grad2d = al.grad2d.cpu().numpy().copy()
+    o.count = al.count.cpu().numpy().copy()
+    return o
+
+
+def assert_same(al, o: oalloc.PoolOracle, what=""):
+    np.testing.assert_array_equal(al.indirection_table.cpu().numpy(), o.table, err_msg=what + " table")
+    np.testing.assert_array_equal(np.array(al.free_slots, np.int32), o.free_list_array(), err_msg=what + " free list")
+    for name in al.layout.offsets:
+        np.testing.assert_array_equal(al.physical_pools[name].cpu().numpy(), o.pools[name], err_msg=what + " " + name)
+        np.testing.assert_array_equal(al.adam_m_pools[name].cpu().numpy(), o.m[name], err_msg=what + " m " + name)
+        np.testing.assert_array_equal(al.adam_v_pools[name].cpu().numpy(), o.v[name], err_msg=what + " v " + name)
+
+
+def test_allocator_split_and_prune_matches_reference_golden(golden_dir):
+    d = np.load(os.path.join(golden_dir, "allocator.npz"))
+    dims = {"means": 3, "scales": 3, "quats": 4, "opacities": 1, "sh0": 3, "shN": 9}
+    al = PointerStableChunkedAllocator(96, sh_degree=1, device=DEV)
+    al.set_initial_gaussians({k: d["init_" + k] for k in dims})
+    np.testing.assert_array_equal(al.indirection_table.cpu().numpy(), d["table0"])
+    np.testing.assert_array_equal(np.array(al.free_slots), d["free0"])
+    for r in range(3):
+        sp = {k + s: d[f"r{r}_sp_{k}{s}"] for k in dims for s in ("_child1", "_child2")}
+        n_p, n_s = al.split_and_prune(d[f"r{r}_prune"], d[f"r{r}_split"], sp)
+        np.testing.assert_array_equal([n_p, n_s], d[f"r{r}_counts"])
+        np.testing.assert_array_equal(al.indirection_table.cpu().numpy(), d[f"r{r}_table"])
+        np.testing.assert_array_equal(np.array(al.free_slots, np.int32), d[f"r{r}_free"])
+        for k in dims:
+            np.testing.assert_array_equal(al.physical_pools[k].cpu().numpy(), d[f"r{r}_pool_{k}"], err_msg=k)
+            np.testing.assert_array_equal(al.adam_m_pools[k].cpu().numpy(), d[f"r{r}_m_{k}"], err_msg=k)
+    n = al.num_active
+    sp = {k + s: np.zeros((n, dd), np.float32) for k, dd in dims.items() for s in ("_child1", "_child2")}
+    with pytest.raises(MemoryError):
+        al.split_and_prune(np.zeros(n, bool), np.ones(n, bool), sp)
+
+
+@pytest.mark.parametrize("n,geometry", [(20_000, False), (100_000, True)])
+def test_densify_step_matches_oracle(n, geometry):
+    r = runner_for_workload("densify-4m", max_steps=3000, n=n, num_views=4, max_gaussians=3 * n)
+    al = r.allocator
+    for step in range(1, 4):
+        r.train_step(step - 1, step)
+    # statistics and a few rows that exercise every prune rule
+    rng = np.random.default_rng(n)
+    N = al.num_active
+    table = al.indirection_table.cpu().numpy()
+    g2 = al.grad2d.cpu().numpy()
+    g2[table] = rng.exponential(2e-4, N).astype(np.float32) * al.count.cpu().numpy()[table].clip(1)
+    al.grad2d.copy_(torch.from_numpy(g2))
+    L = al.layout
+    th = al.theta.cpu().numpy()
+    pick = table[rng.choice(N, 40, replace=False)]
+    th[pick[:10], L.offsets["opacities"]] = -6.0           # too dim (sigmoid < 0.005)
+    th[pick[10:20], L.offsets["scales"]] = 0.5              # too large
+    th[pick[20:25], L.offsets["means"]] = np.nan            # non-finite
+    th[pick[25:30], L.offsets["quats"]:L.offsets["quats"] + 4] *= 1.5   # |q| far from 1
+    al.theta.copy_(torch.from_numpy(th))
+    torch.cuda.synchronize()
+    o = snapshot(al)
+    noise = {"means1": torch.randn((N, 3), device=DEV), "means2": torch.randn((N, 3), device=DEV),
+             "quats2": torch.randn((N, 4), device=DEV)}
+    n_p, n_s = r.densify(3000, noise=noise)
+    torch.cuda.synchronize()
+    # the oracle on the same snapshot
+    act = {k: o.active(k) for k in o.pools}
+    refine, split, prune = odens.densify_masks(o.grad2d[o.table], o.count[o.table], act["scales"],
+                                               act["opacities"], act["means"], act["quats"], r.scene_scale, N)
+    flags = r.last_densify["flags"].cpu().numpy()
+    np.testing.assert_array_equal((flags & 1) != 0, prune)
+    np.testing.assert_array_equal((flags & 2) != 0, refine)
+    np.testing.assert_array_equal((flags & 4) != 0, split)
+    assert prune.sum() > (5 if not geometry else 20) and refine.sum() > 100
+    ns = int(refine.sum())
+    nz = {k: v[:ns].cpu().numpy() for k, v in noise.items()}
+    sp = odens.child_params(act, refine, split, nz["means1"], nz["means2"], nz["quats2"])
+    exp_p, exp_s = o.split_and_prune(prune, refine, sp)
+    assert (n_p, n_s) == (exp_p, exp_s)
+    assert_same(al, o, "densify")
+    assert float(al.grad2d.abs().sum()) == 0.0
+
+
+def test_densify_out_of_capacity_raises():
+    r = runner_for_workload("densify-4m", max_steps=3000, n=5000, num_views=2, max_gaussians=5100)
+    r.train_step(0, 1)
+    al = r.allocator
+    al.grad2d.fill_(1.0)
+    al.count.fill_(1.0)
+    with pytest.raises(MemoryError):
+        r.densify(3000)
