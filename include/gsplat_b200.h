@@ -159,6 +159,26 @@ int gs_cull(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_p
             float opacity_threshold, int32_t* out_ids, int32_t* out_count, void* scratch,
             size_t scratch_bytes, gs_stream_t stream);
 
+/* gs_cull for callers that cannot allocate device memory — it has no
+ * counterpart in the reference.  Some hosts of this library cannot provide a
+ * scratch buffer: a service binding the C ABI from a managed runtime (Go, JVM,
+ * Node) that has no device allocator of its own, or a process whose device
+ * memory is all owned by another framework's pool.  This entry point allocates
+ * nothing (no cudaMalloc, no cudaFree, no allocating library call): its scratch
+ * is a fixed ~1 MiB array built into the library, which every device that
+ * loads the library keeps until the process exits.  The caller still passes
+ * the inputs and the outputs (out_ids, out_count), exactly as for gs_cull.
+ *  - n may be at most 8,388,608 (2^23) active ids; larger n returns
+ *    GS_ERR_CAPACITY before any work.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array and each call overwrites it: calls that can
+ *    overlap on the GPU (other streams, other host threads on the same device)
+ *    race; serialise them. */
+int gs_cull_noalloc(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_plane, float far_plane,
+                    float opacity_threshold, int32_t* out_ids, int32_t* out_count, gs_stream_t stream);
+
 /* ------------------------------------------------------------------ sort / scan */
 
 /* Stable LSD radix sort of (key, value) uint32 pairs on bits [begin_bit, end_bit).

@@ -71,6 +71,8 @@ _SIGS = {
     "gs_cull_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_cull": (ctypes.c_int, [ctypes.POINTER(GsGaussians), i64, ctypes.POINTER(GsCamera), ctypes.c_float,
                                ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "gs_cull_noalloc": (ctypes.c_int, [ctypes.POINTER(GsGaussians), i64, ctypes.POINTER(GsCamera), ctypes.c_float,
+                                       ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp]),
     "gs_radix_sort_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_radix_sort_pairs": (ctypes.c_int, [c_vp] * 4 + [i64, ctypes.c_int, ctypes.c_int, c_vp, ctypes.c_size_t, c_vp]),
     "gs_scan_scratch_bytes": (ctypes.c_size_t, [i64]),

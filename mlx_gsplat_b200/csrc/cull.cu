@@ -5,6 +5,8 @@
 // Pass 2: exclusive scan of the chunk counts.
 // Pass 3: each chunk writes its surviving ids in ascending order.
 // Reads 16 bytes per id (means + opacity), writes 4 bytes per survivor.
+#include <mutex>
+
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -207,7 +209,61 @@ int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, 
     return check_launch("compact count copy", 0);
 }
 
+// ---------------------------------------------------------------- cull without caller scratch
+// gs_cull_noalloc keeps its scratch (mask words, chunk counts, scan partials)
+// in the file-scope device array below instead of a caller buffer.  It is
+// sized for kNoAllocMaxRows active ids; every device that loads the library
+// holds it until the process exits.  Host code never dereferences the array's
+// name: the device address is taken once per device with
+// cudaGetSymbolAddress.  Each call writes every scratch word before reading
+// it, so nothing has to be cleared between calls.
+constexpr int64_t kNoAllocMaxRows = int64_t(1) << 23;  // 8,388,608 active ids
+constexpr size_t cx_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
+constexpr int64_t kNoAllocChunks = (kNoAllocMaxRows + kCullChunk - 1) / kCullChunk;
+constexpr int64_t kNoAllocScanTiles = (kNoAllocChunks + 2047) / 2048;
+constexpr size_t kNoAllocScratchBytes = cx_align((size_t)((kNoAllocMaxRows + 31) / 32 + 1) * 4, 256) +
+                                        cx_align((size_t)(kNoAllocChunks + 1) * 4, 256) +
+                                        cx_align((size_t)(kNoAllocScanTiles + 4) * 4 + 256, 256) + 256;
+
+static __device__ __align__(256) unsigned char g_cull_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_cull_scratch on the current device (looked up on first use).
+static int noalloc_scratch(void** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "cull_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    GS_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "cull_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_cull_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return set_error(GS_ERR_CUDA, "cull_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return GS_OK;
+}
+
 }  // namespace gs
+
+extern "C" int gs_cull_noalloc(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_plane,
+                               float far_plane, float opacity_threshold, int32_t* out_ids, int32_t* out_count,
+                               gs_stream_t stream) {
+    GS_REQUIRE(g && cam, "cull_noalloc: null descriptor");
+    if (n > gs::kNoAllocMaxRows)
+        return gs::set_error(GS_ERR_CAPACITY, "cull_noalloc: %lld active ids exceed the built-in limit of %lld",
+                             (long long)n, (long long)gs::kNoAllocMaxRows);
+    GS_REQUIRE(gs::cull_scratch_bytes(n) <= gs::kNoAllocScratchBytes, "cull_noalloc: scratch sizing mismatch");
+    void* scratch = nullptr;
+    GS_TRY(gs::noalloc_scratch(&scratch));
+    return gs::cull(*g, n, *cam, near_plane, far_plane, opacity_threshold, out_ids, out_count, scratch,
+                    gs::kNoAllocScratchBytes, (cudaStream_t)stream);
+}
 
 extern "C" size_t gs_cull_scratch_bytes(int64_t n) { return gs::cull_scratch_bytes(n); }
 
