@@ -54,13 +54,15 @@ def metric_name(workload: str) -> str:
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="outdoor-1m")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
+    ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
     return ap.parse_args()
 
 
@@ -99,7 +101,7 @@ def barrier(world):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -113,12 +115,14 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0: float = None, t1: float = None):
+        """Median SM clock and the active throttle reasons over the samples taken
+        between host times t0 and t1 (the timed region)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -127,22 +131,29 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        sm, smax, reasons = [], None, set()
+        import datetime
+        sm, smax, reasons, power = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                mhz = float(parts[2])
+                smax = float(parts[3])
+                pw = float(parts[4])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            if t0 is not None and not (t0 - 0.06 <= ts <= t1 + 0.06):
+                continue
+            sm.append(mhz)
+            power.append(pw)
+            for n, v in zip(names, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_median": float(np.median(power)) if power else None}
 
 
 # ----------------------------------------------------------------------------- byte model
@@ -242,11 +253,11 @@ def main():
 
     dev = torch.device("cuda", local)
     wl = synthetic.WORKLOADS[args.workload]
+    nv = args.views or wl.num_views
     runner = runner_for_workload(args.workload, max_steps=10_000, device=dev, upload_targets=False, lr=1.6e-4,
-                                 eps=1e-15)
+                                 eps=1e-15, n=args.gaussians, num_views=nv)
     runner.pg = pg
     runner.world = world
-    nv = wl.num_views
     targets_host = torch.from_numpy(synthetic.make_uint8_targets(wl, nv, seed=1)).pin_memory()
     targets_dev = targets_host.to(dev)
     L = runner.layout
@@ -256,6 +267,8 @@ def main():
     def view_of(step):
         return (rank + world * step) % nv
 
+    clocks = ClockSampler(local)
+    clocks.start()
     step = 0
     for _ in range(args.warmup):
         step += 1
@@ -265,14 +278,13 @@ def main():
     # ---- timed region: inputs resident in HBM
     lib = _lib.load()
     launches0 = lib.gs_kernel_launches()
-    clocks = ClockSampler(local)
-    clocks.start()
     timers = []
     stats = []
     barrier(world)
     torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    t_start = time.time()
     e0.record()
     for _ in range(args.steps):
         step += 1
@@ -282,8 +294,9 @@ def main():
         stats.append((f.V, f.K))
     e1.record()
     torch.cuda.synchronize(dev)
+    t_end = time.time()
     barrier(world)
-    clk = clocks.stop()
+    clk = clocks.stop(t_start, t_end)
     launches = lib.gs_kernel_launches() - launches0
     ms = e0.elapsed_time(e1) / args.steps
     ms_max = max_over_ranks(ms, world)
