@@ -68,12 +68,19 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
 // items own one row (the smallest power of two >= the row's chunk count).
 // Each thread takes two items, ``half`` apart, and issues all eight 16-byte
 // loads before any arithmetic so that more bytes are in flight per thread.
+// Per-column constants live in shared memory: indexing the kernel-parameter
+// copy with a lane-dependent column made every access a divergent constant
+// load (serialised in the address-divergence unit).
+struct ColsSmem {
+    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols];
+};
+
 __device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, const float4& gg, int c0, int ncols,
-                                            bool renorm, const AdamScalars& s, const SlabCols& cols) {
-    if (c0 + 0 < ncols) adam_elem(th.x, mm.x, vv.x, gg.x, s, cols.step_size[c0 + 0], cols.lo[c0 + 0], cols.hi[c0 + 0]);
-    if (c0 + 1 < ncols) adam_elem(th.y, mm.y, vv.y, gg.y, s, cols.step_size[c0 + 1], cols.lo[c0 + 1], cols.hi[c0 + 1]);
-    if (c0 + 2 < ncols) adam_elem(th.z, mm.z, vv.z, gg.z, s, cols.step_size[c0 + 2], cols.lo[c0 + 2], cols.hi[c0 + 2]);
-    if (c0 + 3 < ncols) adam_elem(th.w, mm.w, vv.w, gg.w, s, cols.step_size[c0 + 3], cols.lo[c0 + 3], cols.hi[c0 + 3]);
+                                            bool renorm, const AdamScalars& s, const ColsSmem& cs) {
+    if (c0 + 0 < ncols) adam_elem(th.x, mm.x, vv.x, gg.x, s, cs.step[c0 + 0], cs.lo[c0 + 0], cs.hi[c0 + 0]);
+    if (c0 + 1 < ncols) adam_elem(th.y, mm.y, vv.y, gg.y, s, cs.step[c0 + 1], cs.lo[c0 + 1], cs.hi[c0 + 1]);
+    if (c0 + 2 < ncols) adam_elem(th.z, mm.z, vv.z, gg.z, s, cs.step[c0 + 2], cs.lo[c0 + 2], cs.hi[c0 + 2]);
+    if (c0 + 3 < ncols) adam_elem(th.w, mm.w, vv.w, gg.w, s, cs.step[c0 + 3], cs.lo[c0 + 3], cs.hi[c0 + 3]);
     if (renorm) {
         float ss = __fmul_rn(th.x, th.x);
         ss = __fadd_rn(ss, __fmul_rn(th.y, th.y));
@@ -92,6 +99,13 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
                                                         int lane_shift, int g_chunks, int ncols, int quat_chunk,
                                                         int64_t half, AdamScalars s, SlabCols cols) {
+    __shared__ ColsSmem cs;
+    if (threadIdx.x < kMaxSlabCols) {
+        cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
+        cs.lo[threadIdx.x] = cols.lo[threadIdx.x];
+        cs.hi[threadIdx.x] = cols.hi[threadIdx.x];
+    }
+    __syncthreads();
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int mask = (1 << lane_shift) - 1;
     const int c4 = (int)(t0 & mask);  // half is a multiple of 2^lane_shift: both items share the chunk
@@ -116,13 +130,13 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
     }
     const bool renorm = c4 == quat_chunk;
     if (va) {
-        slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cols);
+        slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
         theta[offa] = tha;
         m[offa] = ma;
         v[offa] = vva;
     }
     if (vb) {
-        slab_update(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cols);
+        slab_update(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cs);
         theta[offb] = thb;
         m[offb] = mb;
         v[offb] = vvb;

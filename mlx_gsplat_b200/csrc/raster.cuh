@@ -219,6 +219,37 @@ __device__ __forceinline__ float quad_form(float ca, float s, float cd, float x,
     return ca * x * x + 2.0f * s * x * y + cd * y * y;
 }
 
+// Minimum of the positive-definite form ca x^2 + 2 s x y + cd y^2 over the
+// rectangle [x0, x1] x [y0, y1] (offsets from the splat centre): zero when the
+// centre is inside, otherwise the smallest of the four edge minima.
+__device__ __forceinline__ float rect_min_quad(float ca, float s, float cd, float x0, float x1, float y0, float y1) {
+    if (x0 <= 0.f && 0.f <= x1 && y0 <= 0.f && 0.f <= y1) return 0.f;
+    float best = 3.4e38f;
+    const float ya = fminf(fmaxf(-s * x0 / cd, y0), y1);
+    best = fminf(best, quad_form(ca, s, cd, x0, ya));
+    const float yb = fminf(fmaxf(-s * x1 / cd, y0), y1);
+    best = fminf(best, quad_form(ca, s, cd, x1, yb));
+    const float xa = fminf(fmaxf(-s * y0 / ca, x0), x1);
+    best = fminf(best, quad_form(ca, s, cd, xa, y0));
+    const float xb = fminf(fmaxf(-s * y1 / ca, x0), x1);
+    best = fminf(best, quad_form(ca, s, cd, xb, y1));
+    return best;
+}
+
+// Can a staged splat (records q0, q1 and its pair cut) reach any pixel centre
+// of the rectangle of pixels [pi0, pi1] x [pj0, pj1]?  Conservative (continuous
+// rectangle, relative slack); a conic that is not positive definite passes.
+// The compositing kernels use it to skip splats that miss a warp's pixel block.
+__device__ __forceinline__ bool splat_hits_block(float4 q0, float4 q1, float cut, int pi0, int pi1, int pj0, int pj1,
+                                                 const RasterParams& p) {
+    if (!(cut >= 0.f)) return false;
+    const float ca = q0.z, cd = q1.y, s = 0.5f * (q0.w + q1.x);
+    if (!(ca > 0.f && cd > 0.f && ca * cd - s * s > 0.f)) return true;
+    const float x0 = (float)pi0 * p.sx + p.hsx - q0.x, x1 = (float)pi1 * p.sx + p.hsx - q0.x;
+    const float y0 = (float)pj0 * p.sy + p.hsy - q0.y, y1 = (float)pj1 * p.sy + p.hsy - q0.y;
+    return rect_min_quad(ca, s, cd, x0, x1, y0, y1) <= cut * 1.0002f + 1e-3f;
+}
+
 // Minimum of the (positive definite) quadratic form over the tile's pixel-centre rectangle.
 __device__ __forceinline__ bool splat_hits_tile(float u, float v, float ca, float cd, const TileBox& tb, int tx,
                                                 int ty, const RasterParams& p) {

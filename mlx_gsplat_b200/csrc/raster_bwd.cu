@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
     const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
     const float px = (float)pi * p.sx + p.hsx;
     const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
+    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * 8;  // this warp's 8x8 block
     const gs_tile_range rg = ranges[tile];
     for (int j = threadIdx.x; j < kBatch; j += kRenderThreads)
 #pragma unroll
@@ -138,7 +139,21 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             s2[j] = splats[3 * vi + 2];
         }
         __syncthreads();
-        for (int k = cnt - 1; k >= 0; --k) {
+        // which staged splats can reach this warp's 8x8 pixel block (same test as the forward)
+        unsigned hits[kBatch / 32];
+#pragma unroll
+        for (int i = 0; i < kBatch / 32; ++i) {
+            const int k = 32 * i + lane;
+            const bool h = k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + 7, p);
+            hits[i] = __ballot_sync(kFull, h);
+        }
+#pragma unroll
+        for (int i = kBatch / 32 - 1; i >= 0; --i) {
+          unsigned bits = hits[i];
+          while (bits) {
+            const int hb = 31 - __clz(bits);
+            bits &= ~(1u << hb);
+            const int k = 32 * i + hb;
             const int idx = bstart + k - rg.start;
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
             const float x = px - q0.x;
@@ -158,6 +173,7 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const float t9 = warp_sum(g[8]);
             if ((lane & 3) == 0) atomicAdd(&acc[k][lane >> 2], t8);
             if (lane == 0) atomicAdd(&acc[k][8], t9);
+          }
         }
         __syncthreads();
         // one global vector reduction per (tile, splat) with a non-zero gradient

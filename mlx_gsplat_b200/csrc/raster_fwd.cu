@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
     const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
     const float px = (float)pi * p.sx + p.hsx;
     const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
+    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * 8;  // this warp's 8x8 block
     const gs_tile_range rg = ranges[tile];
 
     float T0 = 1.f, r0 = 0.f, g0 = 0.f, b0 = 0.f, A0 = 0.f;
@@ -240,16 +241,32 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
         __syncthreads();
         const int cnt = min(kBatch, rg.end - b);
         const int base1 = b - rg.start + 1;
-        for (int k = 0; k < cnt; ++k) {
-            if (__all_sync(kFull, done0 && done1)) break;
-            const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-            const float x = px - q0.x;
-            const float ax = q0.z * x, cx = q1.x * x;
-            const float y0 = py0 - q0.y, y1 = py1 - q0.y;
-            const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
-            const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
-            composite_pixel(m0, q1, q2, T0, r0, g0, b0, A0, last0, done0, base1 + k, p.t_min);
-            composite_pixel(m1, q1, q2, T1, r1, g1, b1, A1, last1, done1, base1 + k, p.t_min);
+        // which staged splats can reach this warp's 8x8 pixel block at all
+        bool warp_done = __all_sync(kFull, done0 && done1);
+        unsigned hits[kBatch / 32];
+#pragma unroll
+        for (int i = 0; i < kBatch / 32; ++i) {
+            const int k = 32 * i + lane;
+            const bool h = !warp_done && k < cnt &&
+                           splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + 7, p);
+            hits[i] = __ballot_sync(kFull, h);
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch / 32; ++i) {
+            unsigned bits = hits[i];
+            while (bits && !warp_done) {
+                const int k = 32 * i + __ffs(bits) - 1;
+                bits &= bits - 1;
+                const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
+                const float x = px - q0.x;
+                const float ax = q0.z * x, cx = q1.x * x;
+                const float y0 = py0 - q0.y, y1 = py1 - q0.y;
+                const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
+                const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
+                composite_pixel(m0, q1, q2, T0, r0, g0, b0, A0, last0, done0, base1 + k, p.t_min);
+                composite_pixel(m1, q1, q2, T1, r1, g1, b1, A1, last1, done1, base1 + k, p.t_min);
+                warp_done = __all_sync(kFull, done0 && done1);
+            }
         }
         __syncthreads();
     }
