@@ -163,6 +163,25 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     for (int k = 0; k < 3; ++k) s.rgb[k] = fminf(fmaxf(s.pre[k], 0.0f), 1.0f);
 }
 
+// ------------------------------------------------------------------ splat falloff
+// g = exp(-m / 2) evaluated as 2^(m * (-log2(e) / 2)) with the hardware base-2
+// exponential (ex2.approx, relative error ~2^-22).  Forward and backward call
+// this one function, so both see bit-identical alphas.
+constexpr float kHalfNegLog2e = -0.72134752044448170368f;  // -log2(e) / 2
+
+__device__ __forceinline__ float splat_falloff(float m) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(m * kHalfNegLog2e));
+    return y;
+}
+
+// Hardware reciprocal (rcp.approx, about 1 ulp).
+__device__ __forceinline__ float fast_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ------------------------------------------------------------------ per-pixel contribution rule
 // A (pixel, splat) pair contributes iff its Mahalanobis distance m satisfies
 // m <= 2 ln(opacity / alpha_cutoff), i.e. alpha = opacity * exp(-m/2) >=

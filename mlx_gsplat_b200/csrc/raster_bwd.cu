@@ -61,33 +61,42 @@ __device__ __forceinline__ void pixel_bwd_init(PixelBwd& s, bool inside, int64_t
     }
 }
 
-// Adds one pixel's contribution of one splat to the nine running sums.
-// ``a2 = 2 conic_a``, ``sbc = conic_b + conic_c``, ``d2 = 2 conic_d`` are per splat.
-__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, float x, float y, float m, float opac, float4 q1,
-                                               float4 q2, float a2, float sbc, float d2, float* g) {
-    const float gv = __expf(-0.5f * m);
-    const float og = opac * gv;
-    const float al = fminf(og, 0.99f);
-    s.T = __fdividef(s.T, 1.f - al);
-    const float val = s.dr * q1.w + s.dg * q2.x + s.db * q2.y + s.dA;
+// Per-splat constants of the backward step: the splat's colour, its opacity,
+// -opacity / 2 (for dL/dm), and -2 conic_a, -(conic_b + conic_c), -2 conic_d
+// (for dL/du, dL/dv).
+struct SplatBwd {
+    float r, g, b, opac, hop, na2, nsbc, nd2;
+};
+
+// Adds one pixel's contribution of one splat to the nine running sums, or
+// nothing when ``valid`` is false.  Branch-free: both pixels of a thread are
+// evaluated whenever any lane of the warp is active, so the work is selected
+// with masks instead of branches (an invalid pixel gets alpha = 0, which
+// leaves T and B unchanged and zeroes every term).
+__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, bool valid, float x, float y, float m,
+                                               const SplatBwd& c, float* g) {
+    const float gv = splat_falloff(m);
+    const float og = c.opac * gv;
+    const float al = valid ? fminf(og, 0.99f) : 0.f;
+    s.T *= fast_rcp(1.f - al);  // T_i = T_{i+1} / (1 - alpha_i), 1 - alpha_i >= 0.01
+    const float val = fmaf(s.dr, c.r, fmaf(s.dg, c.g, fmaf(s.db, c.b, s.dA)));
     const float d = val - s.Bv;
-    const float dal = s.T * d;
-    s.Bv += al * d;  // = al * val + (1 - al) * B
+    s.Bv = fmaf(al, d, s.Bv);  // = al * val + (1 - al) * B
     const float wT = al * s.T;
-    g[6] += wT * s.dr;
-    g[7] += wT * s.dg;
-    g[8] += wT * s.db;
-    if (og > 0.f && og < 0.99f) {
-        const float dog = dal * gv;
-        g[5] += dog;                            // d opacity
-        const float dm = -0.5f * opac * dog;    // dL/dm
-        const float dmx = dm * x, dmy = dm * y;
-        g[0] -= a2 * dmx + sbc * dmy;           // d u
-        g[1] -= sbc * dmx + d2 * dmy;           // d v
-        g[2] += dmx * x;                        // d conic a
-        g[3] += dmx * y;                        // d conic b (= d conic c)
-        g[4] += dmy * y;                        // d conic d
-    }
+    g[6] = fmaf(wT, s.dr, g[6]);
+    g[7] = fmaf(wT, s.dg, g[7]);
+    g[8] = fmaf(wT, s.db, g[8]);
+    // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
+    const bool inside = valid && og > 0.f && og < 0.99f;
+    const float dog = inside ? s.T * d * gv : 0.f;  // dL/dalpha * g
+    g[5] += dog;                                    // d opacity
+    const float dm = c.hop * dog;                   // dL/dm
+    const float dmx = dm * x, dmy = dm * y;
+    g[0] = fmaf(c.na2, dmx, fmaf(c.nsbc, dmy, g[0]));  // d u
+    g[1] = fmaf(c.nsbc, dmx, fmaf(c.nd2, dmy, g[1]));  // d v
+    g[2] = fmaf(dmx, x, g[2]);                         // d conic a
+    g[3] = fmaf(dmx, y, g[3]);                         // d conic b (= d conic c)
+    g[4] = fmaf(dmy, y, g[4]);                         // d conic d
 }
 
 __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
@@ -165,9 +174,17 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const bool v1 = idx < b.last && m1 <= q2.z;
             if (!__any_sync(kFull, v0 || v1)) continue;
             float g[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            const float a2 = 2.f * q0.z, sbc = q0.w + q1.x, d2 = 2.f * q1.y;
-            if (v0) pixel_bwd_step(a, x, y0, m0, q1.z, q1, q2, a2, sbc, d2, g);
-            if (v1) pixel_bwd_step(b, x, y1, m1, q1.z, q1, q2, a2, sbc, d2, g);
+            SplatBwd c;
+            c.r = q1.w;
+            c.g = q2.x;
+            c.b = q2.y;
+            c.opac = q1.z;
+            c.hop = -0.5f * q1.z;
+            c.na2 = -2.f * q0.z;
+            c.nsbc = -(q0.w + q1.x);
+            c.nd2 = -2.f * q1.y;
+            pixel_bwd_step(a, v0, x, y0, m0, c, g);
+            pixel_bwd_step(b, v1, x, y1, m1, c, g);
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
             const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
             const float t9 = warp_sum(g[8]);

@@ -173,7 +173,7 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
 __device__ __forceinline__ void composite_pixel(float m, float4 q1, float4 q2, float& T, float& cr, float& cg,
                                                 float& cb, float& A, int& last, bool& done, int idx1, float t_min) {
     if (!done && m <= q2.z) {
-        const float gv = __expf(-0.5f * m);
+        const float gv = splat_falloff(m);
         const float al = fminf(q1.z * gv, 0.99f);
         const float w = al * T;
         cr += w * q1.w;
