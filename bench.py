@@ -68,19 +68,9 @@ def parse():
 
 # ----------------------------------------------------------------------------- distributed
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-        pg = dist.group.WORLD
-    else:
-        torch.cuda.set_device(local)
+    from mlx_gsplat_b200 import distributed as D
+    rank, world, local, pg = D.init_from_env("nccl", timeout_s=180.0)
+    torch.cuda.set_device(local)
     return world, rank, local, pg
 
 

@@ -27,7 +27,7 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 import torch
 
-from . import _lib, synthetic
+from . import _lib, distributed, synthetic
 from .allocator import PointerStableChunkedAllocator
 from .optimizer import FusedMLXAdam
 from .rendering import (DEFAULT_SETTINGS, RasterSettings, camera_struct, cull_ids, gaussians_struct, grads_struct,
@@ -119,10 +119,7 @@ class RunnerMLX:
         self.settings = RasterSettings(cfg.alpha_cutoff, cfg.transmittance_min)
         self.scene_scale = scene_scale
         self.pg = process_group
-        self.world = 1
-        if process_group is not None:
-            import torch.distributed as dist
-            self.world = dist.get_world_size(process_group)
+        self.world = distributed.world_of(process_group)
         self.last_frame = None
         self.step_count = 0
 
@@ -183,10 +180,8 @@ class RunnerMLX:
         render_backward(frame, g, self._grad_out(step), self.device, grad2d=self.allocator.grad2d,
                         count=self.allocator.count, timer=timer)
         scale = 1.0
-        if self.pg is not None and self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(self.grad[:N], group=self.pg)
-            scale = 1.0 / self.world
+        if self.world > 1:
+            scale = distributed.reduce_gradient_rows(self.grad[:N], self.pg)
             if timer:
                 timer.mark("allreduce")
         self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
@@ -212,10 +207,7 @@ class RunnerMLX:
         al = self.allocator
         L = self.layout
         N = al.num_active
-        if self.pg is not None and self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(al.grad2d, group=self.pg)
-            dist.all_reduce(al.count, group=self.pg)
+        distributed.reduce_densify_stats(al.grad2d, al.count, self.pg)
         g = self._gaussians(step)
         flags = torch.empty(max(N, 1), dtype=torch.uint8, device=self.device)
         f32 = np.float32
@@ -225,14 +217,7 @@ class RunnerMLX:
         self.last_densify = {"flags": flags[:N]}
 
         def make_children(split_slots, refine_rows, n):
-            if noise is not None:
-                nz = noise
-            else:
-                gen = torch.Generator(device=self.device)
-                gen.manual_seed(1_000_003 * int(step) + 17)
-                nz = {"means1": torch.randn((n, 3), generator=gen, device=self.device),
-                      "means2": torch.randn((n, 3), generator=gen, device=self.device),
-                      "quats2": torch.randn((n, 4), generator=gen, device=self.device)}
+            nz = noise if noise is not None else distributed.densify_noise(step, n, self.device)
             self.last_densify["noise"] = nz
             c1 = torch.empty((n, L.stride), dtype=torch.float32, device=self.device)
             c2 = torch.empty_like(c1)

@@ -1,0 +1,176 @@
+"""Views data-parallel host logic with 2 gloo ranks on the CPU: the gradient
+all-reduce and its 1/world scale, the view assignment, identical densify noise
+on every rank, the statistics reduction, and — with the CPU oracle standing in
+for the per-view GPU computation — that a data-parallel Adam step equals the
+single-process step on the mean gradient and leaves the replicas identical."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(fn, world=2):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_entry, args=(fn, r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        r, ok, payload = q.get(timeout=240)
+        results[r] = (ok, payload)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        ok, payload = results[r]
+        assert ok, f"rank {r}: {payload}"
+    return [results[r][1] for r in range(world)]
+
+
+def _entry(fn, rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    try:
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        out = fn(rank, world)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, True, out))
+    except Exception as e:  # report, never hang the parent
+        import traceback
+        q.put((rank, False, traceback.format_exc()))
+
+
+def _reduce_views_noise(rank, world):
+    from mlx_gsplat_b200 import distributed as D
+    pg = dist.group.WORLD
+    g = torch.from_numpy(np.random.default_rng(rank).normal(0, 1, (100, 60)).astype(np.float32))
+    mine = g.clone()
+    scale = D.reduce_gradient_rows(g, pg)
+    views = [D.view_for(7, r, world, 160) for r in range(world)]
+    noise = D.densify_noise(300, 50, "cpu")
+    g2 = torch.full((10,), float(rank + 1))
+    c2 = torch.ones(10)
+    D.reduce_densify_stats(g2, c2, pg)
+    return {"sum": g.numpy(), "mine": mine.numpy(), "scale": scale, "views": views,
+            "noise": {k: v.numpy() for k, v in noise.items()}, "g2": g2.numpy(), "c2": c2.numpy()}
+
+
+def test_gradient_reduction_views_and_noise():
+    a, b = _run(_reduce_views_noise)
+    np.testing.assert_allclose(a["sum"], a["mine"] + b["mine"], rtol=1e-6)
+    np.testing.assert_array_equal(a["sum"], b["sum"])
+    assert a["scale"] == b["scale"] == 0.5
+    assert len(set(a["views"])) == 2 and a["views"] == b["views"]
+    for k in a["noise"]:
+        np.testing.assert_array_equal(a["noise"][k], b["noise"][k])
+    np.testing.assert_array_equal(a["g2"], np.full(10, 3.0, np.float32))
+    np.testing.assert_array_equal(a["c2"], np.full(10, 2.0, np.float32))
+
+
+def _scene():
+    from mlx_gsplat_b200 import synthetic
+    wl = synthetic.WORKLOADS["tiny-3k"]
+    g = synthetic.make_gaussians(wl, seed=3, n=40)
+    views, _ = synthetic.make_cameras(wl, seed=2, num_views=4)
+    K = np.array([[30.0, 0, 16.0], [0, 30.0, 12.0], [0, 0, 1]], np.float32)
+    return g, views, K
+
+
+def _view_grads(g, vm, K):
+    """Per-view gradient rows [N, 14] (quats, means, opacity, scales, sh0) from the oracle."""
+    from oracle import rendering as orend
+    ids = orend.cull(g["means"], g["opacities"], vm, K, 32, 24).astype(np.int64)
+    C, _ = orend.rasterize_dense(g["means"][ids], g["quats"][ids], g["scales"][ids], g["opacities"][ids],
+                                 g["sh0"][ids], vm, K, 32, 24, 32, 24)
+    dC = np.full_like(C, 1.0 / (3 * 32 * 24))
+    _, _, gr = orend.rasterize_dense_vjp(g["means"][ids], g["quats"][ids], g["scales"][ids], g["opacities"][ids],
+                                         g["sh0"][ids], vm, K, 32, 24, 32, 24, dL_dC=dC)
+    rows = np.zeros((g["means"].shape[0], 14), np.float32)
+    for name, off, d in (("quats", 0, 4), ("means", 4, 3), ("opacities", 7, 1), ("scales", 8, 3)):
+        rows[ids, off:off + d] = gr[name]
+    rows[ids, 11:14] = gr["colors"]
+    return rows
+
+
+def _adam_rows(theta, g, scale):
+    from oracle import adam as oadam
+    th = theta.copy()
+    m = np.zeros_like(th)
+    v = np.zeros_like(th)
+    gg = (g * np.float32(scale)).astype(np.float32)
+    oadam.fused_adam_a1(th, gg, m, v, np.arange(th.shape[0], dtype=np.int32), 1e-3, 0.9, 0.999, 1e-15, 0.0, 1,
+                        -1e10, 1e10)
+    return th
+
+
+def _dp_step(rank, world):
+    from mlx_gsplat_b200 import distributed as D
+    g, views, K = _scene()
+    v = D.view_for(0, rank, world, len(views))
+    rows = torch.from_numpy(_view_grads(g, views[v], K))
+    scale = D.reduce_gradient_rows(rows, dist.group.WORLD)
+    theta = np.concatenate([g["quats"], g["means"], g["opacities"], g["scales"], g["sh0"]], 1).astype(np.float32)
+    return {"theta": _adam_rows(theta, rows.numpy(), scale), "view": v}
+
+
+def test_data_parallel_step_equals_mean_gradient_step():
+    a, b = _run(_dp_step)
+    np.testing.assert_array_equal(a["theta"], b["theta"])  # replicas stay identical
+    g, views, K = _scene()
+    total = _view_grads(g, views[a["view"]], K) + _view_grads(g, views[b["view"]], K)
+    theta = np.concatenate([g["quats"], g["means"], g["opacities"], g["scales"], g["sh0"]], 1).astype(np.float32)
+    ref = _adam_rows(theta, total, 0.5)
+    np.testing.assert_allclose(a["theta"], ref, rtol=1e-6, atol=1e-7)
+
+
+def _rank_failure(rank, world):
+    """A rank that raises before the collective: the other rank's collective
+    must end with an error inside the process-group timeout, not hang."""
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    from mlx_gsplat_b200 import distributed as D
+    t = torch.ones(4)
+    try:
+        D.reduce_gradient_rows(t, dist.group.WORLD)
+    except Exception:
+        return "collective failed as expected"
+    return "collective returned"
+
+
+def test_rank_failure_surfaces_as_error():
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_entry, args=(_rank_failure, r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, ok, payload = q.get(timeout=240)
+        got[r] = (ok, payload)
+    for p in procs:
+        p.join(timeout=90)
+        if p.is_alive():
+            p.kill()
+    assert got[1][0] is False and "injected failure" in got[1][1]
+    # rank 0 either saw its collective fail or failed at the final barrier; it did not hang
+    assert got[0][0] is False or got[0][1] == "collective failed as expected"
