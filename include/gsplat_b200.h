@@ -138,12 +138,17 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
  * Per column: clamp bounds ``col_lo/col_hi`` and ``col_lr_scale`` (host arrays
  * of ncols, ncols <= 64).  When ``quat_col >= 0`` (a multiple of 4) the four
  * columns from quat_col are renormalised after the update,
- * q / sqrt(sum q^2 + 1e-8) (mlx_gsplat/trainer.py:380-387). */
+ * q / sqrt(sum q^2 + 1e-8) (mlx_gsplat/trainer.py:380-387).
+ * When ``visible_words`` is given (bit r of word r/32 set = row r was seen
+ * this step, the bitmask gs_cull leaves in its scratch), a row whose bit is
+ * clear does not read g: its gradient is the host row ``unseen_grad_host``
+ * (ncols floats), so the caller needs no gradient rows for unseen Gaussians. */
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                        double lr, double beta1, double beta2, float eps, float weight_decay, int step,
-                       float grad_scale, int mode, gs_stream_t stream);
+                       float grad_scale, int mode, const uint32_t* visible_words, const float* unseen_grad_host,
+                       gs_stream_t stream);
 
 /* ------------------------------------------------------------------ cull */
 
@@ -151,7 +156,9 @@ int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const i
  * active ids i in [0, n) that pass  z > near, z < far, the 50 px tolerance
  * box around the image and logit >= opacity_threshold (skipped when
  * g->opac is NULL) into ``out_ids`` and their number into ``*out_count``
- * (device int32).  Camera-space z and the projected centre are computed in
+ * (device int32).  On return the scratch starts (at its first 256-byte
+ * boundary) with the visibility bitmask: bit i of 32-bit word i/32 is set when
+ * id i passed.  Camera-space z and the projected centre are computed in
  * float32 with every product and sum rounded separately, left to right.
  * Scratch: ``gs_cull_scratch_bytes(n)`` bytes at ``scratch`` (16-byte aligned). */
 size_t gs_cull_scratch_bytes(int64_t n);

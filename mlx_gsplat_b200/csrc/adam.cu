@@ -24,6 +24,7 @@ struct SlabCols {
     float step_size[kMaxSlabCols];
     float lo[kMaxSlabCols];
     float hi[kMaxSlabCols];
+    float gdef[kMaxSlabCols];  // gradient of a row the visibility bits mark unseen
 };
 
 __device__ __forceinline__ void adam_elem(float& th, float& m, float& v, float g, const AdamScalars& s,
@@ -72,7 +73,7 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
 // copy with a lane-dependent column made every access a divergent constant
 // load (serialised in the address-divergence unit).
 struct ColsSmem {
-    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols];
+    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols];
 };
 
 __device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, const float4& gg, int c0, int ncols,
@@ -98,12 +99,14 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
                                                         float4* __restrict__ m, float4* __restrict__ v,
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
                                                         int lane_shift, int g_chunks, int ncols, int quat_chunk,
-                                                        int64_t half, AdamScalars s, SlabCols cols) {
+                                                        int64_t half, const uint32_t* __restrict__ vis,
+                                                        AdamScalars s, SlabCols cols) {
     __shared__ ColsSmem cs;
     if (threadIdx.x < kMaxSlabCols) {
         cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
         cs.lo[threadIdx.x] = cols.lo[threadIdx.x];
         cs.hi[threadIdx.x] = cols.hi[threadIdx.x];
+        cs.gdef[threadIdx.x] = cols.gdef[threadIdx.x];
     }
     __syncthreads();
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -119,14 +122,20 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         tha = theta[offa];
         ma = m[offa];
         vva = v[offa];
-        ga = __ldg(g + ra * g_chunks + c4);
+        if (vis && !((__ldg(vis + (ra >> 5)) >> (ra & 31)) & 1u))
+            ga = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
+        else
+            ga = __ldg(g + ra * g_chunks + c4);
     }
     if (vb) {
         offb = (int64_t)__ldg(idx + rb) * chunks + c4;
         thb = theta[offb];
         mb = m[offb];
         vvb = v[offb];
-        gb = __ldg(g + rb * g_chunks + c4);
+        if (vis && !((__ldg(vis + (rb >> 5)) >> (rb & 31)) & 1u))
+            gb = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
+        else
+            gb = __ldg(g + rb * g_chunks + c4);
     }
     const bool renorm = c4 == quat_chunk;
     if (va) {
@@ -211,8 +220,10 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                                   const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                                   double lr, double beta1, double beta2, float eps, float weight_decay, int step,
-                                  float grad_scale, int mode, gs_stream_t stream) {
+                                  float grad_scale, int mode, const uint32_t* visible_words,
+                                  const float* unseen_grad_host, gs_stream_t stream) {
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
+    GS_REQUIRE(!visible_words || unseen_grad_host, "adam_slab: visible_words needs unseen_grad_host");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
     GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && g_stride >= ncols,
                "adam_slab: strides must be multiples of 4 and >= ncols");
@@ -229,6 +240,7 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         cols.lo[c] = on ? col_lo[c] : 0.f;
         cols.hi[c] = on ? col_hi[c] : 0.f;
         cols.step_size[c] = on ? step_size_for(mode, lr, col_lr_scale ? col_lr_scale[c] : 1.0f, bc1) : 0.f;
+        cols.gdef[c] = (on && unseen_grad_host) ? unseen_grad_host[c] : 0.f;
     }
     const int chunks = (int)(stride / 4);
     int shift = 0;
@@ -240,7 +252,7 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
     adam_slab_kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
-        quat_col < 0 ? -1 : quat_col / 4, half, s, cols);
+        quat_col < 0 ? -1 : quat_col / 4, half, visible_words, s, cols);
     return check_launch("adam_slab_kernel");
 }
 
@@ -261,7 +273,8 @@ extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, u
             hi[c] = a_max;
         }
         return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
-                                  beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED, stream);
+                                  beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED, nullptr, nullptr,
+                                  stream);
     }
     return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
                                weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);

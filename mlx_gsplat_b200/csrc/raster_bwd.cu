@@ -61,20 +61,18 @@ __device__ __forceinline__ void pixel_bwd_init(PixelBwd& s, bool inside, int64_t
     }
 }
 
-// Per-splat constants of the backward step: the splat's colour, its opacity,
-// -opacity / 2 (for dL/dm), and -2 conic_a, -(conic_b + conic_c), -2 conic_d
-// (for dL/du, dL/dv).
+// Per-splat constants of the backward step: colour and opacity.
 struct SplatBwd {
-    float r, g, b, opac, hop, na2, nsbc, nd2;
+    float r, g, b, opac;
 };
 
-// Adds one pixel's contribution of one splat to the nine running sums, or
-// nothing when ``valid`` is false.  Branch-free: both pixels of a thread are
-// evaluated whenever any lane of the warp is active, so the work is selected
-// with masks instead of branches (an invalid pixel gets alpha = 0, which
-// leaves T and B unchanged and zeroes every term).
-__device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, bool valid, float x, float y, float m,
-                                               const SplatBwd& c, float* g) {
+// One pixel's contribution of one splat, or nothing when ``valid`` is false.
+// Adds w T dL/dC to the colour sums g[6..8] and returns dog = dL/dalpha * g
+// (the geometry gradients are linear in it, see the kernel).  Branch-free:
+// both pixels of a thread are evaluated whenever any lane of the warp is
+// active, so the work is selected with masks instead of branches (an invalid
+// pixel gets alpha = 0, which leaves T and B unchanged and zeroes every term).
+__device__ __forceinline__ float pixel_bwd_step(PixelBwd& s, bool valid, float m, const SplatBwd& c, float* g) {
     const float gv = splat_falloff(m);
     const float og = c.opac * gv;
     const float al = valid ? fminf(og, 0.99f) : 0.f;
@@ -88,15 +86,7 @@ __device__ __forceinline__ void pixel_bwd_step(PixelBwd& s, bool valid, float x,
     g[8] = fmaf(wT, s.db, g[8]);
     // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
     const bool inside = valid && og > 0.f && og < 0.99f;
-    const float dog = inside ? s.T * d * gv : 0.f;  // dL/dalpha * g
-    g[5] += dog;                                    // d opacity
-    const float dm = c.hop * dog;                   // dL/dm
-    const float dmx = dm * x, dmy = dm * y;
-    g[0] = fmaf(c.na2, dmx, fmaf(c.nsbc, dmy, g[0]));  // d u
-    g[1] = fmaf(c.nsbc, dmx, fmaf(c.nd2, dmy, g[1]));  // d v
-    g[2] = fmaf(dmx, x, g[2]);                         // d conic a
-    g[3] = fmaf(dmx, y, g[3]);                         // d conic b (= d conic c)
-    g[4] = fmaf(dmy, y, g[4]);                         // d conic d
+    return inside ? s.T * d * gv : 0.f;
 }
 
 __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
@@ -173,18 +163,27 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const bool v0 = idx < a.last && m0 <= q2.z;
             const bool v1 = idx < b.last && m1 <= q2.z;
             if (!__any_sync(kFull, v0 || v1)) continue;
+            // Per thread sums over its two pixels (same column offset x):
+            //   g5 = sum dog, g0 = sum dog x, g1 = sum dog y, g2 = sum dog x^2,
+            //   g3 = sum dog x y, g4 = sum dog y^2, g6..8 = sum w T dL/dC.
+            // With dm = -opacity/2 * dog the splat gradients are linear in these
+            // sums; the per-splat factors are applied once, at the flush.
             float g[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             SplatBwd c;
             c.r = q1.w;
             c.g = q2.x;
             c.b = q2.y;
             c.opac = q1.z;
-            c.hop = -0.5f * q1.z;
-            c.na2 = -2.f * q0.z;
-            c.nsbc = -(q0.w + q1.x);
-            c.nd2 = -2.f * q1.y;
-            pixel_bwd_step(a, v0, x, y0, m0, c, g);
-            pixel_bwd_step(b, v1, x, y1, m1, c, g);
+            const float dog0 = pixel_bwd_step(a, v0, m0, c, g);
+            const float dog1 = pixel_bwd_step(b, v1, m1, c, g);
+            const float dsum = dog0 + dog1;
+            const float t0 = dog0 * y0, t1 = dog1 * y1;
+            g[5] = dsum;
+            g[0] = dsum * x;
+            g[1] = t0 + t1;
+            g[2] = g[0] * x;
+            g[3] = g[1] * x;
+            g[4] = fmaf(t0, y0, t1 * y1);
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
             const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
             const float t9 = warp_sum(g[8]);
@@ -200,9 +199,16 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
 #pragma unroll
             for (int c = 0; c < 9; ++c) any |= r[c] != 0.f;
             if (any) {
+                // dm = -opacity/2 * dog:  du = -sum dm (2a x + (b+c) y),  dv = -sum dm ((b+c) x + 2d y),
+                // d conic a = sum dm x^2,  d conic b = d conic c = sum dm x y,  d conic d = sum dm y^2
+                const float4 q0 = s0[j], q1 = s1[j];
+                const float hop = -0.5f * q1.z, sbc = q0.w + q1.x;
+                const float sx = hop * r[0], sy = hop * r[1];
+                const float du = -(2.f * q0.z * sx + sbc * sy);
+                const float dv = -(sbc * sx + 2.f * q1.y * sy);
                 float* rec = splat_grads + (int64_t)sv[j] * kGradRec;
-                red_add_v4(rec, r[0], r[1], r[2], r[3]);
-                red_add_v4(rec + 4, r[4], r[5], r[6], r[7]);
+                red_add_v4(rec, du, dv, hop * r[2], hop * r[3]);
+                red_add_v4(rec + 4, hop * r[4], r[5], r[6], r[7]);
                 atomicAdd(rec + 8, r[8]);
             }
 #pragma unroll

@@ -122,8 +122,10 @@ def _i32(n: int, device) -> torch.Tensor:
 
 # ----------------------------------------------------------------------------- cull
 def cull_ids(g: GsGaussians, n: int, cam: GsCamera, device, near_plane: float = 0.01, far_plane: float = 1e10,
-             opacity_threshold: float = -5.3, sync: bool = True):
-    """Ascending ids passing the cull; returns ``(ids_buffer, count_tensor, V or None)``."""
+             opacity_threshold: float = -5.3, sync: bool = True, return_scratch: bool = False):
+    """Ascending ids passing the cull; returns ``(ids_buffer, count_tensor, V or None)``
+    (and the scratch buffer, whose first words are the visibility bitmask, when
+    ``return_scratch``)."""
     lib = _lib.lib()
     ids = _i32(n, device)
     cnt = _i32(1, device)
@@ -132,6 +134,8 @@ def cull_ids(g: GsGaussians, n: int, cam: GsCamera, device, near_plane: float = 
     check(lib.gs_cull(g, n, cam, near_plane, far_plane, opacity_threshold, ids.data_ptr(), cnt.data_ptr(),
                       scratch.data_ptr(), scratch.numel(), _lib.stream_ptr(device)), "gs_cull")
     V = int(cnt.item()) if sync else None
+    if return_scratch:
+        return ids, cnt, V, scratch
     return ids, cnt, V
 
 

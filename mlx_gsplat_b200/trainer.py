@@ -122,6 +122,7 @@ class RunnerMLX:
         self.world = distributed.world_of(process_group)
         self.last_frame = None
         self.step_count = 0
+        self.sparse_unseen = True  # single GPU: unseen rows' gradients come from the visibility bits
 
     # ------------------------------------------------------------------ helpers
     def _reg_pattern(self) -> List[float]:
@@ -168,15 +169,21 @@ class RunnerMLX:
         g = self._gaussians(step)
         if timer:
             timer.mark("start")
-        ids, _, V = cull_ids(g, N, cam, self.device, cfg.near_plane, cfg.far_plane, cfg.opacity_threshold)
+        ids, _, V, cull_scratch = cull_ids(g, N, cam, self.device, cfg.near_plane, cfg.far_plane,
+                                           cfg.opacity_threshold, return_scratch=True)
         if timer:
             timer.mark("cull")
         frame = render_forward(g, ids, V, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
                                timer=timer)
-        _lib.check(lib.gs_fill_rows(self.grad.data_ptr(), N, self.layout.stride, _lib.fptr(self._reg_pattern()), st),
-                   "grad init")
-        if timer:
-            timer.mark("grad_init")
+        # Gradient rows of Gaussians this view does not see hold only the
+        # regulariser.  On one GPU Adam takes them from the cull's visibility bits
+        # (no rows written); across GPUs the all-reduce needs every row filled.
+        dense_rows = self.world > 1 or not self.sparse_unseen
+        if dense_rows:
+            _lib.check(lib.gs_fill_rows(self.grad.data_ptr(), N, self.layout.stride, _lib.fptr(self._reg_pattern()),
+                                        st), "grad init")
+            if timer:
+                timer.mark("grad_init")
         render_backward(frame, g, self._grad_out(step), self.device, grad2d=self.allocator.grad2d,
                         count=self.allocator.count, timer=timer)
         scale = 1.0
@@ -184,9 +191,11 @@ class RunnerMLX:
             scale = distributed.reduce_gradient_rows(self.grad[:N], self.pg)
             if timer:
                 timer.mark("allreduce")
+        vis = None if dense_rows else (cull_scratch.data_ptr() + 255) // 256 * 256
         self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
                                  self.allocator.indirection_table, N, self.layout.ncols, self.col_lo, self.col_hi,
-                                 quat_col=self.layout.quat_col, grad_scale=scale)
+                                 quat_col=self.layout.quat_col, grad_scale=scale, visible_words=vis,
+                                 unseen_grad=None if dense_rows else self._reg_pattern()[:self.layout.ncols])
         if timer:
             timer.mark("adam")
         self.last_frame = frame

@@ -17,6 +17,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("wl_name,n", [("tiny-3k", 3000), ("mid-200k", 20_000)])
 def test_train_step_matches_oracle(wl_name, n):
     r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15)
+    r.sparse_unseen = False  # write every gradient row so the test can inspect them
     al, L = r.allocator, r.layout
     step = 1
     theta0 = al.theta.cpu().numpy().copy()
@@ -64,6 +65,21 @@ def test_train_step_matches_oracle(wl_name, n):
         if k == "quats":
             th[table] = odens.quat_renorm(th[table])
         assert_adam_close(after[:, o:o + dd], th, what="adam " + k)
+
+
+def test_unseen_rows_from_visibility_bits_match_dense_rows():
+    """One GPU: Adam takes the gradient of Gaussians a view does not see from the
+    cull's visibility bits instead of pre-filled rows; the result is identical."""
+    runs = []
+    for sparse in (True, False):
+        r = runner_for_workload("mid-200k", max_steps=50, n=30_000, num_views=4, lr=1e-3, eps=1e-15)
+        r.sparse_unseen = sparse
+        for step in range(1, 5):
+            r.train_step(step - 1, step)
+        torch.cuda.synchronize()
+        runs.append([t.cpu().numpy() for t in (r.allocator.theta, r.allocator.adam_m, r.allocator.adam_v)])
+    for a, b in zip(*runs):
+        np.testing.assert_array_equal(a, b)
 
 
 def test_training_reduces_loss():
