@@ -80,6 +80,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the densify and 6M-row Adam measurements")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
     return ap.parse_args()
@@ -183,6 +184,41 @@ def kernel_bytes(name: str, N: int, V: int, K: int, P: int, tiles: int, ncols: i
     if name == "grad_init":
         return N * stride * 4
     return 0.0
+
+
+def adam_standalone(rows: int, layout, dev, iters: int = 10):
+    """The fused slab Adam over ``rows`` pooled rows (one launch per step), timed
+    with CUDA events; bytes = rows * (ncols * 28 + 4) (read theta, m, v, g, write
+    theta, m, v, read the indirection entry)."""
+    from mlx_gsplat_b200.optimizer import FusedMLXAdam
+    S = layout.stride
+    try:
+        th = torch.randn((rows, S), device=dev)
+        m = torch.zeros_like(th)
+        v = torch.zeros_like(th)
+        g = torch.randn_like(th) * 0.01
+        table = torch.arange(rows - 1, -1, -1, dtype=torch.int32, device=dev)
+    except torch.OutOfMemoryError:
+        return None
+    lo, hi = layout.col_bounds()
+    opt = FusedMLXAdam(lr=1e-3, eps=1e-15)
+    for _ in range(3):
+        opt.step_slab(th, g, m, v, table, rows, layout.ncols, lo.tolist(), hi.tolist(), quat_col=layout.quat_col)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        opt.step_slab(th, g, m, v, table, rows, layout.ncols, lo.tolist(), hi.tolist(), quat_col=layout.quat_col)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    b = rows * (layout.ncols * 28 + 4)
+    pk = peaks()["hbm_gbs"]
+    del th, m, v, g, table
+    torch.cuda.empty_cache()
+    return {"rows": rows, "ms": ms, "gbs": b / (ms * 1e-3) / 1e9, "frac": b / (ms * 1e-3) / 1e9 / pk,
+            "bytes": b, "inputs": "5.8 GB of slabs > L2"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
@@ -358,6 +394,25 @@ def main():
         e2e = {"value": world * 1000.0 / ms_e2e, "unit": "train steps/s", "ms_per_step": ms_e2e,
                "h2d_bytes_per_step": int(stage.numel()), "d2h_bytes_per_step": 4}
 
+    # ---- one densify/prune step on this scene (all ranks: the statistics are all-reduced)
+    densify_ms = None
+    if not args.no_extras:
+        al = runner.allocator
+        al.grad2d.normal_(2e-4, 1e-4).abs_()
+        al.count.fill_(1.0)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        n_p, n_s = runner.densify(step + 1)
+        torch.cuda.synchronize(dev)
+        densify_ms = {"ms": (time.perf_counter() - t0) * 1e3, "pruned": n_p, "refined": n_s,
+                      "active_after": al.num_active, "note": "wall clock incl. host count read-backs"}
+
+    # ---- the large workload's standalone fused Adam: 6M rows x 59 columns, theta/m/v/g
+    adam_6m = None
+    if world == 1 and not args.no_extras:
+        adam_6m = adam_standalone(6_000_000, L, dev)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline(args.workload, args.cpu_seconds)
@@ -377,6 +432,7 @@ def main():
                 "kernels_ms": {k: round(v["ms"], 4) for k, v in per.items()},
                 "phases_ms": {k: round(v, 4) for k, v in phase.items()},
                 "roofline": roof, "clocks": clk, "e2e": e2e, "cpu_baseline": base,
+                "densify": densify_ms, "adam_6m": adam_6m,
                 "gpu_launches": int(launches)}
         print(json.dumps(line), flush=True)
     if world > 1:
