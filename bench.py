@@ -299,8 +299,11 @@ def main():
     dev = torch.device("cuda", local)
     wl = synthetic.WORKLOADS[args.workload]
     nv = args.views or wl.num_views
+    n_init = args.gaussians or wl.num_gaussians
+    # a pool with headroom (the trainer's max_gaussians), so a densify step has free slots
     runner = runner_for_workload(args.workload, max_steps=10_000, device=dev, upload_targets=False, lr=1.6e-4,
-                                 eps=1e-15, n=args.gaussians, num_views=nv)
+                                 eps=1e-15, n=args.gaussians, num_views=nv,
+                                 max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2))
     runner.pg = pg
     runner.world = world
     targets_host = torch.from_numpy(synthetic.make_uint8_targets(wl, nv, seed=1)).pin_memory()
