@@ -119,36 +119,36 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
     int64_t offa = 0, offb = 0;
     if (va) {
         offa = (int64_t)__ldg(idx + ra) * chunks + c4;
-        tha = theta[offa];
-        ma = m[offa];
-        vva = v[offa];
+        tha = __ldcs(theta + offa);
+        ma = __ldcs(m + offa);
+        vva = __ldcs(v + offa);
         if (vis && !((__ldg(vis + (ra >> 5)) >> (ra & 31)) & 1u))
             ga = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
         else
-            ga = __ldg(g + ra * g_chunks + c4);
+            ga = __ldcs(g + ra * g_chunks + c4);
     }
     if (vb) {
         offb = (int64_t)__ldg(idx + rb) * chunks + c4;
-        thb = theta[offb];
-        mb = m[offb];
-        vvb = v[offb];
+        thb = __ldcs(theta + offb);
+        mb = __ldcs(m + offb);
+        vvb = __ldcs(v + offb);
         if (vis && !((__ldg(vis + (rb >> 5)) >> (rb & 31)) & 1u))
             gb = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
         else
-            gb = __ldg(g + rb * g_chunks + c4);
+            gb = __ldcs(g + rb * g_chunks + c4);
     }
     const bool renorm = c4 == quat_chunk;
     if (va) {
         slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
-        theta[offa] = tha;
-        m[offa] = ma;
-        v[offa] = vva;
+        __stcs(theta + offa, tha);
+        __stcs(m + offa, ma);
+        __stcs(v + offa, vva);
     }
     if (vb) {
         slab_update(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cs);
-        theta[offb] = thb;
-        m[offb] = mb;
-        v[offb] = vvb;
+        __stcs(theta + offb, thb);
+        __stcs(m + offb, mb);
+        __stcs(v + offb, vvb);
     }
 }
 
