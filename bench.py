@@ -401,15 +401,21 @@ def main():
     densify_ms = None
     if not args.no_extras:
         al = runner.allocator
-        al.grad2d.normal_(2e-4, 1e-4).abs_()
+        # statistics with mean 1e-4: about e^-2 = 13.5% of the Gaussians exceed the 2e-4 threshold
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        al.grad2d.exponential_(1e4, generator=gen)
         al.count.fill_(1.0)
         barrier(world)
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        n_p, n_s = runner.densify(step + 1)
-        torch.cuda.synchronize(dev)
-        densify_ms = {"ms": (time.perf_counter() - t0) * 1e3, "pruned": n_p, "refined": n_s,
-                      "active_after": al.num_active, "note": "wall clock incl. host count read-backs"}
+        try:
+            n_p, n_s = runner.densify(step + 1)
+            torch.cuda.synchronize(dev)
+            densify_ms = {"ms": (time.perf_counter() - t0) * 1e3, "pruned": n_p, "refined": n_s,
+                          "active_after": al.num_active, "note": "wall clock incl. host count read-backs"}
+        except MemoryError as e:
+            densify_ms = {"error": str(e)}
 
     # ---- the large workload's standalone fused Adam: 6M rows x 59 columns, theta/m/v/g
     adam_6m = None

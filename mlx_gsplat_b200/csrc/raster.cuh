@@ -243,14 +243,17 @@ __device__ __forceinline__ float quad_form(float ca, float s, float cd, float x,
 // centre is inside, otherwise the smallest of the four edge minima.
 __device__ __forceinline__ float rect_min_quad(float ca, float s, float cd, float x0, float x1, float y0, float y1) {
     if (x0 <= 0.f && 0.f <= x1 && y0 <= 0.f && 0.f <= y1) return 0.f;
+    // edge minimisers; an approximate reciprocal only moves them by ~1e-7 relative
+    // and the form is stationary there, so the minimum changes at second order
+    const float rcd = fast_rcp(cd), rca = fast_rcp(ca);
     float best = 3.4e38f;
-    const float ya = fminf(fmaxf(-s * x0 / cd, y0), y1);
+    const float ya = fminf(fmaxf(-s * x0 * rcd, y0), y1);
     best = fminf(best, quad_form(ca, s, cd, x0, ya));
-    const float yb = fminf(fmaxf(-s * x1 / cd, y0), y1);
+    const float yb = fminf(fmaxf(-s * x1 * rcd, y0), y1);
     best = fminf(best, quad_form(ca, s, cd, x1, yb));
-    const float xa = fminf(fmaxf(-s * y0 / ca, x0), x1);
+    const float xa = fminf(fmaxf(-s * y0 * rca, x0), x1);
     best = fminf(best, quad_form(ca, s, cd, xa, y0));
-    const float xb = fminf(fmaxf(-s * y1 / ca, x0), x1);
+    const float xb = fminf(fmaxf(-s * y1 * rca, x0), x1);
     best = fminf(best, quad_form(ca, s, cd, xb, y1));
     return best;
 }
@@ -277,20 +280,7 @@ __device__ __forceinline__ bool splat_hits_tile(float u, float v, float ca, floa
     const int j0 = ty * kTile, j1 = min(j0 + kTile - 1, p.rh - 1);
     const float x0 = (float)i0 * p.sx + p.hsx - u, x1 = (float)i1 * p.sx + p.hsx - u;
     const float y0 = (float)j0 * p.sy + p.hsy - v, y1 = (float)j1 * p.sy + p.hsy - v;
-    if (x0 <= 0.f && 0.f <= x1 && y0 <= 0.f && 0.f <= y1) return true;
-    const float s = tb.s;
-    float best = 3.4e38f;
-    {
-        const float ya = fminf(fmaxf(-s * x0 / cd, y0), y1);
-        best = fminf(best, quad_form(ca, s, cd, x0, ya));
-        const float yb = fminf(fmaxf(-s * x1 / cd, y0), y1);
-        best = fminf(best, quad_form(ca, s, cd, x1, yb));
-        const float xa = fminf(fmaxf(-s * y0 / ca, x0), x1);
-        best = fminf(best, quad_form(ca, s, cd, xa, y0));
-        const float xb = fminf(fmaxf(-s * y1 / ca, x0), x1);
-        best = fminf(best, quad_form(ca, s, cd, xb, y1));
-    }
-    return best <= tb.m_cut * 1.0002f + 1e-3f;
+    return rect_min_quad(ca, tb.s, cd, x0, x1, y0, y1) <= tb.m_cut * 1.0002f + 1e-3f;
 }
 
 }  // namespace gs

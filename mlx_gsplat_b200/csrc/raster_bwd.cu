@@ -226,7 +226,7 @@ __device__ __forceinline__ void put(float* base, int64_t off, float v, bool acc)
 
 // Chain rule from the splat gradient record back to means, quaternions,
 // log-scales, opacity logits and SH colour coefficients.
-__global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
+__global__ void __launch_bounds__(128, 8) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
                                                           RasterParams p, const float* __restrict__ splat_grads,
                                                           gs_gaussian_grads o, float* __restrict__ grad2d,
                                                           float* __restrict__ count) {
