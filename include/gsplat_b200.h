@@ -234,6 +234,12 @@ int gs_bin_emit(const float* splats, const uint32_t* order, const uint32_t* offs
 int gs_tile_ranges(const uint32_t* sorted_tile_keys, int64_t num_entries, int32_t num_tiles,
                    gs_tile_range* ranges, gs_stream_t stream);
 
+/* Dispatch order for the compositing kernels: the num_tiles tile indices
+ * ordered by decreasing entry count (bucketed; ties in any order), so the
+ * heaviest tiles start first and the launch does not end on a few long tiles.
+ * Results do not depend on the order; it only changes when each tile runs. */
+int gs_tile_order(const gs_tile_range* ranges, int32_t num_tiles, int32_t* order, gs_stream_t stream);
+
 #define GS_LOSS_NONE 0       /* no loss: the backward takes dL/dcolor, dL/dalpha buffers */
 #define GS_LOSS_L1_U8 1      /* mean |C - target| with a uint8 HWC target (scaled by 1/255) */
 #define GS_LOSS_L1_F32 2     /* mean |C - target| with a float32 HWC target */
@@ -244,8 +250,11 @@ int gs_tile_ranges(const uint32_t* sorted_tile_keys, int64_t num_entries, int32_
  * (HWC float32), the final transmittance and the number of entries each pixel
  * consumed (for the backward).  With a loss mode, ``loss_partials[tile]``
  * receives that tile's sum of |C - target| (or of C).  Entry values at or
- * beyond ``num_visible`` are never dereferenced (they read splat 0). */
-int gs_render_forward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+ * beyond ``num_visible`` are never dereferenced (they read splat 0).
+ * ``tile_order`` (num_tiles entries from gs_tile_order, or NULL for tile index
+ * order) only sets the order in which tiles are dispatched. */
+int gs_render_forward(const gs_tile_range* ranges, const int32_t* tile_order, const uint32_t* entry_vals,
+                      const float* splats,
                       int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, float* out_color, float* out_alpha,
                       float* final_T, int32_t* n_contrib, int loss_mode, const void* target, float* loss_partials,
                       gs_stream_t stream);
@@ -255,8 +264,10 @@ int gs_render_forward(const gs_tile_range* ranges, const uint32_t* entry_vals, c
  * atomics, the 12-float record {du, dv, dconic_a, dconic_bc}, {dconic_d,
  * dopacity, dr, dg}, {db, 0, 0, 0} into ``splat_grads`` (zeroed by the caller).
  * dL/dcolor comes from ``dL_dcolor`` [RH,RW,3] (+ ``dL_dalpha`` [RH,RW,1],
- * may be NULL) for GS_LOSS_NONE, or is formed from the loss mode. */
-int gs_render_backward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+ * may be NULL) for GS_LOSS_NONE, or is formed from the loss mode.
+ * ``tile_order`` as in gs_render_forward. */
+int gs_render_backward(const gs_tile_range* ranges, const int32_t* tile_order, const uint32_t* entry_vals,
+                       const float* splats,
                        int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, const float* out_color,
                        const float* final_T, const int32_t* n_contrib, int loss_mode, const void* target,
                        const float* dL_dcolor, const float* dL_dalpha, float* splat_grads, gs_stream_t stream);

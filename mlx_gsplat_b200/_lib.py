@@ -84,10 +84,11 @@ _SIGS = {
     "gs_bin_emit": (ctypes.c_int, [c_vp] * 4 + [i64, ctypes.POINTER(GsCamera), ctypes.POINTER(GsRasterSettings),
                                                 c_vp, c_vp, i64, c_vp, c_vp]),
     "gs_tile_ranges": (ctypes.c_int, [c_vp, i64, ctypes.c_int32, c_vp, c_vp]),
-    "gs_render_forward": (ctypes.c_int, [c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
+    "gs_tile_order": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp, c_vp]),
+    "gs_render_forward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
                                          ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, c_vp, ctypes.c_int,
                                          c_vp, c_vp, c_vp]),
-    "gs_render_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
+    "gs_render_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
                                           ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, ctypes.c_int, c_vp,
                                           c_vp, c_vp, c_vp, c_vp]),
     "gs_project_backward": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, i64, ctypes.POINTER(GsCamera), c_vp,

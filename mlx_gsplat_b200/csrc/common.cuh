@@ -17,8 +17,6 @@ int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, 
 
 constexpr int kTile = 16;               // tile edge in pixels
 constexpr int kTileThreads = kTile * kTile;
-constexpr int kRenderThreads = 128;     // compositing CTA: two pixels per thread
-constexpr int kBatch = 256;             // splats staged in shared memory per batch
 constexpr unsigned kFull = 0xffffffffu;
 
 int set_error(int code, const char* fmt, ...);

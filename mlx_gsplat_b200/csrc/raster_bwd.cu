@@ -5,6 +5,21 @@
 
 namespace gs {
 
+// Compositing layout: one CTA per 16x16 tile; each thread owns kPx pixels of
+// one column, 4 rows apart, so a warp covers an 8-wide, 4 * kPx-tall block.
+#ifndef GS_BWD_PX
+#define GS_BWD_PX 4
+#endif
+#ifndef GS_BWD_BATCH
+#define GS_BWD_BATCH 128
+#endif
+constexpr int kPx = GS_BWD_PX;
+static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
+constexpr int kRenderThreads = kTileThreads / kPx;
+constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
+constexpr int kBatch = GS_BWD_BATCH;  // splats staged in shared memory per batch
+static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
+
 constexpr int kGradRec = 12;  // floats per splat gradient record
 
 // For every tile: walk the tile's entries from the last one any pixel used
@@ -13,9 +28,9 @@ constexpr int kGradRec = 12;  // floats per splat gradient record
 //   val_i = dL/dC . rgb_i + dL/dA,   B_{i-1} = alpha_i val_i + (1 - alpha_i) B_i
 // the alpha gradient is dL/dalpha_i = T_i (val_i - B_i).  The clip of
 // opacity * g to [0, 0.99] passes the gradient only strictly inside
-// (MLX's maximum/minimum rule).  Thread layout as in the forward (two pixels
-// of one column per thread, 128 threads per tile).  The nine per-splat sums
-// of a warp's 64 pixels are reduced with 14 shuffles, added into per-batch
+// (MLX's maximum/minimum rule).  Thread layout as in the forward (kPx pixels
+// of one column per thread, one CTA per tile).  The nine per-splat sums of a
+// warp's pixels are reduced with 14 shuffles, added into per-batch
 // shared-memory accumulators, and flushed with one global vector reduction
 // per (tile, splat).
 struct PixelBwd {
@@ -90,7 +105,7 @@ __device__ __forceinline__ float pixel_bwd_step(PixelBwd& s, bool valid, float m
 }
 
 __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
-    const gs_tile_range* __restrict__ ranges, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
+    const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
     const float* __restrict__ dL_dcolor, const float* __restrict__ dL_dalpha, float* __restrict__ splat_grads) {
@@ -98,29 +113,31 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
     __shared__ uint32_t sv[kBatch];
     __shared__ float acc[kBatch][9];  // per-batch CTA sums of the splat gradients
     __shared__ int smax;
-    const int tile = blockIdx.x;
+    const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
+    if (tile < 0 || tile >= p.tiles_x * p.tiles_y) return;  // uniform over the CTA
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pi = tx * kTile + (warp & 1) * 8 + (lane & 7);
-    const int pj0 = ty * kTile + (warp >> 1) * 8 + (lane >> 3);
-    const int pj1 = pj0 + 4;
-    const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
+    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * kBlockRows;  // this warp's block
+    const int pi = bx0 + (lane & 7);
     const float px = (float)pi * p.sx + p.hsx;
-    const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
-    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * 8;  // this warp's 8x8 block
     const gs_tile_range rg = ranges[tile];
     for (int j = threadIdx.x; j < kBatch; j += kRenderThreads)
 #pragma unroll
         for (int c = 0; c < 9; ++c) acc[j][c] = 0.f;
 
-    PixelBwd a, b;
-    pixel_bwd_init(a, in0, (int64_t)pj0 * p.rw + pi, p, out_color, final_T, n_contrib, loss_mode, target, dL_dcolor,
-                   dL_dalpha);
-    pixel_bwd_init(b, in1, (int64_t)pj1 * p.rw + pi, p, out_color, final_T, n_contrib, loss_mode, target, dL_dcolor,
-                   dL_dalpha);
+    PixelBwd s[kPx];
+    float py[kPx];
+    int mylast = 0;
+#pragma unroll
+    for (int k = 0; k < kPx; ++k) {
+        const int pj = by0 + (lane >> 3) + 4 * k;
+        py[k] = (float)pj * p.sy + p.hsy;
+        pixel_bwd_init(s[k], pi < p.rw && pj < p.rh, (int64_t)pj * p.rw + pi, p, out_color, final_T, n_contrib,
+                       loss_mode, target, dL_dcolor, dL_dalpha);
+        mylast = max(mylast, s[k].last);
+    }
     if (threadIdx.x == 0) smax = 0;
     __syncthreads();
-    const int mylast = max(a.last, b.last);
     if (mylast > 0) atomicMax(&smax, mylast);
     __syncthreads();
     const int max_last = smax;
@@ -138,12 +155,13 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             s2[j] = splats[3 * vi + 2];
         }
         __syncthreads();
-        // which staged splats can reach this warp's 8x8 pixel block (same test as the forward)
+        // which staged splats can reach this warp's pixel block (same test as the forward)
         unsigned hits[kBatch / 32];
 #pragma unroll
         for (int i = 0; i < kBatch / 32; ++i) {
             const int k = 32 * i + lane;
-            const bool h = k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + 7, p);
+            const bool h =
+                k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + kBlockRows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
 #pragma unroll
@@ -157,13 +175,18 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
             const float x = px - q0.x;
             const float ax = q0.z * x, cx = q1.x * x;
-            const float y0 = py0 - q0.y, y1 = py1 - q0.y;
-            const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
-            const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
-            const bool v0 = idx < a.last && m0 <= q2.z;
-            const bool v1 = idx < b.last && m1 <= q2.z;
-            if (!__any_sync(kFull, v0 || v1)) continue;
-            // Per thread sums over its two pixels (same column offset x):
+            float y[kPx], m[kPx];
+            bool v[kPx];
+            bool any = false;
+#pragma unroll
+            for (int r = 0; r < kPx; ++r) {
+                y[r] = py[r] - q0.y;
+                m[r] = x * (ax + q0.w * y[r]) + y[r] * (cx + q1.y * y[r]);
+                v[r] = idx < s[r].last && m[r] <= q2.z;
+                any |= v[r];
+            }
+            if (!__any_sync(kFull, any)) continue;
+            // Per thread sums over its pixels (same column offset x):
             //   g5 = sum dog, g0 = sum dog x, g1 = sum dog y, g2 = sum dog x^2,
             //   g3 = sum dog x y, g4 = sum dog y^2, g6..8 = sum w T dL/dC.
             // With dm = -opacity/2 * dog the splat gradients are linear in these
@@ -174,16 +197,19 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             c.g = q2.x;
             c.b = q2.y;
             c.opac = q1.z;
-            const float dog0 = pixel_bwd_step(a, v0, m0, c, g);
-            const float dog1 = pixel_bwd_step(b, v1, m1, c, g);
-            const float dsum = dog0 + dog1;
-            const float t0 = dog0 * y0, t1 = dog1 * y1;
+            float dsum = 0.f;
+#pragma unroll
+            for (int r = 0; r < kPx; ++r) {
+                const float dog = pixel_bwd_step(s[r], v[r], m[r], c, g);
+                const float t = dog * y[r];
+                dsum += dog;
+                g[1] += t;
+                g[4] = fmaf(t, y[r], g[4]);
+            }
             g[5] = dsum;
             g[0] = dsum * x;
-            g[1] = t0 + t1;
             g[2] = g[0] * x;
             g[3] = g[1] * x;
-            g[4] = fmaf(t0, y0, t1 * y1);
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
             const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
             const float t9 = warp_sum(g[8]);
@@ -226,7 +252,7 @@ __device__ __forceinline__ void put(float* base, int64_t off, float v, bool acc)
 
 // Chain rule from the splat gradient record back to means, quaternions,
 // log-scales, opacity logits and SH colour coefficients.
-__global__ void __launch_bounds__(128, 8) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
+__global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
                                                           RasterParams p, const float* __restrict__ splat_grads,
                                                           gs_gaussian_grads o, float* __restrict__ grad2d,
                                                           float* __restrict__ count) {
@@ -406,7 +432,8 @@ __global__ void __launch_bounds__(128, 8) project_bwd_kernel(gs_gaussians g, con
 
 using namespace gs;
 
-extern "C" int gs_render_backward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+extern "C" int gs_render_backward(const gs_tile_range* ranges, const int32_t* tile_order, const uint32_t* entry_vals,
+                                  const float* splats,
                                   int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs,
                                   const float* out_color,
                                   const float* final_T, const int32_t* n_contrib, int loss_mode, const void* target,
@@ -421,7 +448,8 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const uint32_t* e
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
     render_bwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
-        ranges, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T, n_contrib, loss_mode,
+        ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T,
+        n_contrib, loss_mode,
         target, dL_dcolor, dL_dalpha, splat_grads);
     return check_launch("render_bwd_kernel");
 }

@@ -163,13 +163,83 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
     if (i == n - 1 || keys[i + 1] != t) ranges[t].end = (int32_t)(i + 1);
 }
 
+// Compositing layout: one CTA per 16x16 tile; each thread owns kPx pixels of
+// one column, 4 rows apart, so a warp covers an 8-wide, 4 * kPx-tall block.
+#ifndef GS_FWD_PX
+#define GS_FWD_PX 2
+#endif
+#ifndef GS_FWD_BATCH
+#define GS_FWD_BATCH 256
+#endif
+constexpr int kPx = GS_FWD_PX;
+static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
+constexpr int kRenderThreads = kTileThreads / kPx;
+constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
+constexpr int kBatch = GS_FWD_BATCH;  // splats staged in shared memory per batch
+static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
+
+// Dispatch order of the compositing CTAs: tiles by decreasing entry count
+// (longest-processing-time-first), so the heaviest tiles start in the first
+// wave and the kernel does not end on a few long tiles.  One CTA: counts are
+// bucketed linearly against the largest count into kOrderBuckets buckets and
+// counting-sorted (order within a bucket is arbitrary; every tile's result is
+// independent of when it runs).
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderBuckets = 1024;
+static_assert(kOrderThreads == kOrderBuckets && kOrderThreads == 32 * 32, "one bucket per thread, 32 warps");
+
+__global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const gs_tile_range* __restrict__ ranges,
+                                                                   int32_t num_tiles, int32_t* __restrict__ order) {
+    __shared__ int32_t start[kOrderBuckets];
+    __shared__ int32_t warp_tot[kOrderThreads / 32];
+    __shared__ int32_t smax;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    if (t == 0) smax = 0;
+    start[t] = 0;
+    __syncthreads();
+    int mx = 0;
+    for (int i = t; i < num_tiles; i += kOrderThreads) mx = max(mx, ranges[i].end - ranges[i].start);
+    atomicMax(&smax, mx);
+    __syncthreads();
+    const int64_t cmax = smax;
+    auto bucket = [&](int i) -> int {
+        const int64_t c = max(ranges[i].end - ranges[i].start, 0);
+        return cmax > 0 ? (kOrderBuckets - 1) - (int)(c * (kOrderBuckets - 1) / cmax) : 0;
+    };
+    for (int i = t; i < num_tiles; i += kOrderThreads) atomicAdd(&start[bucket(i)], 1);
+    __syncthreads();
+    // exclusive scan of the bucket sizes (one bucket per thread)
+    const int v = start[t];
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_tot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_tot[lane] = w;  // inclusive per-warp totals
+    }
+    __syncthreads();
+    start[t] = incl - v + (warp > 0 ? warp_tot[warp - 1] : 0);
+    __syncthreads();
+    for (int i = t; i < num_tiles; i += kOrderThreads) order[atomicAdd(&start[bucket(i)], 1)] = i;
+}
+
 // ---------------------------------------------------------------- compositing
-// One CTA of 128 threads per 16x16 tile; each thread owns two pixels of one
-// column, 4 rows apart.  Warp w owns the 8x8 block ((w & 1) * 8, (w >> 1) * 8):
-// lane l has column l & 7 and rows (l >> 3) and (l >> 3) + 4.  Splats are
-// staged 256 at a time in shared memory (two per thread) and read back as
-// broadcasts; a warp skips the rest of a batch once all its 64 pixels are
-// saturated (T < t_min) and the CTA stops when all 256 are.
+// One CTA per 16x16 tile; each thread owns kPx pixels of one column, 4 rows
+// apart.  Warp w owns the 8 x kBlockRows block ((w & 1) * 8, (w >> 1) *
+// kBlockRows): lane l has column l & 7 and rows (l >> 3) + 4 k.  Splats are
+// staged kBatch at a time in shared memory and read back as broadcasts; a warp
+// skips the rest of a batch once all its pixels are saturated (T < t_min) and
+// the CTA stops when all 256 are.
 __device__ __forceinline__ void composite_pixel(float m, float4 q1, float4 q2, float& T, float& cr, float& cg,
                                                 float& cb, float& A, int& last, bool& done, int idx1, float t_min) {
     if (!done && m <= q2.z) {
@@ -202,30 +272,37 @@ __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, i
 }
 
 __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
-    const gs_tile_range* __restrict__ ranges, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
+    const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, float* __restrict__ out_color, float* __restrict__ out_alpha, float* __restrict__ final_T,
     int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
     float* __restrict__ loss_partials) {
     __shared__ float4 s0[kBatch], s1[kBatch], s2[kBatch];
     __shared__ float red[kRenderThreads / 32];
-    const int tile = blockIdx.x;
+    const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
+    if (tile < 0 || tile >= p.tiles_x * p.tiles_y) return;  // uniform over the CTA
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pi = tx * kTile + (warp & 1) * 8 + (lane & 7);
-    const int pj0 = ty * kTile + (warp >> 1) * 8 + (lane >> 3);
-    const int pj1 = pj0 + 4;
-    const bool in0 = pi < p.rw && pj0 < p.rh, in1 = pi < p.rw && pj1 < p.rh;
+    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * kBlockRows;  // this warp's block
+    const int pi = bx0 + (lane & 7);
     const float px = (float)pi * p.sx + p.hsx;
-    const float py0 = (float)pj0 * p.sy + p.hsy, py1 = (float)pj1 * p.sy + p.hsy;
-    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * 8;  // this warp's 8x8 block
     const gs_tile_range rg = ranges[tile];
 
-    float T0 = 1.f, r0 = 0.f, g0 = 0.f, b0 = 0.f, A0 = 0.f;
-    float T1 = 1.f, r1 = 0.f, g1 = 0.f, b1 = 0.f, A1 = 0.f;
-    int last0 = 0, last1 = 0;
-    bool done0 = !in0, done1 = !in1;
+    float py[kPx], T[kPx], cr[kPx], cg[kPx], cb[kPx], A[kPx];
+    int last[kPx];
+    bool done[kPx];
+    bool all_done = true;
+#pragma unroll
+    for (int k = 0; k < kPx; ++k) {
+        const int pj = by0 + (lane >> 3) + 4 * k;
+        py[k] = (float)pj * p.sy + p.hsy;
+        T[k] = 1.f;
+        cr[k] = cg[k] = cb[k] = A[k] = 0.f;
+        last[k] = 0;
+        done[k] = !(pi < p.rw && pj < p.rh);
+        all_done &= done[k];
+    }
     for (int b = rg.start; b < rg.end; b += kBatch) {
-        if (__syncthreads_count(done0 && done1) == kRenderThreads) break;
+        if (__syncthreads_count(all_done) == kRenderThreads) break;
 #pragma unroll
         for (int h = 0; h < kBatch / kRenderThreads; ++h) {
             const int j = threadIdx.x + h * kRenderThreads;
@@ -241,14 +318,14 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
         __syncthreads();
         const int cnt = min(kBatch, rg.end - b);
         const int base1 = b - rg.start + 1;
-        // which staged splats can reach this warp's 8x8 pixel block at all
-        bool warp_done = __all_sync(kFull, done0 && done1);
+        // which staged splats can reach this warp's pixel block at all
+        bool warp_done = __all_sync(kFull, all_done);
         unsigned hits[kBatch / 32];
 #pragma unroll
         for (int i = 0; i < kBatch / 32; ++i) {
             const int k = 32 * i + lane;
             const bool h = !warp_done && k < cnt &&
-                           splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + 7, p);
+                           splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + kBlockRows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
 #pragma unroll
@@ -260,37 +337,35 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
                 const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
                 const float x = px - q0.x;
                 const float ax = q0.z * x, cx = q1.x * x;
-                const float y0 = py0 - q0.y, y1 = py1 - q0.y;
-                const float m0 = x * (ax + q0.w * y0) + y0 * (cx + q1.y * y0);
-                const float m1 = x * (ax + q0.w * y1) + y1 * (cx + q1.y * y1);
-                composite_pixel(m0, q1, q2, T0, r0, g0, b0, A0, last0, done0, base1 + k, p.t_min);
-                composite_pixel(m1, q1, q2, T1, r1, g1, b1, A1, last1, done1, base1 + k, p.t_min);
-                warp_done = __all_sync(kFull, done0 && done1);
+                all_done = true;
+#pragma unroll
+                for (int r = 0; r < kPx; ++r) {
+                    const float y = py[r] - q0.y;
+                    const float m = x * (ax + q0.w * y) + y * (cx + q1.y * y);
+                    composite_pixel(m, q1, q2, T[r], cr[r], cg[r], cb[r], A[r], last[r], done[r], base1 + k,
+                                    p.t_min);
+                    all_done &= done[r];
+                }
+                warp_done = __all_sync(kFull, all_done);
             }
         }
         __syncthreads();
     }
 
     float lsum = 0.f;
-    if (in0) {
-        const int64_t pix = (int64_t)pj0 * p.rw + pi;
-        out_color[3 * pix + 0] = r0;
-        out_color[3 * pix + 1] = g0;
-        out_color[3 * pix + 2] = b0;
-        out_alpha[pix] = A0;
-        final_T[pix] = T0;
-        n_contrib[pix] = last0;
-        lsum += pixel_loss(loss_mode, target, pix, r0, g0, b0);
-    }
-    if (in1) {
-        const int64_t pix = (int64_t)pj1 * p.rw + pi;
-        out_color[3 * pix + 0] = r1;
-        out_color[3 * pix + 1] = g1;
-        out_color[3 * pix + 2] = b1;
-        out_alpha[pix] = A1;
-        final_T[pix] = T1;
-        n_contrib[pix] = last1;
-        lsum += pixel_loss(loss_mode, target, pix, r1, g1, b1);
+#pragma unroll
+    for (int k = 0; k < kPx; ++k) {
+        const int pj = by0 + (lane >> 3) + 4 * k;
+        if (pi < p.rw && pj < p.rh) {
+            const int64_t pix = (int64_t)pj * p.rw + pi;
+            out_color[3 * pix + 0] = cr[k];
+            out_color[3 * pix + 1] = cg[k];
+            out_color[3 * pix + 2] = cb[k];
+            out_alpha[pix] = A[k];
+            final_T[pix] = T[k];
+            n_contrib[pix] = last[k];
+            lsum += pixel_loss(loss_mode, target, pix, cr[k], cg[k], cb[k]);
+        }
     }
     if (loss_mode != GS_LOSS_NONE) {
         lsum = warp_sum(lsum);
@@ -373,7 +448,14 @@ extern "C" int gs_tile_ranges(const uint32_t* sorted_tile_keys, int64_t num_entr
     return check_launch("tile_ranges_kernel");
 }
 
-extern "C" int gs_render_forward(const gs_tile_range* ranges, const uint32_t* entry_vals, const float* splats,
+extern "C" int gs_tile_order(const gs_tile_range* ranges, int32_t num_tiles, int32_t* order, gs_stream_t stream) {
+    GS_REQUIRE(ranges && order && num_tiles > 0, "tile_order: bad arguments");
+    tile_order_kernel<<<1, kOrderThreads, 0, (cudaStream_t)stream>>>(ranges, num_tiles, order);
+    return check_launch("tile_order_kernel");
+}
+
+extern "C" int gs_render_forward(const gs_tile_range* ranges, const int32_t* tile_order, const uint32_t* entry_vals,
+                                 const float* splats,
                                  int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs,
                                  float* out_color,
                                  float* out_alpha, float* final_T, int32_t* n_contrib, int loss_mode,
@@ -385,7 +467,8 @@ extern "C" int gs_render_forward(const gs_tile_range* ranges, const uint32_t* en
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
     render_fwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
-        ranges, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, out_alpha, final_T, n_contrib,
+        ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, out_alpha,
+        final_T, n_contrib,
         loss_mode, target, loss_partials);
     return check_launch("render_fwd_kernel");
 }

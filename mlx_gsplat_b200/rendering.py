@@ -165,6 +165,7 @@ class TileFrame:
     def __init__(self):
         self.V = 0
         self.K = 0
+        self.tile_order = None  # dispatch order of the compositing CTAs (None: tile index order)
 
 
 def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, settings: RasterSettings,
@@ -221,6 +222,9 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
                                           f.entry_vals.data_ptr(), K, 0, tile_bits, sb2.data_ptr(), sb2.numel(), st),
                   "tile sort")
             check(lib.gs_tile_ranges(f.tile_keys.data_ptr(), K, T, f.ranges.data_ptr(), st), "gs_tile_ranges")
+            # heaviest tiles first: the compositing launches then end evenly across the SMs
+            f.tile_order = _i32(T, device)
+            check(lib.gs_tile_order(f.ranges.data_ptr(), T, f.tile_order.data_ptr(), st), "gs_tile_order")
             if timer:
                 timer.mark("bin+tile_sort")
         else:
@@ -230,7 +234,8 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
         f.entry_vals = _i32(1, device)
         f.ranges.zero_()
     tptr = None if target is None else target.data_ptr()
-    check(lib.gs_render_forward(f.ranges.data_ptr(), f.entry_vals.data_ptr(), f.splats.data_ptr(), V, cam, rs,
+    check(lib.gs_render_forward(f.ranges.data_ptr(), _lib.ptr(f.tile_order), f.entry_vals.data_ptr(),
+                                f.splats.data_ptr(), V, cam, rs,
                                 f.color.data_ptr(), f.alpha.data_ptr(), f.final_T.data_ptr(), f.n_contrib.data_ptr(),
                                 loss_mode, tptr, None if f.loss_partials is None else f.loss_partials.data_ptr(), st),
           "gs_render_forward")
@@ -249,7 +254,8 @@ def render_backward(f: TileFrame, g: GsGaussians, out: GsGaussianGrads, device,
         return
     f.splat_grads = torch.zeros((f.V, 12), dtype=torch.float32, device=device)
     tptr = None if f.target is None else f.target.data_ptr()
-    check(lib.gs_render_backward(f.ranges.data_ptr(), f.entry_vals.data_ptr(), f.splats.data_ptr(), f.V, f.cam, f.rs,
+    check(lib.gs_render_backward(f.ranges.data_ptr(), _lib.ptr(f.tile_order), f.entry_vals.data_ptr(),
+                                 f.splats.data_ptr(), f.V, f.cam, f.rs,
                                  f.color.data_ptr(), f.final_T.data_ptr(), f.n_contrib.data_ptr(), f.loss_mode, tptr,
                                  None if dL_dcolor is None else dL_dcolor.data_ptr(),
                                  None if dL_dalpha is None else dL_dalpha.data_ptr(), f.splat_grads.data_ptr(), st),
