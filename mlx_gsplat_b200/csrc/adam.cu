@@ -72,7 +72,7 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
 // Per-column constants live in shared memory: indexing the kernel-parameter
 // copy with a lane-dependent column made every access a divergent constant
 // load (serialised in the address-divergence unit).
-struct ColsSmem {
+struct __align__(16) ColsSmem {
     float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols];
 };
 
@@ -115,28 +115,33 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
     if (c4 >= chunks || 4 * c4 >= ncols) return;
     const int64_t ra = t0 >> lane_shift, rb = (t0 + half) >> lane_shift;
     const bool va = ra < n_rows, vb = rb < n_rows;
-    float4 tha, ma, vva, ga, thb, mb, vvb, gb;
+    // Two dependency levels, each issued for both items before anything waits:
+    // the indirection entries and visibility words, then every data load.
     int64_t offa = 0, offb = 0;
+    uint32_t wa = ~0u, wb = ~0u;
     if (va) {
         offa = (int64_t)__ldg(idx + ra) * chunks + c4;
-        tha = __ldcs(theta + offa);
-        ma = __ldcs(m + offa);
-        vva = __ldcs(v + offa);
-        if (vis && !((__ldg(vis + (ra >> 5)) >> (ra & 31)) & 1u))
-            ga = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
-        else
-            ga = __ldcs(g + ra * g_chunks + c4);
+        if (vis) wa = __ldg(vis + (ra >> 5));
     }
     if (vb) {
         offb = (int64_t)__ldg(idx + rb) * chunks + c4;
+        if (vis) wb = __ldg(vis + (rb >> 5));
+    }
+    const bool ga_seen = va && ((wa >> (ra & 31)) & 1u), gb_seen = vb && ((wb >> (rb & 31)) & 1u);
+    const float4 gdef = reinterpret_cast<const float4*>(cs.gdef)[c4];
+    float4 tha = gdef, ma = gdef, vva = gdef, ga = gdef, thb = gdef, mb = gdef, vvb = gdef, gb = gdef;
+    if (va) {
+        tha = __ldcs(theta + offa);
+        ma = __ldcs(m + offa);
+        vva = __ldcs(v + offa);
+    }
+    if (vb) {
         thb = __ldcs(theta + offb);
         mb = __ldcs(m + offb);
         vvb = __ldcs(v + offb);
-        if (vis && !((__ldg(vis + (rb >> 5)) >> (rb & 31)) & 1u))
-            gb = make_float4(cs.gdef[4 * c4], cs.gdef[4 * c4 + 1], cs.gdef[4 * c4 + 2], cs.gdef[4 * c4 + 3]);
-        else
-            gb = __ldcs(g + rb * g_chunks + c4);
     }
+    if (ga_seen) ga = __ldcs(g + ra * g_chunks + c4);
+    if (gb_seen) gb = __ldcs(g + rb * g_chunks + c4);
     const bool renorm = c4 == quat_chunk;
     if (va) {
         slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);

@@ -182,6 +182,32 @@ __device__ __forceinline__ float fast_rcp(float x) {
     return y;
 }
 
+// ------------------------------------------------------------------ pixel pairs
+// The compositing kernels evaluate two pixels of one column together with the
+// sm_100 paired fp32 instructions (one issue slot for two round-to-nearest
+// multiplies / adds / fused multiply-adds); each lane of a pair rounds exactly
+// like its scalar counterpart.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+// Mahalanobis distances of a pixel pair at offsets (x, y.x) and (x, y.y) from a
+// splat with conic (a, b; c, d), given ax = a x and cx = c x:
+//   m = x (a x + b y) + y (c x + d y).
+// The forward and the backward both call this, so they agree bit for bit.
+__device__ __forceinline__ float2 pair_quad(float2 y, float x, float ax, float cx, float b, float d) {
+    const float2 t1 = __ffma2_rn(f2(b), y, f2(ax));
+    const float2 t2 = __ffma2_rn(f2(d), y, f2(cx));
+    return __ffma2_rn(f2(x), t1, __fmul2_rn(y, t2));
+}
+
+// splat_falloff of both lanes.
+__device__ __forceinline__ float2 pair_falloff(float2 m) {
+    const float2 e = __fmul2_rn(m, f2(kHalfNegLog2e));
+    float2 r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(e.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(e.y));
+    return r;
+}
+
 // ------------------------------------------------------------------ per-pixel contribution rule
 // A (pixel, splat) pair contributes iff its Mahalanobis distance m satisfies
 // m <= 2 ln(opacity / alpha_cutoff), i.e. alpha = opacity * exp(-m/2) >=

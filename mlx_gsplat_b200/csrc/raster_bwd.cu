@@ -10,6 +10,9 @@ namespace gs {
 #ifndef GS_BWD_PX
 #define GS_BWD_PX 4
 #endif
+#ifndef GS_BWD_MIN_CTAS
+#define GS_BWD_MIN_CTAS 16
+#endif
 #ifndef GS_BWD_BATCH
 #define GS_BWD_BATCH 128
 #endif
@@ -17,6 +20,7 @@ constexpr int kPx = GS_BWD_PX;
 static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
 constexpr int kRenderThreads = kTileThreads / kPx;
 constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
+constexpr int kPairs = kPx / 2;          // pixel pairs per thread
 constexpr int kBatch = GS_BWD_BATCH;  // splats staged in shared memory per batch
 static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
 
@@ -81,30 +85,49 @@ struct SplatBwd {
     float r, g, b, opac;
 };
 
-// One pixel's contribution of one splat, or nothing when ``valid`` is false.
-// Adds w T dL/dC to the colour sums g[6..8] and returns dog = dL/dalpha * g
-// (the geometry gradients are linear in it, see the kernel).  Branch-free:
-// both pixels of a thread are evaluated whenever any lane of the warp is
-// active, so the work is selected with masks instead of branches (an invalid
-// pixel gets alpha = 0, which leaves T and B unchanged and zeroes every term).
-__device__ __forceinline__ float pixel_bwd_step(PixelBwd& s, bool valid, float m, const SplatBwd& c, float* g) {
-    const float gv = splat_falloff(m);
-    const float og = c.opac * gv;
-    const float al = valid ? fminf(og, 0.99f) : 0.f;
-    s.T *= fast_rcp(1.f - al);  // T_i = T_{i+1} / (1 - alpha_i), 1 - alpha_i >= 0.01
-    const float val = fmaf(s.dr, c.r, fmaf(s.dg, c.g, fmaf(s.db, c.b, s.dA)));
-    const float d = val - s.Bv;
-    s.Bv = fmaf(al, d, s.Bv);  // = al * val + (1 - al) * B
-    const float wT = al * s.T;
-    g[6] = fmaf(wT, s.dr, g[6]);
-    g[7] = fmaf(wT, s.dg, g[7]);
-    g[8] = fmaf(wT, s.db, g[8]);
+// Backward state of a pixel pair (lanes .x / .y: rows r and r + 4 of a column).
+struct PairBwd {
+    float2 T, dr, dg, db, dA, Bv;
+    int last0, last1;
+};
+
+// One splat's step for a pixel pair; v0 / v1 say whether each pixel takes
+// part.  Adds w T dL/dC to the colour sums and dog = dL/dalpha * g (the
+// geometry gradients are linear in it, see the kernel) with its y moments to
+// the pair sums.  Branch-free: a pixel that does not take part gets alpha = 0,
+// which leaves T and B unchanged and zeroes every term.
+__device__ __forceinline__ void pair_bwd_step(PairBwd& s, bool v0, bool v1, float2 m, float2 y, const SplatBwd& c,
+                                              float2& sd, float2& sy, float2& syy, float2& sr, float2& sg,
+                                              float2& sb) {
+    const float2 gv = pair_falloff(m);
+    const float2 og = __fmul2_rn(f2(c.opac), gv);
+    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+    const float2 oma = __ffma2_rn(al, f2(-1.f), f2(1.f));  // 1 - alpha >= 0.01
+    s.T = __fmul2_rn(s.T, make_float2(fast_rcp(oma.x), fast_rcp(oma.y)));  // T_i = T_{i+1} / (1 - alpha_i)
+    const float2 val = __ffma2_rn(s.dr, f2(c.r), __ffma2_rn(s.dg, f2(c.g), __ffma2_rn(s.db, f2(c.b), s.dA)));
+    const float2 d = __ffma2_rn(s.Bv, f2(-1.f), val);  // val - B
+    s.Bv = __ffma2_rn(al, d, s.Bv);                     // = al * val + (1 - al) * B
+    const float2 wT = __fmul2_rn(al, s.T);
+    sr = __ffma2_rn(wT, s.dr, sr);
+    sg = __ffma2_rn(wT, s.dg, sg);
+    sb = __ffma2_rn(wT, s.db, sb);
     // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
-    const bool inside = valid && og > 0.f && og < 0.99f;
-    return inside ? s.T * d * gv : 0.f;
+    // (opacity * g > 0 holds for every pixel that takes part: m <= the pair cut)
+    const float2 gi = make_float2(v0 && og.x < 0.99f ? gv.x : 0.f, v1 && og.y < 0.99f ? gv.y : 0.f);
+    const float2 dog = __fmul2_rn(__fmul2_rn(s.T, d), gi);
+    sd = __fadd2_rn(sd, dog);
+    const float2 t = __fmul2_rn(dog, y);
+    sy = __fadd2_rn(sy, t);
+    syy = __ffma2_rn(t, y, syy);
 }
 
-__global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
+// GS_BWD_MIN_CTAS > 0 asks the register allocator for that many resident CTAs per SM
+#if GS_BWD_MIN_CTAS > 0
+#define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads, GS_BWD_MIN_CTAS)
+#else
+#define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads)
+#endif
+__global__ void GS_BWD_BOUNDS render_bwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
@@ -125,16 +148,27 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
 #pragma unroll
         for (int c = 0; c < 9; ++c) acc[j][c] = 0.f;
 
-    PixelBwd s[kPx];
-    float py[kPx];
+    PairBwd s[kPairs];
+    float2 py[kPairs];
     int mylast = 0;
 #pragma unroll
-    for (int k = 0; k < kPx; ++k) {
-        const int pj = by0 + (lane >> 3) + 4 * k;
-        py[k] = (float)pj * p.sy + p.hsy;
-        pixel_bwd_init(s[k], pi < p.rw && pj < p.rh, (int64_t)pj * p.rw + pi, p, out_color, final_T, n_contrib,
+    for (int q = 0; q < kPairs; ++q) {
+        const int pj = by0 + (lane >> 3) + 8 * q;
+        PixelBwd a, b;
+        pixel_bwd_init(a, pi < p.rw && pj < p.rh, (int64_t)pj * p.rw + pi, p, out_color, final_T, n_contrib,
                        loss_mode, target, dL_dcolor, dL_dalpha);
-        mylast = max(mylast, s[k].last);
+        pixel_bwd_init(b, pi < p.rw && pj + 4 < p.rh, (int64_t)(pj + 4) * p.rw + pi, p, out_color, final_T,
+                       n_contrib, loss_mode, target, dL_dcolor, dL_dalpha);
+        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)(pj + 4) * p.sy + p.hsy);
+        s[q].T = make_float2(a.T, b.T);
+        s[q].dr = make_float2(a.dr, b.dr);
+        s[q].dg = make_float2(a.dg, b.dg);
+        s[q].db = make_float2(a.db, b.db);
+        s[q].dA = make_float2(a.dA, b.dA);
+        s[q].Bv = f2(0.f);
+        s[q].last0 = a.last;
+        s[q].last1 = b.last;
+        mylast = max(mylast, max(a.last, b.last));
     }
     if (threadIdx.x == 0) smax = 0;
     __syncthreads();
@@ -175,15 +209,16 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
             const float x = px - q0.x;
             const float ax = q0.z * x, cx = q1.x * x;
-            float y[kPx], m[kPx];
-            bool v[kPx];
+            float2 y[kPairs], m[kPairs];
+            bool v0[kPairs], v1[kPairs];
             bool any = false;
 #pragma unroll
-            for (int r = 0; r < kPx; ++r) {
-                y[r] = py[r] - q0.y;
-                m[r] = x * (ax + q0.w * y[r]) + y[r] * (cx + q1.y * y[r]);
-                v[r] = idx < s[r].last && m[r] <= q2.z;
-                any |= v[r];
+            for (int q = 0; q < kPairs; ++q) {
+                y[q] = __fadd2_rn(py[q], f2(-q0.y));
+                m[q] = pair_quad(y[q], x, ax, cx, q0.w, q1.y);
+                v0[q] = idx < s[q].last0 && m[q].x <= q2.z;
+                v1[q] = idx < s[q].last1 && m[q].y <= q2.z;
+                any |= v0[q] | v1[q];
             }
             if (!__any_sync(kFull, any)) continue;
             // Per thread sums over its pixels (same column offset x):
@@ -191,23 +226,22 @@ __global__ void __launch_bounds__(kRenderThreads) render_bwd_kernel(
             //   g3 = sum dog x y, g4 = sum dog y^2, g6..8 = sum w T dL/dC.
             // With dm = -opacity/2 * dog the splat gradients are linear in these
             // sums; the per-splat factors are applied once, at the flush.
-            float g[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             SplatBwd c;
             c.r = q1.w;
             c.g = q2.x;
             c.b = q2.y;
             c.opac = q1.z;
-            float dsum = 0.f;
+            float2 sd = f2(0.f), sy = f2(0.f), syy = f2(0.f), sr = f2(0.f), sg = f2(0.f), sb = f2(0.f);
 #pragma unroll
-            for (int r = 0; r < kPx; ++r) {
-                const float dog = pixel_bwd_step(s[r], v[r], m[r], c, g);
-                const float t = dog * y[r];
-                dsum += dog;
-                g[1] += t;
-                g[4] = fmaf(t, y[r], g[4]);
-            }
-            g[5] = dsum;
-            g[0] = dsum * x;
+            for (int q = 0; q < kPairs; ++q) pair_bwd_step(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+            float g[9];
+            g[5] = sd.x + sd.y;
+            g[1] = sy.x + sy.y;
+            g[4] = syy.x + syy.y;
+            g[6] = sr.x + sr.y;
+            g[7] = sg.x + sg.y;
+            g[8] = sb.x + sb.y;
+            g[0] = g[5] * x;
             g[2] = g[0] * x;
             g[3] = g[1] * x;
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly

@@ -168,6 +168,9 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
 #ifndef GS_FWD_PX
 #define GS_FWD_PX 2
 #endif
+#ifndef GS_FWD_MIN_CTAS
+#define GS_FWD_MIN_CTAS 8
+#endif
 #ifndef GS_FWD_BATCH
 #define GS_FWD_BATCH 256
 #endif
@@ -175,6 +178,7 @@ constexpr int kPx = GS_FWD_PX;
 static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
 constexpr int kRenderThreads = kTileThreads / kPx;
 constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
+constexpr int kPairs = kPx / 2;          // pixel pairs per thread
 constexpr int kBatch = GS_FWD_BATCH;  // splats staged in shared memory per batch
 static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
 
@@ -240,22 +244,6 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const gs_tile
 // staged kBatch at a time in shared memory and read back as broadcasts; a warp
 // skips the rest of a batch once all its pixels are saturated (T < t_min) and
 // the CTA stops when all 256 are.
-__device__ __forceinline__ void composite_pixel(float m, float4 q1, float4 q2, float& T, float& cr, float& cg,
-                                                float& cb, float& A, int& last, bool& done, int idx1, float t_min) {
-    if (!done && m <= q2.z) {
-        const float gv = splat_falloff(m);
-        const float al = fminf(q1.z * gv, 0.99f);
-        const float w = al * T;
-        cr += w * q1.w;
-        cg += w * q2.x;
-        cb += w * q2.y;
-        A += w;
-        T *= (1.f - al);
-        last = idx1;
-        if (T < t_min) done = true;
-    }
-}
-
 __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, int64_t pix, float cr, float cg,
                                             float cb) {
     if (loss_mode == GS_LOSS_L1_U8) {
@@ -271,7 +259,13 @@ __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, i
     return 0.f;
 }
 
-__global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
+// GS_FWD_MIN_CTAS > 0 asks the register allocator for that many resident CTAs per SM
+#if GS_FWD_MIN_CTAS > 0
+#define GS_FWD_BOUNDS __launch_bounds__(kRenderThreads, GS_FWD_MIN_CTAS)
+#else
+#define GS_FWD_BOUNDS __launch_bounds__(kRenderThreads)
+#endif
+__global__ void GS_FWD_BOUNDS render_fwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, float* __restrict__ out_color, float* __restrict__ out_alpha, float* __restrict__ final_T,
     int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
@@ -287,19 +281,21 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
     const float px = (float)pi * p.sx + p.hsx;
     const gs_tile_range rg = ranges[tile];
 
-    float py[kPx], T[kPx], cr[kPx], cg[kPx], cb[kPx], A[kPx];
+    // pixel pairs: pair q holds rows (lane >> 3) + 8 q and (lane >> 3) + 8 q + 4
+    float2 py[kPairs], T[kPairs], cr[kPairs], cg[kPairs], cb[kPairs], A[kPairs];
     int last[kPx];
     bool done[kPx];
     bool all_done = true;
 #pragma unroll
-    for (int k = 0; k < kPx; ++k) {
-        const int pj = by0 + (lane >> 3) + 4 * k;
-        py[k] = (float)pj * p.sy + p.hsy;
-        T[k] = 1.f;
-        cr[k] = cg[k] = cb[k] = A[k] = 0.f;
-        last[k] = 0;
-        done[k] = !(pi < p.rw && pj < p.rh);
-        all_done &= done[k];
+    for (int q = 0; q < kPairs; ++q) {
+        const int pj = by0 + (lane >> 3) + 8 * q;
+        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)(pj + 4) * p.sy + p.hsy);
+        T[q] = f2(1.f);
+        cr[q] = cg[q] = cb[q] = A[q] = f2(0.f);
+        last[2 * q] = last[2 * q + 1] = 0;
+        done[2 * q] = !(pi < p.rw && pj < p.rh);
+        done[2 * q + 1] = !(pi < p.rw && pj + 4 < p.rh);
+        all_done &= done[2 * q] & done[2 * q + 1];
     }
     for (int b = rg.start; b < rg.end; b += kBatch) {
         if (__syncthreads_count(all_done) == kRenderThreads) break;
@@ -337,14 +333,31 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
                 const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
                 const float x = px - q0.x;
                 const float ax = q0.z * x, cx = q1.x * x;
+                const int idx1 = base1 + k;
                 all_done = true;
 #pragma unroll
-                for (int r = 0; r < kPx; ++r) {
-                    const float y = py[r] - q0.y;
-                    const float m = x * (ax + q0.w * y) + y * (cx + q1.y * y);
-                    composite_pixel(m, q1, q2, T[r], cr[r], cg[r], cb[r], A[r], last[r], done[r], base1 + k,
-                                    p.t_min);
-                    all_done &= done[r];
+                for (int q = 0; q < kPairs; ++q) {
+                    // Branch-free front-to-back step: a pixel that is done or
+                    // out of the splat's reach gets alpha = 0 (T, colour unchanged).
+                    const float2 m = pair_quad(__fadd2_rn(py[q], f2(-q0.y)), x, ax, cx, q0.w, q1.y);
+                    const float2 og = __fmul2_rn(f2(q1.z), pair_falloff(m));
+                    const bool v0 = !done[2 * q] && m.x <= q2.z, v1 = !done[2 * q + 1] && m.y <= q2.z;
+                    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+                    const float2 w = __fmul2_rn(al, T[q]);
+                    cr[q] = __ffma2_rn(w, f2(q1.w), cr[q]);
+                    cg[q] = __ffma2_rn(w, f2(q2.x), cg[q]);
+                    cb[q] = __ffma2_rn(w, f2(q2.y), cb[q]);
+                    A[q] = __fadd2_rn(A[q], w);
+                    T[q] = __fmul2_rn(T[q], __ffma2_rn(al, f2(-1.f), f2(1.f)));  // T (1 - alpha)
+                    if (v0) {
+                        last[2 * q] = idx1;
+                        done[2 * q] = T[q].x < p.t_min;
+                    }
+                    if (v1) {
+                        last[2 * q + 1] = idx1;
+                        done[2 * q + 1] = T[q].y < p.t_min;
+                    }
+                    all_done &= done[2 * q] & done[2 * q + 1];
                 }
                 warp_done = __all_sync(kFull, all_done);
             }
@@ -356,15 +369,18 @@ __global__ void __launch_bounds__(kRenderThreads) render_fwd_kernel(
 #pragma unroll
     for (int k = 0; k < kPx; ++k) {
         const int pj = by0 + (lane >> 3) + 4 * k;
+        const int q = k >> 1;
+        const bool hi = k & 1;
         if (pi < p.rw && pj < p.rh) {
             const int64_t pix = (int64_t)pj * p.rw + pi;
-            out_color[3 * pix + 0] = cr[k];
-            out_color[3 * pix + 1] = cg[k];
-            out_color[3 * pix + 2] = cb[k];
-            out_alpha[pix] = A[k];
-            final_T[pix] = T[k];
+            const float r = hi ? cr[q].y : cr[q].x, g = hi ? cg[q].y : cg[q].x, bl = hi ? cb[q].y : cb[q].x;
+            out_color[3 * pix + 0] = r;
+            out_color[3 * pix + 1] = g;
+            out_color[3 * pix + 2] = bl;
+            out_alpha[pix] = hi ? A[q].y : A[q].x;
+            final_T[pix] = hi ? T[q].y : T[q].x;
             n_contrib[pix] = last[k];
-            lsum += pixel_loss(loss_mode, target, pix, cr[k], cg[k], cb[k]);
+            lsum += pixel_loss(loss_mode, target, pix, r, g, bl);
         }
     }
     if (loss_mode != GS_LOSS_NONE) {
