@@ -182,6 +182,26 @@ __device__ __forceinline__ float fast_rcp(float x) {
     return y;
 }
 
+// ------------------------------------------------------------------ compositing layout
+// One CTA per 16x16 tile; each thread owns P pixels of one column, row_step
+// rows apart, so warp w covers a cols-wide, rows-tall block of the tile
+// (8 x 8 for P = 2, 8 x 16 for P = 4, the whole tile for P = 8).  A thread's
+// pixels are taken two at a time (pair q: its pixels 2q and 2q + 1).
+template <int P>
+struct CompositeLayout {
+    static_assert(P == 2 || P == 4 || P == 8, "compositing pixels per thread must be 2, 4 or 8");
+    static constexpr int threads = kTileThreads / P;
+    static constexpr int cols = P == 8 ? 16 : 8;
+    static constexpr int row_step = 32 / cols;
+    static constexpr int rows = row_step * P;
+    static constexpr int blocks_x = kTile / cols;
+    static constexpr int pairs = P / 2;
+    __device__ static int block_x(int warp) { return (warp % blocks_x) * cols; }
+    __device__ static int block_y(int warp) { return (warp / blocks_x) * rows; }
+    __device__ static int col(int lane) { return lane % cols; }
+    __device__ static int row(int lane, int k) { return lane / cols + row_step * k; }  // row of pixel k
+};
+
 // ------------------------------------------------------------------ pixel pairs
 // The compositing kernels evaluate two pixels of one column together with the
 // sm_100 paired fp32 instructions (one issue slot for two round-to-nearest

@@ -5,8 +5,7 @@
 
 namespace gs {
 
-// Compositing layout: one CTA per 16x16 tile; each thread owns kPx pixels of
-// one column, 4 rows apart, so a warp covers an 8-wide, 4 * kPx-tall block.
+// Compositing layout (CompositeLayout): pixels per thread, batch and register budget.
 #ifndef GS_BWD_PX
 #define GS_BWD_PX 4
 #endif
@@ -16,11 +15,10 @@ namespace gs {
 #ifndef GS_BWD_BATCH
 #define GS_BWD_BATCH 128
 #endif
+using Layout = CompositeLayout<GS_BWD_PX>;
 constexpr int kPx = GS_BWD_PX;
-static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
-constexpr int kRenderThreads = kTileThreads / kPx;
-constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
-constexpr int kPairs = kPx / 2;          // pixel pairs per thread
+constexpr int kRenderThreads = Layout::threads;
+constexpr int kPairs = Layout::pairs;
 constexpr int kBatch = GS_BWD_BATCH;  // splats staged in shared memory per batch
 static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
 
@@ -85,7 +83,7 @@ struct SplatBwd {
     float r, g, b, opac;
 };
 
-// Backward state of a pixel pair (lanes .x / .y: rows r and r + 4 of a column).
+// Backward state of a pixel pair (lanes .x / .y: a thread's pixels 2q and 2q + 1).
 struct PairBwd {
     float2 T, dr, dg, db, dA, Bv;
     int last0, last1;
@@ -140,8 +138,8 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
     if (tile < 0 || tile >= p.tiles_x * p.tiles_y) return;  // uniform over the CTA
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * kBlockRows;  // this warp's block
-    const int pi = bx0 + (lane & 7);
+    const int bx0 = tx * kTile + Layout::block_x(warp), by0 = ty * kTile + Layout::block_y(warp);  // warp block
+    const int pi = bx0 + Layout::col(lane);
     const float px = (float)pi * p.sx + p.hsx;
     const gs_tile_range rg = ranges[tile];
     for (int j = threadIdx.x; j < kBatch; j += kRenderThreads)
@@ -153,13 +151,13 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
     int mylast = 0;
 #pragma unroll
     for (int q = 0; q < kPairs; ++q) {
-        const int pj = by0 + (lane >> 3) + 8 * q;
+        const int pj = by0 + Layout::row(lane, 2 * q), pj1 = by0 + Layout::row(lane, 2 * q + 1);
         PixelBwd a, b;
         pixel_bwd_init(a, pi < p.rw && pj < p.rh, (int64_t)pj * p.rw + pi, p, out_color, final_T, n_contrib,
                        loss_mode, target, dL_dcolor, dL_dalpha);
-        pixel_bwd_init(b, pi < p.rw && pj + 4 < p.rh, (int64_t)(pj + 4) * p.rw + pi, p, out_color, final_T,
-                       n_contrib, loss_mode, target, dL_dcolor, dL_dalpha);
-        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)(pj + 4) * p.sy + p.hsy);
+        pixel_bwd_init(b, pi < p.rw && pj1 < p.rh, (int64_t)pj1 * p.rw + pi, p, out_color, final_T, n_contrib,
+                       loss_mode, target, dL_dcolor, dL_dalpha);
+        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)pj1 * p.sy + p.hsy);
         s[q].T = make_float2(a.T, b.T);
         s[q].dr = make_float2(a.dr, b.dr);
         s[q].dg = make_float2(a.dg, b.dg);
@@ -195,7 +193,8 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
         for (int i = 0; i < kBatch / 32; ++i) {
             const int k = 32 * i + lane;
             const bool h =
-                k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + kBlockRows - 1, p);
+                k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + Layout::cols - 1, by0,
+                                            by0 + Layout::rows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
 #pragma unroll

@@ -163,8 +163,7 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
     if (i == n - 1 || keys[i + 1] != t) ranges[t].end = (int32_t)(i + 1);
 }
 
-// Compositing layout: one CTA per 16x16 tile; each thread owns kPx pixels of
-// one column, 4 rows apart, so a warp covers an 8-wide, 4 * kPx-tall block.
+// Compositing layout (CompositeLayout): pixels per thread, batch and register budget.
 #ifndef GS_FWD_PX
 #define GS_FWD_PX 2
 #endif
@@ -174,11 +173,10 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n,
 #ifndef GS_FWD_BATCH
 #define GS_FWD_BATCH 256
 #endif
+using Layout = CompositeLayout<GS_FWD_PX>;
 constexpr int kPx = GS_FWD_PX;
-static_assert(kPx == 2 || kPx == 4, "compositing pixels per thread must be 2 or 4");
-constexpr int kRenderThreads = kTileThreads / kPx;
-constexpr int kBlockRows = 4 * kPx;      // rows of a warp's pixel block
-constexpr int kPairs = kPx / 2;          // pixel pairs per thread
+constexpr int kRenderThreads = Layout::threads;
+constexpr int kPairs = Layout::pairs;
 constexpr int kBatch = GS_FWD_BATCH;  // splats staged in shared memory per batch
 static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
 
@@ -238,12 +236,11 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(const gs_tile
 }
 
 // ---------------------------------------------------------------- compositing
-// One CTA per 16x16 tile; each thread owns kPx pixels of one column, 4 rows
-// apart.  Warp w owns the 8 x kBlockRows block ((w & 1) * 8, (w >> 1) *
-// kBlockRows): lane l has column l & 7 and rows (l >> 3) + 4 k.  Splats are
-// staged kBatch at a time in shared memory and read back as broadcasts; a warp
-// skips the rest of a batch once all its pixels are saturated (T < t_min) and
-// the CTA stops when all 256 are.
+// One CTA per 16x16 tile, pixels laid out by CompositeLayout.  Splats are
+// staged kBatch at a time in shared memory and read back as broadcasts; each
+// warp first tests which staged splats can reach its pixel block, then walks
+// only those.  A warp skips the rest of a batch once all its pixels are
+// saturated (T < t_min) and the CTA stops when all 256 are.
 __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, int64_t pix, float cr, float cg,
                                             float cb) {
     if (loss_mode == GS_LOSS_L1_U8) {
@@ -276,25 +273,25 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     if (tile < 0 || tile >= p.tiles_x * p.tiles_y) return;  // uniform over the CTA
     const int tx = tile % p.tiles_x, ty = tile / p.tiles_x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bx0 = tx * kTile + (warp & 1) * 8, by0 = ty * kTile + (warp >> 1) * kBlockRows;  // this warp's block
-    const int pi = bx0 + (lane & 7);
+    const int bx0 = tx * kTile + Layout::block_x(warp), by0 = ty * kTile + Layout::block_y(warp);  // warp block
+    const int pi = bx0 + Layout::col(lane);
     const float px = (float)pi * p.sx + p.hsx;
     const gs_tile_range rg = ranges[tile];
 
-    // pixel pairs: pair q holds rows (lane >> 3) + 8 q and (lane >> 3) + 8 q + 4
+    // pixel pairs: pair q holds the thread's pixels 2q and 2q + 1
     float2 py[kPairs], T[kPairs], cr[kPairs], cg[kPairs], cb[kPairs], A[kPairs];
     int last[kPx];
     bool done[kPx];
     bool all_done = true;
 #pragma unroll
     for (int q = 0; q < kPairs; ++q) {
-        const int pj = by0 + (lane >> 3) + 8 * q;
-        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)(pj + 4) * p.sy + p.hsy);
+        const int pj = by0 + Layout::row(lane, 2 * q), pj1 = by0 + Layout::row(lane, 2 * q + 1);
+        py[q] = make_float2((float)pj * p.sy + p.hsy, (float)pj1 * p.sy + p.hsy);
         T[q] = f2(1.f);
         cr[q] = cg[q] = cb[q] = A[q] = f2(0.f);
         last[2 * q] = last[2 * q + 1] = 0;
         done[2 * q] = !(pi < p.rw && pj < p.rh);
-        done[2 * q + 1] = !(pi < p.rw && pj + 4 < p.rh);
+        done[2 * q + 1] = !(pi < p.rw && pj1 < p.rh);
         all_done &= done[2 * q] & done[2 * q + 1];
     }
     for (int b = rg.start; b < rg.end; b += kBatch) {
@@ -321,7 +318,8 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
         for (int i = 0; i < kBatch / 32; ++i) {
             const int k = 32 * i + lane;
             const bool h = !warp_done && k < cnt &&
-                           splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + 7, by0, by0 + kBlockRows - 1, p);
+                           splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + Layout::cols - 1, by0,
+                                            by0 + Layout::rows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
 #pragma unroll
@@ -368,7 +366,7 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     float lsum = 0.f;
 #pragma unroll
     for (int k = 0; k < kPx; ++k) {
-        const int pj = by0 + (lane >> 3) + 4 * k;
+        const int pj = by0 + Layout::row(lane, k);
         const int q = k >> 1;
         const bool hi = k & 1;
         if (pi < p.rw && pj < p.rh) {
