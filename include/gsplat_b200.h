@@ -119,6 +119,7 @@ int gs_clear_buffer_cache(void);
 
 #define GS_ADAM_FUSED 0 /* the Metal kernel's semantics (scrub + clamp, float32 bias corrections) */
 #define GS_ADAM_PURE 1  /* mlx_gsplat/optimizer.py:146-175: lr_scale, float64 bias corrections, no scrub/clamp */
+#define GS_ADAM_EXACT 0x100 /* OR into gs_fused_adam_slab's mode: IEEE-rounded sqrt and division in the step */
 
 /* One parameter group with explicit row strides (pools whose rows are views
  * into a wider slab).  ``grad_scale`` multiplies g first (1/world_size after
@@ -142,7 +143,13 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
  * When ``visible_words`` is given (bit r of word r/32 set = row r was seen
  * this step, the bitmask gs_cull leaves in its scratch), a row whose bit is
  * clear does not read g: its gradient is the host row ``unseen_grad_host``
- * (ncols floats), so the caller needs no gradient rows for unseen Gaussians. */
+ * (ncols floats), so the caller needs no gradient rows for unseen Gaussians.
+ * Rounding: m and v are always rounded exactly as the per-element update
+ * (gs_fused_adam_group) rounds them.  The step m / (sqrt(v) / sqrt(bc2) + eps)
+ * uses the hardware approximate square root and reciprocal (a few ulp of the
+ * step, relative error below 1e-6) unless ``mode`` has GS_ADAM_EXACT, which
+ * makes every operation IEEE round-to-nearest (bit-identical to
+ * gs_fused_adam_group, at a higher instruction cost). */
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,

@@ -15,7 +15,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libgsplat_b200.so")
 
 GS_OK, GS_ERR_INVALID, GS_ERR_CUDA, GS_ERR_CAPACITY = 0, 1, 2, 3
-GS_ADAM_FUSED, GS_ADAM_PURE = 0, 1
+GS_ADAM_FUSED, GS_ADAM_PURE, GS_ADAM_EXACT = 0, 1, 0x100
 GS_LOSS_NONE, GS_LOSS_L1_U8, GS_LOSS_L1_F32, GS_LOSS_MEAN = 0, 1, 2, 3
 
 c_float_p = ctypes.POINTER(ctypes.c_float)

@@ -16,6 +16,7 @@ namespace gs {
 struct AdamScalars {
     float b1, b2, omb1, omb2;  // beta, (1 - beta) as the selected semantics round them
     float eps, wd, sqrt_bc2, grad_scale;
+    float inv_sqrt_bc2;        // 1 / sqrt(1 - beta2^t) for the approximate step
     int scrub, clamp;
 };
 
@@ -43,6 +44,50 @@ __device__ __forceinline__ void adam_elem(float& th, float& m, float& v, float g
     if (s.scrub && !isfinite(delta)) delta = 0.0f;
     float t = __fsub_rn(th, delta);
     if (s.clamp) t = fminf(fmaxf(t, lo), hi);
+    th = t;
+    m = mn;
+    v = vn;
+}
+
+// The same update with the moments rounded exactly as above and the step
+// formed with the hardware square root and reciprocal (sqrt.approx,
+// rcp.approx: a few ulp on the step, none on m and v) and without branches.
+// kFused selects the fused kernel's scrub-and-clamp semantics.
+__device__ __forceinline__ float approx_sqrt(float x) {
+    float y;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float approx_rcp(float x) {
+    float y;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float approx_rsqrt(float x) {
+    float y;
+    asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <bool kFused>
+__device__ __forceinline__ void adam_elem_fast(float& th, float& m, float& v, float g, const AdamScalars& s,
+                                               float step_size, float lo, float hi) {
+    g = __fmul_rn(g, s.grad_scale);
+    if (kFused) g = isnan(g) ? 0.0f : g;
+    if (s.wd != 0.0f) g = __fadd_rn(g, __fmul_rn(s.wd, th));
+    float mn = __fadd_rn(__fmul_rn(s.b1, m), __fmul_rn(s.omb1, g));
+    float vn = __fadd_rn(__fmul_rn(s.b2, v), __fmul_rn(s.omb2, __fmul_rn(g, g)));
+    if (kFused) {
+        mn = isfinite(mn) ? mn : 0.0f;
+        vn = isfinite(vn) ? vn : 0.0f;
+    }
+    const float denom = fmaf(approx_sqrt(vn), s.inv_sqrt_bc2, s.eps);
+    float delta = step_size * (mn * approx_rcp(denom));
+    if (kFused) delta = isfinite(delta) ? delta : 0.0f;
+    float t = th - delta;
+    if (kFused) t = fminf(fmaxf(t, lo), hi);
     th = t;
     m = mn;
     v = vn;
@@ -76,13 +121,36 @@ struct __align__(16) ColsSmem {
     float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols];
 };
 
+template <bool kExact, bool kFused>
+__device__ __forceinline__ void slab_elem(float& th, float& m, float& v, float g, int c, int ncols,
+                                          const AdamScalars& s, const ColsSmem& cs) {
+    if (kExact) {
+        if (c < ncols) adam_elem(th, m, v, g, s, cs.step[c], cs.lo[c], cs.hi[c]);
+    } else {
+        // padding columns are computed and then discarded (no branch)
+        float t = th, mn = m, vn = v;
+        adam_elem_fast<kFused>(t, mn, vn, g, s, cs.step[c], cs.lo[c], cs.hi[c]);
+        const bool on = c < ncols;
+        th = on ? t : th;
+        m = on ? mn : m;
+        v = on ? vn : v;
+    }
+}
+
+template <bool kExact, bool kFused>
 __device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, const float4& gg, int c0, int ncols,
                                             bool renorm, const AdamScalars& s, const ColsSmem& cs) {
-    if (c0 + 0 < ncols) adam_elem(th.x, mm.x, vv.x, gg.x, s, cs.step[c0 + 0], cs.lo[c0 + 0], cs.hi[c0 + 0]);
-    if (c0 + 1 < ncols) adam_elem(th.y, mm.y, vv.y, gg.y, s, cs.step[c0 + 1], cs.lo[c0 + 1], cs.hi[c0 + 1]);
-    if (c0 + 2 < ncols) adam_elem(th.z, mm.z, vv.z, gg.z, s, cs.step[c0 + 2], cs.lo[c0 + 2], cs.hi[c0 + 2]);
-    if (c0 + 3 < ncols) adam_elem(th.w, mm.w, vv.w, gg.w, s, cs.step[c0 + 3], cs.lo[c0 + 3], cs.hi[c0 + 3]);
-    if (renorm) {
+    slab_elem<kExact, kFused>(th.x, mm.x, vv.x, gg.x, c0 + 0, ncols, s, cs);
+    slab_elem<kExact, kFused>(th.y, mm.y, vv.y, gg.y, c0 + 1, ncols, s, cs);
+    slab_elem<kExact, kFused>(th.z, mm.z, vv.z, gg.z, c0 + 2, ncols, s, cs);
+    slab_elem<kExact, kFused>(th.w, mm.w, vv.w, gg.w, c0 + 3, ncols, s, cs);
+    if (!kExact && renorm) {
+        const float r = approx_rsqrt(th.x * th.x + th.y * th.y + th.z * th.z + th.w * th.w + 1e-8f);
+        th.x *= r;
+        th.y *= r;
+        th.z *= r;
+        th.w *= r;
+    } else if (renorm) {
         float ss = __fmul_rn(th.x, th.x);
         ss = __fadd_rn(ss, __fmul_rn(th.y, th.y));
         ss = __fadd_rn(ss, __fmul_rn(th.z, th.z));
@@ -95,6 +163,7 @@ __device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, 
     }
 }
 
+template <bool kExact, bool kFused>
 __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
                                                         float4* __restrict__ m, float4* __restrict__ v,
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
@@ -144,13 +213,13 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
     if (gb_seen) gb = __ldcs(g + rb * g_chunks + c4);
     const bool renorm = c4 == quat_chunk;
     if (va) {
-        slab_update(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
+        slab_update<kExact, kFused>(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
         __stcs(theta + offa, tha);
         __stcs(m + offa, ma);
         __stcs(v + offa, vva);
     }
     if (vb) {
-        slab_update(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cs);
+        slab_update<kExact, kFused>(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cs);
         __stcs(theta + offb, thb);
         __stcs(m + offb, mb);
         __stcs(v + offb, vvb);
@@ -177,6 +246,7 @@ static AdamScalars make_scalars(int mode, double beta1, double beta2, float eps,
         const float bc1 = 1.0f - powf(b1, (float)step);
         const float bc2 = 1.0f - powf(b2, (float)step);
         s.sqrt_bc2 = sqrtf(bc2);
+        s.inv_sqrt_bc2 = 1.0f / s.sqrt_bc2;
         *bc1_out = bc1;
         s.scrub = 1;
         s.clamp = 1;
@@ -186,6 +256,7 @@ static AdamScalars make_scalars(int mode, double beta1, double beta2, float eps,
         const double bc1 = 1.0 - pow(beta1, (double)step);
         const double bc2 = 1.0 - pow(beta2, (double)step);
         s.sqrt_bc2 = (float)sqrt(bc2);
+        s.inv_sqrt_bc2 = (float)(1.0 / sqrt(bc2));
         *bc1_out = bc1;
         s.scrub = 0;
         s.clamp = 0;
@@ -227,6 +298,8 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                                   float grad_scale, int mode, const uint32_t* visible_words,
                                   const float* unseen_grad_host, gs_stream_t stream) {
+    const bool exact = (mode & GS_ADAM_EXACT) != 0;
+    mode &= ~GS_ADAM_EXACT;
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
     GS_REQUIRE(!visible_words || unseen_grad_host, "adam_slab: visible_words needs unseen_grad_host");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
@@ -254,7 +327,9 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
     // multiple of 256, hence of 2^shift) after the first
     const int64_t n = num_active << shift;
     const int64_t half = (n + 511) / 512 * 256;
-    adam_slab_kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
+    auto kernel = exact ? (mode == GS_ADAM_FUSED ? adam_slab_kernel<true, true> : adam_slab_kernel<true, false>)
+                        : (mode == GS_ADAM_FUSED ? adam_slab_kernel<false, true> : adam_slab_kernel<false, false>);
+    kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
         quat_col < 0 ? -1 : quat_col / 4, half, visible_words, s, cols);
@@ -278,8 +353,8 @@ extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, u
             hi[c] = a_max;
         }
         return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
-                                  beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED, nullptr, nullptr,
-                                  stream);
+                                  beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED | GS_ADAM_EXACT,
+                                  nullptr, nullptr, stream);
     }
     return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
                                weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);

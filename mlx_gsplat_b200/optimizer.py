@@ -106,11 +106,12 @@ class FusedMLXAdam:
     def step_slab(self, theta: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
                   table: torch.Tensor, num_active: int, ncols: int, col_lo, col_hi, quat_col: int = -1,
                   grad_scale: float = 1.0, pure: bool = False, col_lr_scale=None, visible_words: Optional[int] = None,
-                  unseen_grad=None) -> None:
+                  unseen_grad=None, exact: bool = False) -> None:
         """One launch over every group of a ``[max, stride]`` slab (fused semantics).
         With ``visible_words`` (device address of the cull's visibility bitmask) rows
         the bitmask marks unseen take ``unseen_grad`` (ncols floats) as their gradient
-        instead of reading ``g``."""
+        instead of reading ``g``.  The step uses the hardware approximate square
+        root and reciprocal (relative error below 1e-6) unless ``exact``."""
         self.t += 1
         lib = _lib.lib()
         _lib.check(lib.gs_fused_adam_slab(theta.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(),
@@ -118,6 +119,7 @@ class FusedMLXAdam:
                                           _lib.fptr(col_lo), _lib.fptr(col_hi),
                                           None if col_lr_scale is None else _lib.fptr(col_lr_scale), quat_col,
                                           self.lr, self.beta1, self.beta2, self.eps, self.weight_decay, self.t,
-                                          grad_scale, _lib.GS_ADAM_PURE if pure else _lib.GS_ADAM_FUSED,
+                                          grad_scale, (_lib.GS_ADAM_PURE if pure else _lib.GS_ADAM_FUSED) |
+                                          (_lib.GS_ADAM_EXACT if exact else 0),
                                           visible_words, None if unseen_grad is None else _lib.fptr(unseen_grad),
                                           _lib.stream_ptr(theta.device)), "fused adam (slab)")

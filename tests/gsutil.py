@@ -38,3 +38,19 @@ def assert_adam_close(got, ref, rtol=ADAM_RTOL, what="adam"):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     np.testing.assert_allclose(got, ref, rtol=rtol, atol=1e-30, err_msg=what)
+
+
+def assert_adam_update_close(got, ref, before, rtol=ADAM_RTOL, what="adam"):
+    """Adam-updated parameters whose step was formed with the hardware
+    approximate square root and reciprocal: within ``rtol`` of the parameter
+    plus ``rtol`` of the step the oracle took (|before - ref|), so that a
+    parameter the step moves close to zero is judged against the step."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    before = np.asarray(before, np.float64)
+    tol = rtol * (np.abs(ref) + np.abs(before - ref))
+    err = np.abs(got - ref)
+    bad = ~(err <= tol)
+    assert not bad.any(), (f"{what}: {int(bad.sum())} elements out of tolerance; worst excess "
+                           f"{(err - tol)[bad].max():.3g}")
+

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from gsutil import assert_adam_close, assert_grad_close
+from gsutil import assert_adam_update_close, assert_grad_close
 from mlx_gsplat_b200 import synthetic
 from mlx_gsplat_b200.trainer import runner_for_workload, sh_cols_for
 from oracle import adam as oadam
@@ -64,7 +64,7 @@ def test_train_step_matches_oracle(wl_name, n):
                             beta1=0.9, beta2=0.999, eps=1e-15, weight_decay=0.0, step=1, a_min=lo, a_max=hi)
         if k == "quats":
             th[table] = odens.quat_renorm(th[table])
-        assert_adam_close(after[:, o:o + dd], th, what="adam " + k)
+        assert_adam_update_close(after[:, o:o + dd], th, theta0[:, o:o + dd], what="adam " + k)
 
 
 def test_unseen_rows_from_visibility_bits_match_dense_rows():
