@@ -67,13 +67,67 @@ __device__ __forceinline__ int64_t param_row(const gs_gaussians& g, int32_t id) 
     return g.table ? (int64_t)__ldg(g.table + id) : (int64_t)id;
 }
 
-// rendering.py:153-244 for one Gaussian.  ``cols`` points at its colour row.
-__device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, const float* cols,
-                                            const RasterParams& p, ProjState& s) {
-    const float* mp = g.means + row * g.means_stride;
-    s.mx = __ldg(mp + 0);
-    s.my = __ldg(mp + 1);
-    s.mz = __ldg(mp + 2);
+// The parameters the projection reads for one Gaussian.
+struct GaussianIn {
+    float mx, my, mz;
+    float qw, qx, qy, qz;
+    float ls[3];    // log-scales
+    float logit;    // opacity logit
+    float col[12];  // SH degree 0 (3) and, with colors_dim >= 12, degree 1 (9)
+};
+
+// The pooled row layout, one row per Gaussian: quats (0-3) | means (4-6) |
+// opacity (7) | scales (8-10) | colours (11-).  When a descriptor's pointers
+// describe exactly that (equal strides that are a multiple of 4 floats,
+// 16-byte-aligned rows, colours addressed by row) a row is moved with 16-byte
+// vector accesses instead of one scalar access per value.
+constexpr int kRowMean = 4, kRowOpac = 7, kRowScale = 8, kRowColor = 11;
+
+inline bool slab_rows(const gs_gaussians& g) {
+    const int64_t S = g.quats_stride;
+    const int need = kRowColor + (g.colors_dim >= 12 ? 12 : 3);
+    return g.quats && g.colors_by_visible == 0 && S % 4 == 0 && S >= (need + 3) / 4 * 4 && g.means_stride == S &&
+           g.scales_stride == S && g.opac_stride == S && g.colors_stride == S && g.means == g.quats + kRowMean &&
+           g.opac == g.quats + kRowOpac && g.scales == g.quats + kRowScale && g.colors == g.quats + kRowColor &&
+           (reinterpret_cast<uintptr_t>(g.quats) & 15u) == 0;
+}
+
+template <bool kSlab>
+__device__ __forceinline__ void load_gaussian(const gs_gaussians& g, int64_t row, int64_t crow, GaussianIn& in) {
+    const bool sh1 = g.colors_dim >= 12;
+    if (kSlab) {
+        const float4* r = reinterpret_cast<const float4*>(g.quats + row * g.quats_stride);
+        const float4 a = __ldg(r), b = __ldg(r + 1), c = __ldg(r + 2), d = __ldg(r + 3);
+        in.qw = a.x, in.qx = a.y, in.qy = a.z, in.qz = a.w;
+        in.mx = b.x, in.my = b.y, in.mz = b.z, in.logit = b.w;
+        in.ls[0] = c.x, in.ls[1] = c.y, in.ls[2] = c.z;
+        in.col[0] = c.w, in.col[1] = d.x, in.col[2] = d.y;
+        if (sh1) {
+            const float4 e = __ldg(r + 4), f = __ldg(r + 5);
+            in.col[3] = d.z, in.col[4] = d.w;
+            in.col[5] = e.x, in.col[6] = e.y, in.col[7] = e.z, in.col[8] = e.w;
+            in.col[9] = f.x, in.col[10] = f.y, in.col[11] = f.z;
+        }
+    } else {
+        const float* mp = g.means + row * g.means_stride;
+        const float* qp = g.quats + row * g.quats_stride;
+        const float* sp = g.scales + row * g.scales_stride;
+        const float* cp = g.colors + crow * g.colors_stride;
+        in.mx = __ldg(mp), in.my = __ldg(mp + 1), in.mz = __ldg(mp + 2);
+        in.qw = __ldg(qp), in.qx = __ldg(qp + 1), in.qy = __ldg(qp + 2), in.qz = __ldg(qp + 3);
+        in.ls[0] = __ldg(sp), in.ls[1] = __ldg(sp + 1), in.ls[2] = __ldg(sp + 2);
+        in.logit = __ldg(g.opac + row * g.opac_stride);
+        const int nc = sh1 ? 12 : 3;
+#pragma unroll
+        for (int k = 0; k < 12; ++k) in.col[k] = k < nc ? __ldg(cp + k) : 0.f;
+    }
+}
+
+// rendering.py:153-244 for one Gaussian.
+__device__ __forceinline__ void project_one(const GaussianIn& in, bool sh1, const RasterParams& p, ProjState& s) {
+    s.mx = in.mx;
+    s.my = in.my;
+    s.mz = in.mz;
     s.tx = cam_row(p.vm, 0, s.mx, s.my, s.mz);
     s.ty = cam_row(p.vm, 1, s.mx, s.my, s.mz);
     s.tz = cam_row(p.vm, 2, s.mx, s.my, s.mz);
@@ -81,11 +135,10 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     s.u = __fadd_rn(__fdiv_rn(__fmul_rn(s.tx, p.fx), s.z), p.cx);
     s.v = __fadd_rn(__fdiv_rn(__fmul_rn(s.ty, p.fy), s.z), p.cy);
 
-    const float* qp = g.quats + row * g.quats_stride;
-    s.qw = __ldg(qp + 0);
-    s.qx = __ldg(qp + 1);
-    s.qy = __ldg(qp + 2);
-    s.qz = __ldg(qp + 3);
+    s.qw = in.qw;
+    s.qx = in.qx;
+    s.qy = in.qy;
+    s.qz = in.qz;
     s.qn = sqrtf(s.qw * s.qw + s.qx * s.qx + s.qy * s.qy + s.qz * s.qz + 1e-8f);
     const float r = s.qw / s.qn, x = s.qx / s.qn, y = s.qy / s.qn, z = s.qz / s.qn;
     s.R[0] = 1.f - 2.f * (y * y + z * z);
@@ -98,10 +151,9 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     s.R[7] = 2.f * (y * z + r * x);
     s.R[8] = 1.f - 2.f * (x * x + y * y);
 
-    const float* sp = g.scales + row * g.scales_stride;
-    s.S[0] = expf(__ldg(sp + 0));
-    s.S[1] = expf(__ldg(sp + 1));
-    s.S[2] = expf(__ldg(sp + 2));
+    s.S[0] = expf(in.ls[0]);
+    s.S[1] = expf(in.ls[1]);
+    s.S[2] = expf(in.ls[2]);
     float M[9];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
@@ -140,8 +192,7 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     s.cc = -s.c / s.det;
     s.cd = s.a / s.det;
 
-    const float logit = __ldg(g.opac + row * g.opac_stride);
-    s.opac = 1.0f / (1.0f + expf(-logit));
+    s.opac = 1.0f / (1.0f + expf(-in.logit));
 
     const float dx = s.mx - p.campos[0], dy = s.my - p.campos[1], dz = s.mz - p.campos[2];
     s.dnorm = sqrtf(dx * dx + dy * dy + dz * dz);
@@ -149,12 +200,12 @@ __device__ __forceinline__ void project_one(const gs_gaussians& g, int64_t row, 
     s.dir[0] = dx * inv;
     s.dir[1] = dy * inv;
     s.dir[2] = dz * inv;
-    float c0 = __ldg(cols + 0) * kSH_C0, c1 = __ldg(cols + 1) * kSH_C0, c2 = __ldg(cols + 2) * kSH_C0;
-    if (g.colors_dim >= 12) {
+    float c0 = in.col[0] * kSH_C0, c1 = in.col[1] * kSH_C0, c2 = in.col[2] * kSH_C0;
+    if (sh1) {
         const float xd = s.dir[0], yd = s.dir[1], zd = s.dir[2];
-        c0 += kSH_C1 * (__ldg(cols + 3) * yd + __ldg(cols + 4) * zd + __ldg(cols + 5) * xd);
-        c1 += kSH_C1 * (__ldg(cols + 6) * yd + __ldg(cols + 7) * zd + __ldg(cols + 8) * xd);
-        c2 += kSH_C1 * (__ldg(cols + 9) * yd + __ldg(cols + 10) * zd + __ldg(cols + 11) * xd);
+        c0 += kSH_C1 * (in.col[3] * yd + in.col[4] * zd + in.col[5] * xd);
+        c1 += kSH_C1 * (in.col[6] * yd + in.col[7] * zd + in.col[8] * xd);
+        c2 += kSH_C1 * (in.col[9] * yd + in.col[10] * zd + in.col[11] * xd);
     }
     s.pre[0] = c0 + 0.5f;
     s.pre[1] = c1 + 0.5f;

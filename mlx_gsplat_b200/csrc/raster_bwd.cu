@@ -16,7 +16,6 @@ namespace gs {
 #define GS_BWD_BATCH 128
 #endif
 using Layout = CompositeLayout<GS_BWD_PX>;
-constexpr int kPx = GS_BWD_PX;
 constexpr int kRenderThreads = Layout::threads;
 constexpr int kPairs = Layout::pairs;
 constexpr int kBatch = GS_BWD_BATCH;  // splats staged in shared memory per batch
@@ -30,8 +29,8 @@ constexpr int kGradRec = 12;  // floats per splat gradient record
 //   val_i = dL/dC . rgb_i + dL/dA,   B_{i-1} = alpha_i val_i + (1 - alpha_i) B_i
 // the alpha gradient is dL/dalpha_i = T_i (val_i - B_i).  The clip of
 // opacity * g to [0, 0.99] passes the gradient only strictly inside
-// (MLX's maximum/minimum rule).  Thread layout as in the forward (kPx pixels
-// of one column per thread, one CTA per tile).  The nine per-splat sums of a
+// (MLX's maximum/minimum rule).  Pixel layout as in the forward
+// (CompositeLayout, one CTA per tile).  The nine per-splat sums of a
 // warp's pixels are reduced with 14 shuffles, added into per-batch
 // shared-memory accumulators, and flushed with one global vector reduction
 // per (tile, splat).
@@ -285,6 +284,17 @@ __device__ __forceinline__ void put(float* base, int64_t off, float v, bool acc)
 
 // Chain rule from the splat gradient record back to means, quaternions,
 // log-scales, opacity logits and SH colour coefficients.
+// The gradient rows in the pooled row layout (see slab_rows), stored, not accumulated.
+inline bool slab_grad_rows(const gs_gaussian_grads& o) {
+    const int64_t S = o.quats_stride;
+    return o.quats && o.means && o.scales && o.opac && o.colors && !o.accumulate && !o.colors_by_visible &&
+           S % 4 == 0 && kRowColor + o.colors_write <= S && o.means_stride == S && o.scales_stride == S &&
+           o.opac_stride == S && o.colors_stride == S && o.means == o.quats + kRowMean &&
+           o.opac == o.quats + kRowOpac && o.scales == o.quats + kRowScale && o.colors == o.quats + kRowColor &&
+           (reinterpret_cast<uintptr_t>(o.quats) & 15u) == 0;
+}
+
+template <bool kSlabIn, bool kSlabOut>
 __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
                                                           RasterParams p, const float* __restrict__ splat_grads,
                                                           gs_gaussian_grads o, float* __restrict__ grad2d,
@@ -293,10 +303,10 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     if (vi >= nv) return;
     const int32_t id = ids[vi];
     const int64_t row = param_row(g, id);
-    const int64_t crow = g.colors_by_visible ? vi : row;
-    const float* cols = g.colors + crow * g.colors_stride;
+    GaussianIn in;
+    load_gaussian<kSlabIn>(g, row, g.colors_by_visible ? vi : row, in);
     ProjState s;
-    project_one(g, row, cols, p, s);
+    project_one(in, g.colors_dim >= 12, p, s);
     const float* G = splat_grads + vi * kGradRec;
     const float du = G[0], dv = G[1], dca = G[2], dcbc = G[3], dcd = G[4], dop = G[5];
     const float drgb[3] = {G[6], G[7], G[8]};
@@ -411,9 +421,9 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
 #pragma unroll
         for (int ch = 0; ch < 3; ++ch) {
             const float e = kSH_C1 * dpre[ch];
-            ddir[1] += e * __ldg(cols + 3 + 3 * ch + 0);
-            ddir[2] += e * __ldg(cols + 3 + 3 * ch + 1);
-            ddir[0] += e * __ldg(cols + 3 + 3 * ch + 2);
+            ddir[1] += e * in.col[3 + 3 * ch + 0];
+            ddir[2] += e * in.col[3 + 3 * ch + 1];
+            ddir[0] += e * in.col[3 + 3 * ch + 2];
         }
         const float n = s.dnorm, ne = n + 1e-8f;
         const float dx = s.mx - p.campos[0], dy = s.my - p.campos[1], dzz = s.mz - p.campos[2];
@@ -431,20 +441,59 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     const float reg = o.reg;
 #pragma unroll
     for (int k = 0; k < 3; ++k) dm[k] += reg;
-    if (o.means) {
+    if (kSlabOut) {
+        // the row's first 24 columns from registers, 16 bytes at a time; the
+        // colour columns past SH degree 1 hold only the regulariser
+        float vals[24];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) vals[k] = dquat[k] + reg;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) vals[kRowMean + k] = dm[k];
+        vals[kRowOpac] = dlogit + reg;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) vals[kRowScale + k] = dscale[k] + reg;
+#pragma unroll
+        for (int k = 0; k < 13; ++k) vals[kRowColor + k] = (k < 12 ? dcol[k] : 0.f) + (k < o.reg_color_cols ? reg : 0.f);
+        float* rowp = o.quats + (int64_t)id * o.quats_stride;
+        const int W = kRowColor + o.colors_write;
+#pragma unroll
+        for (int j = 0; j < 6; ++j) {
+            if (4 * j + 3 < W) {
+                reinterpret_cast<float4*>(rowp)[j] = make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2],
+                                                                 vals[4 * j + 3]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (4 * j + c < W) rowp[4 * j + c] = vals[4 * j + c];
+            }
+        }
+        for (int c = 24; c < W; c += 4) {
+            float t[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) t[u] = c + u - kRowColor < o.reg_color_cols ? reg : 0.f;
+            if (c + 3 < W) {
+                reinterpret_cast<float4*>(rowp + c)[0] = make_float4(t[0], t[1], t[2], t[3]);
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (c + u < W) rowp[c + u] = t[u];
+            }
+        }
+    }
+    if (!kSlabOut && o.means) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) put(o.means, (int64_t)id * o.means_stride + k, dm[k], acc);
     }
-    if (o.quats) {
+    if (!kSlabOut && o.quats) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) put(o.quats, (int64_t)id * o.quats_stride + k, dquat[k] + reg, acc);
     }
-    if (o.scales) {
+    if (!kSlabOut && o.scales) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) put(o.scales, (int64_t)id * o.scales_stride + k, dscale[k] + reg, acc);
     }
-    if (o.opac) put(o.opac, (int64_t)id * o.opac_stride, dlogit + reg, acc);
-    if (o.colors) {
+    if (!kSlabOut && o.opac) put(o.opac, (int64_t)id * o.opac_stride, dlogit + reg, acc);
+    if (!kSlabOut && o.colors) {
         const int64_t orow = o.colors_by_visible ? vi : (int64_t)id;
         float* dst = o.colors + orow * o.colors_stride;
         for (int k = 0; k < o.colors_write; ++k) {
@@ -496,7 +545,10 @@ extern "C" int gs_project_backward(const gs_gaussians* g, const int32_t* ids, in
     GS_REQUIRE(!grad2d || count, "project_backward: grad2d needs count");
     GS_REQUIRE(out->colors == nullptr || out->colors_write >= 0, "project_backward: bad colors_write");
     const RasterParams p = make_raster_params(*cam, nullptr);
-    project_bwd_kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p,
-                                                                                     splat_grads, *out, grad2d, count);
+    const bool in_rows = slab_rows(*g), out_rows = slab_grad_rows(*out);
+    auto kernel = in_rows ? (out_rows ? project_bwd_kernel<true, true> : project_bwd_kernel<true, false>)
+                          : (out_rows ? project_bwd_kernel<false, true> : project_bwd_kernel<false, false>);
+    kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p, splat_grads, *out,
+                                                                         grad2d, count);
     return check_launch("project_bwd_kernel");
 }

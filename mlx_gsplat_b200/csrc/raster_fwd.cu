@@ -75,6 +75,7 @@ __device__ __forceinline__ uint32_t warp_bin(bool has, const TileBox& tb, float 
 }
 
 // ---------------------------------------------------------------- projection + tile count
+template <bool kSlab>
 __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids,
                                                           int64_t nv, RasterParams p, float4* __restrict__ splats,
                                                           uint32_t* __restrict__ depth_keys,
@@ -90,9 +91,10 @@ __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const 
     if (active) {
         const int32_t id = ids[vi];
         const int64_t row = param_row(g, id);
-        const int64_t crow = g.colors_by_visible ? vi : row;
+        GaussianIn in;
+        load_gaussian<kSlab>(g, row, g.colors_by_visible ? vi : row, in);
         ProjState s;
-        project_one(g, row, g.colors + crow * g.colors_stride, p, s);
+        project_one(in, g.colors_dim >= 12, p, s);
         splats[3 * vi + 0] = make_float4(s.u, s.v, s.ca, s.cb);
         splats[3 * vi + 1] = make_float4(s.cc, s.cd, s.opac, s.rgb[0]);
         splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], pair_cut(s.opac, p), s.tz);
@@ -411,8 +413,10 @@ extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int
     GS_REQUIRE(cam->render_width > 0 && cam->render_height > 0 && cam->width > 0 && cam->height > 0,
                "project_forward: bad image size");
     const RasterParams p = make_raster_params(*cam, rs);
-    project_fwd_kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(
-        *g, ids, num_visible, p, reinterpret_cast<float4*>(splats), depth_keys, tile_counts);
+    auto kernel = slab_rows(*g) ? project_fwd_kernel<true> : project_fwd_kernel<false>;
+    kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p,
+                                                                        reinterpret_cast<float4*>(splats),
+                                                                        depth_keys, tile_counts);
     return check_launch("project_fwd_kernel");
 }
 

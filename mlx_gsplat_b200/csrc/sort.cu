@@ -5,7 +5,9 @@
 // every (digit, tile) its global output offset; (3) per tile, a stable local
 // rank of each key within its digit — warps own contiguous runs of keys and
 // rank them 32 at a time with __match_any_sync plus per-warp digit counters in
-// shared memory, then a cross-warp prefix — and a scatter to offset + rank.
+// shared memory, then a cross-warp prefix — the tile staged in shared memory
+// in sorted order, and written out in that order to offset + rank, so each
+// digit's run of keys is stored by consecutive threads.
 // There is no inter-CTA waiting (reduce-then-scan), so no kernel can spin.
 #include "common.cuh"
 #include "scan.cuh"
@@ -41,14 +43,18 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
                                                                 uint32_t mask, const uint32_t* __restrict__ offsets,
                                                                 int64_t n_tiles) {
     __shared__ uint32_t goff[kBins];
+    __shared__ uint32_t lstart[kBins];  // tile-local start of each digit
+    __shared__ uint32_t wtot[kSortWarps];
     __shared__ uint32_t wcnt[kSortWarps][kBins];
+    __shared__ uint32_t skey[kSortTile], sval[kSortTile];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     goff[threadIdx.x] = offsets[(int64_t)threadIdx.x * n_tiles + blockIdx.x];
 #pragma unroll
     for (int w = 0; w < kSortWarps; ++w) wcnt[w][threadIdx.x] = 0;
     __syncthreads();
 
-    const int64_t wbase = (int64_t)blockIdx.x * kSortTile + (int64_t)warp * (32 * kSortItems);
+    const int64_t tbase = (int64_t)blockIdx.x * kSortTile;
+    const int64_t wbase = tbase + (int64_t)warp * (32 * kSortItems);
     const unsigned lt = lanemask_lt();
     uint32_t key[kSortItems], val[kSortItems], rank[kSortItems];
     int dig[kSortItems];
@@ -69,23 +75,50 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
         rank[r] = prior + before;
     }
     __syncthreads();
-    {
-        uint32_t run = 0;
+    // per digit (one per thread): cross-warp prefix, then the tile-local
+    // digit starts by a block-wide exclusive scan of the digit totals
+    uint32_t run = 0;
 #pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) {
-            const uint32_t c = wcnt[w][threadIdx.x];
-            wcnt[w][threadIdx.x] = run;
-            run += c;
-        }
+    for (int w = 0; w < kSortWarps; ++w) {
+        const uint32_t c = wcnt[w][threadIdx.x];
+        wcnt[w][threadIdx.x] = run;
+        run += c;
     }
+    uint32_t inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) wtot[warp] = inc;
     __syncthreads();
+    uint32_t wpre = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) wpre += w < warp ? wtot[w] : 0u;
+    lstart[threadIdx.x] = wpre + inc - run;
+    __syncthreads();
+    // stage the tile in sorted order, then write it out in that order: each
+    // digit's keys go to consecutive global positions from consecutive threads
 #pragma unroll
     for (int r = 0; r < kSortItems; ++r) {
         const int d = dig[r];
         if (d < kBins) {
-            const uint32_t pos = goff[d] + wcnt[warp][d] + rank[r];
-            keys_out[pos] = key[r];
-            vals_out[pos] = val[r];
+            const uint32_t lp = lstart[d] + wcnt[warp][d] + rank[r];
+            skey[lp] = key[r];
+            sval[lp] = val[r];
+        }
+    }
+    __syncthreads();
+    const int tile_n = (int)(n - tbase < kSortTile ? n - tbase : kSortTile);
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+        const int j = r * kSortThreads + threadIdx.x;
+        if (j < tile_n) {
+            const uint32_t k = skey[j];
+            const int d = (int)((k >> shift) & mask);
+            const uint32_t pos = goff[d] + (uint32_t)j - lstart[d];
+            keys_out[pos] = k;
+            vals_out[pos] = sval[j];
         }
     }
 }
