@@ -523,6 +523,7 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const int32_t* ti
                                   gs_stream_t stream) {
     GS_REQUIRE(cam && ranges && final_T && n_contrib && splat_grads, "render_backward: null pointer");
     GS_REQUIRE(loss_mode >= GS_LOSS_NONE && loss_mode <= GS_LOSS_MEAN, "render_backward: bad loss mode");
+    GS_REQUIRE(!rs || rs->transmittance_min <= 1.f, "render_backward: transmittance_min must be <= 1");
     GS_REQUIRE(loss_mode != GS_LOSS_NONE || dL_dcolor, "render_backward: dL_dcolor required");
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || (target && out_color),
                "render_backward: target and out_color required");

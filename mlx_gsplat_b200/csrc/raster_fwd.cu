@@ -280,24 +280,29 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     const float px = (float)pi * p.sx + p.hsx;
     const gs_tile_range rg = ranges[tile];
 
-    // pixel pairs: pair q holds the thread's pixels 2q and 2q + 1
+    // pixel pairs: pair q holds the thread's pixels 2q and 2q + 1.  A pixel
+    // takes part while T >= t_min; pixels outside the image start with T = -1
+    // (never written back), so they never take part.
     float2 py[kPairs], T[kPairs], cr[kPairs], cg[kPairs], cb[kPairs], A[kPairs];
     int last[kPx];
-    bool done[kPx];
-    bool all_done = true;
+    const float t_min = p.t_min;
+    const float t_out = fminf(-1.f, t_min - 1.f);
 #pragma unroll
     for (int q = 0; q < kPairs; ++q) {
         const int pj = by0 + Layout::row(lane, 2 * q), pj1 = by0 + Layout::row(lane, 2 * q + 1);
         py[q] = make_float2((float)pj * p.sy + p.hsy, (float)pj1 * p.sy + p.hsy);
-        T[q] = f2(1.f);
+        T[q] = make_float2(pi < p.rw && pj < p.rh ? 1.f : t_out, pi < p.rw && pj1 < p.rh ? 1.f : t_out);
         cr[q] = cg[q] = cb[q] = A[q] = f2(0.f);
         last[2 * q] = last[2 * q + 1] = 0;
-        done[2 * q] = !(pi < p.rw && pj < p.rh);
-        done[2 * q + 1] = !(pi < p.rw && pj1 < p.rh);
-        all_done &= done[2 * q] & done[2 * q + 1];
     }
+    auto all_dead = [&]() {
+        bool d = true;
+#pragma unroll
+        for (int q = 0; q < kPairs; ++q) d &= (T[q].x < t_min) & (T[q].y < t_min);
+        return d;
+    };
     for (int b = rg.start; b < rg.end; b += kBatch) {
-        if (__syncthreads_count(all_done) == kRenderThreads) break;
+        if (__syncthreads_count(all_dead()) == kRenderThreads) break;
 #pragma unroll
         for (int h = 0; h < kBatch / kRenderThreads; ++h) {
             const int j = threadIdx.x + h * kRenderThreads;
@@ -314,7 +319,7 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
         const int cnt = min(kBatch, rg.end - b);
         const int base1 = b - rg.start + 1;
         // which staged splats can reach this warp's pixel block at all
-        bool warp_done = __all_sync(kFull, all_done);
+        bool warp_done = __all_sync(kFull, all_dead());
         unsigned hits[kBatch / 32];
 #pragma unroll
         for (int i = 0; i < kBatch / 32; ++i) {
@@ -324,24 +329,26 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
                                             by0 + Layout::rows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
+        // the saturation vote runs once per word of 32 staged splats: a pixel
+        // that saturates inside a word stops taking part at once (T < t_min)
 #pragma unroll
         for (int i = 0; i < kBatch / 32; ++i) {
+            if (warp_done) break;
             unsigned bits = hits[i];
-            while (bits && !warp_done) {
+            while (bits) {
                 const int k = 32 * i + __ffs(bits) - 1;
                 bits &= bits - 1;
                 const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
                 const float x = px - q0.x;
                 const float ax = q0.z * x, cx = q1.x * x;
                 const int idx1 = base1 + k;
-                all_done = true;
 #pragma unroll
                 for (int q = 0; q < kPairs; ++q) {
-                    // Branch-free front-to-back step: a pixel that is done or
+                    // Branch-free front-to-back step: a pixel that is saturated or
                     // out of the splat's reach gets alpha = 0 (T, colour unchanged).
                     const float2 m = pair_quad(__fadd2_rn(py[q], f2(-q0.y)), x, ax, cx, q0.w, q1.y);
                     const float2 og = __fmul2_rn(f2(q1.z), pair_falloff(m));
-                    const bool v0 = !done[2 * q] && m.x <= q2.z, v1 = !done[2 * q + 1] && m.y <= q2.z;
+                    const bool v0 = T[q].x >= t_min && m.x <= q2.z, v1 = T[q].y >= t_min && m.y <= q2.z;
                     const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
                     const float2 w = __fmul2_rn(al, T[q]);
                     cr[q] = __ffma2_rn(w, f2(q1.w), cr[q]);
@@ -349,18 +356,11 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
                     cb[q] = __ffma2_rn(w, f2(q2.y), cb[q]);
                     A[q] = __fadd2_rn(A[q], w);
                     T[q] = __fmul2_rn(T[q], __ffma2_rn(al, f2(-1.f), f2(1.f)));  // T (1 - alpha)
-                    if (v0) {
-                        last[2 * q] = idx1;
-                        done[2 * q] = T[q].x < p.t_min;
-                    }
-                    if (v1) {
-                        last[2 * q + 1] = idx1;
-                        done[2 * q + 1] = T[q].y < p.t_min;
-                    }
-                    all_done &= done[2 * q] & done[2 * q + 1];
+                    last[2 * q] = v0 ? idx1 : last[2 * q];
+                    last[2 * q + 1] = v1 ? idx1 : last[2 * q + 1];
                 }
-                warp_done = __all_sync(kFull, all_done);
             }
+            warp_done = __all_sync(kFull, all_dead());
         }
         __syncthreads();
     }
@@ -480,6 +480,7 @@ extern "C" int gs_render_forward(const gs_tile_range* ranges, const int32_t* til
                                  const void* target, float* loss_partials, gs_stream_t stream) {
     GS_REQUIRE(cam && ranges && out_color && out_alpha && final_T && n_contrib, "render_forward: null pointer");
     GS_REQUIRE(loss_mode >= GS_LOSS_NONE && loss_mode <= GS_LOSS_MEAN, "render_forward: bad loss mode");
+    GS_REQUIRE(!rs || rs->transmittance_min <= 1.f, "render_forward: transmittance_min must be <= 1");
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_partials, "render_forward: loss_partials required");
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || target, "render_forward: target required");
     const RasterParams p = make_raster_params(*cam, rs);

@@ -64,9 +64,17 @@ def _oracle_grads(g, cols_vis, ids, vm, K, W, H, dC, dA=None, pixel_ids=None):
     return C, A, full
 
 
-@pytest.mark.parametrize("sh_dim", [3, 12])
-def test_tiny_full_image_forward_backward_vs_oracle(sh_dim):
+@pytest.mark.parametrize("sh_dim,saturate", [(3, False), (12, False), (12, True)],
+                         ids=["sh0", "sh1", "sh1-saturated"])
+def test_tiny_full_image_forward_backward_vs_oracle(sh_dim, saturate):
+    """Whole image and every gradient against the dense oracle.  The saturated
+    case raises every opacity logit by 8 (alpha clipped at 0.99), so that many
+    pixels reach T < 1e-6 and stop compositing early; the dense oracle never
+    stops, and the difference stays below the remaining transmittance."""
     wl, g, cols = _scene("tiny-3k", 3000, seed=0, sh_dim=sh_dim)
+    if saturate:
+        g = dict(g)
+        g["opacities"] = (g["opacities"] + 8.0).astype(np.float32)
     views, K = synthetic.make_cameras(wl, seed=2)
     rng = np.random.default_rng(1)
     P = wl.pixels
@@ -88,6 +96,8 @@ def test_tiny_full_image_forward_backward_vs_oracle(sh_dim):
         wA = rng.uniform(-1, 1, (wl.height, wl.width, 1)).astype(np.float32) / P
         (torch.sum(C * _t(wC)) + torch.sum(A * _t(wA))).backward()
         Cr, Ar, gr = _oracle_grads(g, cols_vis, idn, vm, K, wl.width, wl.height, wC, wA)
+        if saturate:
+            assert (1.0 - A.detach().cpu().numpy() < 1e-6).mean() > 0.05, "too few saturated pixels"
         assert_image_close(C.detach().cpu().numpy(), Cr, what=f"view {vi} colors")
         assert_image_close(A.detach().cpu().numpy(), Ar, what=f"view {vi} alphas")
         for k in NAMES:
