@@ -85,6 +85,16 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                  : "memory");
 }
 
+// Shared-memory float add when ``on`` (a predicated reduction: no branch
+// around it and no returned value).
+__device__ __forceinline__ void red_add_shared_if(float* addr, float v, bool on) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(addr);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p red.shared.add.f32 [%0], %1;\n\t}" ::"r"(a), "f"(v),
+        "r"((unsigned)on)
+        : "memory");
+}
+
 // Camera-space point of world position m: row i of  viewmat @ [m, 1],
 // summed left to right with each product and sum rounded (no fused
 // multiply-add), the order the CPU oracle uses, so the cull decision

@@ -245,8 +245,8 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             // warp totals: lane l ends with the total of value (l >> 2) & 7; g[8] by butterfly
             const float t8 = warp_sum8(g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], lane);
             const float t9 = warp_sum(g[8]);
-            if ((lane & 3) == 0) atomicAdd(&acc[k][lane >> 2], t8);
-            if (lane == 0) atomicAdd(&acc[k][8], t9);
+            red_add_shared_if(&acc[k][(lane >> 2) & 7], t8, (lane & 3) == 0);
+            red_add_shared_if(&acc[k][8], t9, lane == 0);
           }
         }
         __syncthreads();
