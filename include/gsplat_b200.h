@@ -196,7 +196,9 @@ int gs_cull_noalloc(const gs_gaussians* g, int64_t n, const gs_camera* cam, floa
 /* ------------------------------------------------------------------ sort / scan */
 
 /* Stable LSD radix sort of (key, value) uint32 pairs on bits [begin_bit, end_bit).
- * Sorted output lands in keys_out/vals_out.  Scratch: gs_radix_sort_scratch_bytes(n). */
+ * Sorted output lands in keys_out/vals_out.  ``vals_in`` may be NULL (for a
+ * non-empty bit range): the values are then the input positions 0..n-1, so
+ * vals_out receives the sorting permutation.  Scratch: gs_radix_sort_scratch_bytes(n). */
 size_t gs_radix_sort_scratch_bytes(int64_t n);
 int gs_radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                         uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, void* scratch,
@@ -214,10 +216,16 @@ int gs_exclusive_scan_u32(const uint32_t* in, uint32_t* out, int64_t n, void* sc
  * mlx_gsplat/rendering.py:153-244, written as a 48-byte splat record
  * ``splats[v]`` = {u, v, conic_a, conic_b}, {conic_c, conic_d, opacity, r},
  * {g, b, depth, 0}; the sortable depth key ``depth_keys[v]``; and
- * ``tile_counts[v]``, the number of 16x16 tiles binned for it. */
+ * ``tile_counts[v]``, the number of 16x16 tiles binned for it.
+ * ``bin_scratch`` (gs_bin_scratch_bytes(num_visible) bytes of device memory,
+ * or NULL) carries binning state from here to gs_bin_emit of the same view:
+ * the binned tiles of every small tile box as a bitmask, so that emission
+ * does not test them again, and the list of splats with very large boxes,
+ * which are counted (here) and emitted by whole CTAs instead of one warp. */
+size_t gs_bin_scratch_bytes(int64_t num_visible);
 int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible, const gs_camera* cam,
                        const gs_raster_settings* rs, float* splats, uint32_t* depth_keys,
-                       uint32_t* tile_counts, gs_stream_t stream);
+                       uint32_t* tile_counts, void* bin_scratch, gs_stream_t stream);
 
 /* Offsets of each visible Gaussian's binned entries in depth order:
  * offsets[r] = sum of tile_counts[order[q]] for q < r, and offsets[n] = the
@@ -231,10 +239,13 @@ int gs_bin_offsets(const uint32_t* order, const uint32_t* tile_counts, int64_t n
  * id in ``tile_keys`` and v in ``entry_vals``.  ``capacity`` bounds the
  * output arrays: a Gaussian whose entries would pass it writes nothing and
  * sets the device flag ``*overflow_flag = 1`` (the caller zeroes it first and
- * reads it back when it did not size the arrays from the scan total). */
+ * reads it back when it did not size the arrays from the scan total).
+ * ``bin_scratch`` must be the one gs_project_forward filled for this view
+ * (or NULL when that call had none). */
 int gs_bin_emit(const float* splats, const uint32_t* order, const uint32_t* offsets, const uint32_t* tile_counts,
                 int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, uint32_t* tile_keys,
-                uint32_t* entry_vals, int64_t capacity, int32_t* overflow_flag, gs_stream_t stream);
+                uint32_t* entry_vals, int64_t capacity, int32_t* overflow_flag, void* bin_scratch,
+                gs_stream_t stream);
 
 /* Fills [start, end) per tile from the tile-sorted keys (ranges must hold
  * num_tiles entries; tiles without entries get {0, 0}). */

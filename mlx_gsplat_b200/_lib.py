@@ -78,11 +78,12 @@ _SIGS = {
     "gs_scan_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_exclusive_scan_u32": (ctypes.c_int, [c_vp, c_vp, i64, c_vp, ctypes.c_size_t, c_vp]),
     "gs_project_forward": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, i64, ctypes.POINTER(GsCamera),
-                                          ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, c_vp]),
+                                          ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "gs_bin_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_bin_offsets_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_bin_offsets": (ctypes.c_int, [c_vp, c_vp, i64, c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "gs_bin_emit": (ctypes.c_int, [c_vp] * 4 + [i64, ctypes.POINTER(GsCamera), ctypes.POINTER(GsRasterSettings),
-                                                c_vp, c_vp, i64, c_vp, c_vp]),
+                                                c_vp, c_vp, i64, c_vp, c_vp, c_vp]),
     "gs_tile_ranges": (ctypes.c_int, [c_vp, i64, ctypes.c_int32, c_vp, c_vp]),
     "gs_tile_order": (ctypes.c_int, [c_vp, ctypes.c_int32, c_vp, c_vp]),
     "gs_render_forward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),

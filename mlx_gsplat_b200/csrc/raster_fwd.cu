@@ -11,36 +11,53 @@ namespace gs {
 // lanes one after another and tests 32 tiles of the current box at a time
 // (ballot + popcount give the output positions), so a splat covering
 // thousands of tiles costs thousands / 32 warp steps rather than serialising
-// one thread.  Counting and emission run the same code on the same floats, so
-// they agree tile for tile.
+// one thread.  The counting pass also returns, for a box of at most 64
+// tiles, the bitmask of the tiles it binned (bit t = tile t of the box in
+// row-major order); the emitting pass, given that mask, expands it instead of
+// testing the tiles again, so both passes agree tile for tile.
+constexpr int kMaskTiles = 64;
+
 template <bool kEmit>
 __device__ __forceinline__ uint32_t warp_bin(bool has, const TileBox& tb, float u, float v, float ca, float cd,
                                              const RasterParams& p, uint32_t base, uint32_t expected, uint32_t vi,
-                                             uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+                                             bool use_masks, uint64_t mask_in, uint32_t* __restrict__ keys,
+                                             uint32_t* __restrict__ vals, uint64_t& mask_out) {
     const int lane = threadIdx.x & 31;
     const unsigned lt = lanemask_lt();
     uint32_t mine = 0;
+    mask_out = 0;
     unsigned todo = __ballot_sync(kFull, has);
     while (todo) {
         const int j = __ffs(todo) - 1;
         todo &= todo - 1;
         const int x0 = __shfl_sync(kFull, tb.x0, j), x1 = __shfl_sync(kFull, tb.x1, j);
         const int y0 = __shfl_sync(kFull, tb.y0, j), y1 = __shfl_sync(kFull, tb.y1, j);
+        const int w = x1 - x0 + 1;
+        const int area = w * (y1 - y0 + 1);
+        const bool from_mask = kEmit && use_masks && area <= kMaskTiles;
         TileBox b;
-        b.exact = __shfl_sync(kFull, (int)tb.exact, j) != 0;
-        b.m_cut = __shfl_sync(kFull, tb.m_cut, j);
-        b.s = __shfl_sync(kFull, tb.s, j);
-        const float uj = __shfl_sync(kFull, u, j), vj = __shfl_sync(kFull, v, j);
-        const float caj = __shfl_sync(kFull, ca, j), cdj = __shfl_sync(kFull, cd, j);
+        float uj = 0.f, vj = 0.f, caj = 0.f, cdj = 0.f;
+        uint64_t mj = 0;
+        if (from_mask) {
+            mj = ((uint64_t)__shfl_sync(kFull, (uint32_t)(mask_in >> 32), j) << 32) |
+                 __shfl_sync(kFull, (uint32_t)mask_in, j);
+        } else {
+            b.exact = __shfl_sync(kFull, (int)tb.exact, j) != 0;
+            b.m_cut = __shfl_sync(kFull, tb.m_cut, j);
+            b.s = __shfl_sync(kFull, tb.s, j);
+            uj = __shfl_sync(kFull, u, j);
+            vj = __shfl_sync(kFull, v, j);
+            caj = __shfl_sync(kFull, ca, j);
+            cdj = __shfl_sync(kFull, cd, j);
+        }
         uint32_t basej = 0, expj = 0, vij = 0;
         if (kEmit) {
             basej = __shfl_sync(kFull, base, j);
             expj = __shfl_sync(kFull, expected, j);
             vij = __shfl_sync(kFull, vi, j);
         }
-        const int w = x1 - x0 + 1;
-        const int area = w * (y1 - y0 + 1);
         uint32_t cnt = 0;
+        uint64_t bits = 0;
         for (int t0 = 0; t0 < area; t0 += 32) {
             const int t = t0 + lane;
             bool hit = false;
@@ -48,10 +65,11 @@ __device__ __forceinline__ uint32_t warp_bin(bool has, const TileBox& tb, float 
             if (t < area) {
                 const int r = t / w;
                 const int tx = x0 + (t - r * w), ty = y0 + r;
-                hit = splat_hits_tile(uj, vj, caj, cdj, b, tx, ty, p);
+                hit = from_mask ? ((mj >> t) & 1u) != 0 : splat_hits_tile(uj, vj, caj, cdj, b, tx, ty, p);
                 tile_id = ty * p.tiles_x + tx;
             }
             const unsigned bal = __ballot_sync(kFull, hit);
+            if (!kEmit && t0 < kMaskTiles) bits |= (uint64_t)bal << t0;
             if (kEmit && hit) {
                 const uint32_t k = cnt + __popc(bal & lt);
                 if (k < expj) {
@@ -69,9 +87,132 @@ __device__ __forceinline__ uint32_t warp_bin(bool has, const TileBox& tb, float 
                 vals[basej + k] = 0u;
             }
         }
-        if (lane == j) mine = cnt;
+        if (lane == j) {
+            mine = cnt;
+            mask_out = area <= kMaskTiles ? bits : 0;
+        }
     }
     return mine;
+}
+
+// ---------------------------------------------------------------- binning scratch
+// Splats whose tile box has more than kBigTiles tiles are not binned by their
+// warp: the counting pass appends them to a list, and CTA-wide kernels count
+// and emit them (kBigThreads tiles tested at a time), so a few very large
+// splats do not leave one warp running long after the rest of the launch.
+constexpr int kBigTiles = 256;
+constexpr int kBigThreads = 256;
+constexpr unsigned kBigGrid = 2 * 148;
+
+struct BinScratch {
+    uint32_t* big_count;  // number of listed splats
+    uint32_t* big_list;   // their visible indices
+    uint32_t* big_base;   // per visible index: first output entry (UINT32_MAX: not to emit)
+    uint64_t* masks;      // per visible index: binned-tile bitmask of a box of <= 64 tiles
+};
+
+inline size_t bin_scratch_bytes(int64_t nv) {
+    const size_t n = (size_t)(nv > 0 ? nv : 1);
+    return 256 + align_up(n * 4, 256) * 2 + align_up(n * 8, 256) + 256;
+}
+
+inline BinScratch bin_scratch_layout(void* scratch, int64_t nv) {
+    const size_t n = (size_t)(nv > 0 ? nv : 1);
+    char* q = reinterpret_cast<char*>(align_up(reinterpret_cast<uintptr_t>(scratch), 256));
+    BinScratch b;
+    b.big_count = reinterpret_cast<uint32_t*>(q);
+    q += 256;
+    b.big_list = reinterpret_cast<uint32_t*>(q);
+    q += align_up(n * 4, 256);
+    b.big_base = reinterpret_cast<uint32_t*>(q);
+    q += align_up(n * 4, 256);
+    b.masks = reinterpret_cast<uint64_t*>(q);
+    return b;
+}
+
+// Tile t (row-major) of a box tests exactly as the warp path does.
+__device__ __forceinline__ bool box_tile_hit(const TileBox& tb, int t, int w, float u, float v, float ca, float cd,
+                                             const RasterParams& p, int& tile_id) {
+    const int r = t / w;
+    const int tx = tb.x0 + (t - r * w), ty = tb.y0 + r;
+    tile_id = ty * p.tiles_x + tx;
+    return splat_hits_tile(u, v, ca, cd, tb, tx, ty, p);
+}
+
+// Block-wide exclusive prefix of one flag per thread; returns the prefix and
+// the block total in *total.  ``wsum`` holds kBigThreads / 32 entries.
+__device__ __forceinline__ uint32_t block_flag_prefix(bool f, uint32_t* wsum, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned bal = __ballot_sync(kFull, f);
+    if (lane == 0) wsum[warp] = __popc(bal);
+    __syncthreads();
+    uint32_t before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < kBigThreads / 32; ++w) {
+        const uint32_t c = wsum[w];
+        before += w < warp ? c : 0u;
+        all += c;
+    }
+    __syncthreads();
+    *total = all;
+    return before + __popc(bal & lanemask_lt());
+}
+
+__global__ void __launch_bounds__(kBigThreads) bin_count_big_kernel(const float4* __restrict__ splats, BinScratch bs,
+                                                                    RasterParams p,
+                                                                    uint32_t* __restrict__ tile_counts) {
+    const uint32_t n = *bs.big_count;
+    for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
+        const uint32_t vi = bs.big_list[i];
+        const float4 a = splats[3 * vi], b = splats[3 * vi + 1];
+        TileBox tb;
+        splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb);  // listed only when it has a box
+        const int w = tb.x1 - tb.x0 + 1, area = w * (tb.y1 - tb.y0 + 1);
+        uint32_t cnt = 0;
+        for (int t0 = 0; t0 < area; t0 += kBigThreads) {
+            const int t = t0 + threadIdx.x;
+            int tile_id;
+            const bool hit = t < area && box_tile_hit(tb, t, w, a.x, a.y, a.z, b.y, p, tile_id);
+            cnt += __syncthreads_count(hit);
+        }
+        if (threadIdx.x == 0) tile_counts[vi] = cnt;
+    }
+}
+
+__global__ void __launch_bounds__(kBigThreads) bin_emit_big_kernel(const float4* __restrict__ splats, BinScratch bs,
+                                                                   const uint32_t* __restrict__ tile_counts,
+                                                                   RasterParams p, uint32_t* __restrict__ tile_keys,
+                                                                   uint32_t* __restrict__ vals) {
+    __shared__ uint32_t wsum[kBigThreads / 32];
+    const uint32_t n = *bs.big_count;
+    for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
+        const uint32_t vi = bs.big_list[i];
+        const uint32_t base = bs.big_base[vi];
+        if (base == 0xffffffffu) continue;  // over capacity (uniform over the block)
+        const uint32_t cnt = tile_counts[vi];
+        const float4 a = splats[3 * vi], b = splats[3 * vi + 1];
+        TileBox tb;
+        splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb);
+        const int w = tb.x1 - tb.x0 + 1, area = w * (tb.y1 - tb.y0 + 1);
+        uint32_t done = 0;
+        for (int t0 = 0; t0 < area; t0 += kBigThreads) {
+            const int t = t0 + threadIdx.x;
+            int tile_id = 0;
+            const bool hit = t < area && box_tile_hit(tb, t, w, a.x, a.y, a.z, b.y, p, tile_id);
+            uint32_t total;
+            const uint32_t k = done + block_flag_prefix(hit, wsum, &total);
+            if (hit && k < cnt) {
+                tile_keys[base + k] = (uint32_t)tile_id;
+                vals[base + k] = vi;
+            }
+            done += total;
+        }
+        // the counting pass gave cnt == done; a shortfall becomes sentinel entries
+        for (uint32_t k = done + threadIdx.x; k < cnt; k += kBigThreads) {
+            tile_keys[base + k] = 0xffffffffu;
+            vals[base + k] = 0u;
+        }
+    }
 }
 
 // ---------------------------------------------------------------- projection + tile count
@@ -79,7 +220,8 @@ template <bool kSlab>
 __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids,
                                                           int64_t nv, RasterParams p, float4* __restrict__ splats,
                                                           uint32_t* __restrict__ depth_keys,
-                                                          uint32_t* __restrict__ tile_counts) {
+                                                          uint32_t* __restrict__ tile_counts, bool use_bs,
+                                                          BinScratch bs) {
     const int64_t vi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const bool active = vi < nv;
     bool has = false;
@@ -100,13 +242,21 @@ __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const 
         splats[3 * vi + 2] = make_float4(s.rgb[1], s.rgb[2], pair_cut(s.opac, p), s.tz);
         depth_keys[vi] = float_sort_key(s.tz);
         has = splat_tile_box(s.u, s.v, s.ca, s.cb, s.cc, s.cd, s.opac, p, tb);
+        if (has && use_bs && (tb.x1 - tb.x0 + 1) * (tb.y1 - tb.y0 + 1) > kBigTiles) {
+            bs.big_list[atomicAdd(bs.big_count, 1u)] = (uint32_t)vi;  // counted by bin_count_big_kernel
+            has = false;
+        }
         u = s.u;
         v = s.v;
         ca = s.ca;
         cd = s.cd;
     }
-    const uint32_t cnt = warp_bin<false>(has, tb, u, v, ca, cd, p, 0u, 0u, 0u, nullptr, nullptr);
-    if (active) tile_counts[vi] = cnt;
+    uint64_t mask;
+    const uint32_t cnt = warp_bin<false>(has, tb, u, v, ca, cd, p, 0u, 0u, 0u, false, 0u, nullptr, nullptr, mask);
+    if (active) {
+        tile_counts[vi] = cnt;
+        if (use_bs) bs.masks[vi] = mask;
+    }
 }
 
 // counts in depth order: out[r] = tile_counts[order[r]]
@@ -116,14 +266,26 @@ __global__ void gather_counts_kernel(const uint32_t* __restrict__ order, const u
     if (r < n) out[r] = counts[order[r]];
 }
 
-__global__ void __launch_bounds__(128) bin_emit_kernel(const float4* __restrict__ splats,
-                                                       const uint32_t* __restrict__ order,
-                                                       const uint32_t* __restrict__ offsets,
-                                                       const uint32_t* __restrict__ tile_counts, int64_t nv,
-                                                       RasterParams p, uint32_t* __restrict__ tile_keys,
-                                                       uint32_t* __restrict__ vals, int64_t capacity,
-                                                       int32_t* __restrict__ overflow) {
+// Emission: a warp owns 32 consecutive depth ranks, whose entries form one
+// contiguous range of the output.  When every splat of the warp has a
+// recorded mask (a box of at most 64 tiles), the lanes expand their masks into
+// shared memory and the warp stores the range with consecutive lanes on
+// consecutive entries; otherwise each lane expands its own mask in place and
+// large boxes are tested cooperatively.
+constexpr int kEmitThreads = 64;
+constexpr int kEmitStage = 32 * kMaskTiles;  // entries a warp of masked splats can produce
+
+__global__ void __launch_bounds__(kEmitThreads) bin_emit_kernel(const float4* __restrict__ splats,
+                                                               const uint32_t* __restrict__ order,
+                                                               const uint32_t* __restrict__ offsets,
+                                                               const uint32_t* __restrict__ tile_counts, int64_t nv,
+                                                               RasterParams p, uint32_t* __restrict__ tile_keys,
+                                                               uint32_t* __restrict__ vals, int64_t capacity,
+                                                               int32_t* __restrict__ overflow, bool use_bs,
+                                                               BinScratch bs) {
+    __shared__ uint32_t skey[kEmitThreads / 32][kEmitStage], sval[kEmitThreads / 32][kEmitStage];
     const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     bool has = false;
     TileBox tb;
     tb.x0 = tb.x1 = tb.y0 = tb.y1 = 0;
@@ -131,28 +293,99 @@ __global__ void __launch_bounds__(128) bin_emit_kernel(const float4* __restrict_
     tb.m_cut = tb.s = 0.f;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     uint32_t vi = 0, cnt = 0, base = 0;
+    uint64_t mask = 0;
+    bool staged = true;  // this lane's entries (if any) can go through the warp's staging
     if (r < nv) {
         vi = order[r];
         cnt = tile_counts[vi];
         base = offsets[r];
         if (cnt > 0) {
-            if ((int64_t)base + cnt > capacity) {
-                atomicExch(overflow, 1);
+            const bool over = (int64_t)base + cnt > capacity;
+            if (over) atomicExch(overflow, 1);
+            a = splats[3 * vi];
+            b = splats[3 * vi + 1];
+            has = splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb);
+            const int area = (tb.x1 - tb.x0 + 1) * (tb.y1 - tb.y0 + 1);
+            if (has && use_bs && area > kBigTiles) {
+                // listed by the counting pass: bin_emit_big_kernel writes it
+                bs.big_base[vi] = over ? 0xffffffffu : base;
+                has = false;
+                staged = false;  // its range lies inside the warp's span: no staging for this warp
+                cnt = 0;
+            } else if (over) {
+                has = false;
+                staged = false;
+                cnt = 0;
             } else {
-                a = splats[3 * vi];
-                b = splats[3 * vi + 1];
-                has = splat_tile_box(a.x, a.y, a.z, a.w, b.x, b.y, b.z, p, tb);
-                if (!has) {
-                    // cannot happen (the count pass found tiles); keep the sorted list well formed
-                    for (uint32_t k = 0; k < cnt; ++k) {
-                        tile_keys[base + k] = 0xffffffffu;
-                        vals[base + k] = 0u;
-                    }
-                }
+                if (use_bs) mask = bs.masks[vi];
+                staged = has && use_bs && area <= kMaskTiles && cnt <= (uint32_t)kMaskTiles;
             }
         }
     }
-    warp_bin<true>(has, tb, a.x, a.y, a.z, b.y, p, base, cnt, vi, tile_keys, vals);
+    const int w = tb.x1 - tb.x0 + 1;
+    const uint32_t inv_w = (65536u + (uint32_t)w - 1u) / (uint32_t)w;  // t / w = (t * inv_w) >> 16 for t < 64
+    if (__all_sync(kFull, staged)) {
+        // the warp's range starts at the first rank's offset (lanes past nv and
+        // splats without tiles add nothing)
+        const uint32_t base0 = __shfl_sync(kFull, base, 0);
+        const uint32_t end = cnt > 0 ? base + cnt : 0u;
+        uint32_t total = end > base0 ? end - base0 : 0u;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total = max(total, __shfl_xor_sync(kFull, total, o));
+        if (cnt > 0) {
+            const uint32_t local = base - base0;
+            uint64_t mm = mask;
+            for (uint32_t k = 0; k < cnt; ++k) {
+                // bit t: tile t of the box, row-major (none missing when both passes agree)
+                uint32_t key = 0xffffffffu, val = 0u;
+                if (mm) {
+                    const int t = __ffsll((long long)mm) - 1;
+                    mm &= mm - 1;
+                    const int ty = (int)(((uint32_t)t * inv_w) >> 16), tx = t - ty * w;
+                    key = (uint32_t)((tb.y0 + ty) * p.tiles_x + tb.x0 + tx);
+                    val = vi;
+                }
+                skey[warp][local + k] = key;
+                sval[warp][local + k] = val;
+            }
+        }
+        __syncwarp();
+        for (uint32_t o = lane; o < total; o += 32) {
+            tile_keys[base0 + o] = skey[warp][o];
+            vals[base0 + o] = sval[warp][o];
+        }
+        return;
+    }
+    if (has) {
+        const int area = w * (tb.y1 - tb.y0 + 1);
+        if (use_bs && area <= kMaskTiles) {
+            // small box: this lane expands its own recorded mask in place
+            uint32_t k = 0;
+            uint64_t mm = mask;
+            while (mm && k < cnt) {
+                const int t = __ffsll((long long)mm) - 1;
+                mm &= mm - 1;
+                const int ty = (int)(((uint32_t)t * inv_w) >> 16), tx = t - ty * w;
+                tile_keys[base + k] = (uint32_t)((tb.y0 + ty) * p.tiles_x + tb.x0 + tx);
+                vals[base + k] = vi;
+                ++k;
+            }
+            for (; k < cnt; ++k) {
+                tile_keys[base + k] = 0xffffffffu;
+                vals[base + k] = 0u;
+            }
+            has = false;
+        }
+    } else {
+        // no box (cannot happen after the count pass found tiles): keep the list well formed
+        for (uint32_t k = 0; k < cnt; ++k) {
+            tile_keys[base + k] = 0xffffffffu;
+            vals[base + k] = 0u;
+        }
+    }
+    // large boxes: the warp tests their tiles cooperatively
+    uint64_t unused;
+    warp_bin<true>(has, tb, a.x, a.y, a.z, b.y, p, base, cnt, vi, false, 0u, tile_keys, vals, unused);
 }
 
 __global__ void tile_ranges_kernel(const uint32_t* __restrict__ keys, int64_t n, int32_t num_tiles,
@@ -400,9 +633,12 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
 
 using namespace gs;
 
+extern "C" size_t gs_bin_scratch_bytes(int64_t num_visible) { return bin_scratch_bytes(num_visible); }
+
 extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible,
                                   const gs_camera* cam, const gs_raster_settings* rs, float* splats,
-                                  uint32_t* depth_keys, uint32_t* tile_counts, gs_stream_t stream) {
+                                  uint32_t* depth_keys, uint32_t* tile_counts, void* bin_scratch,
+                                  gs_stream_t stream) {
     GS_REQUIRE(g && cam, "project_forward: null descriptor");
     GS_REQUIRE(num_visible >= 0, "project_forward: negative count");
     if (num_visible == 0) return GS_OK;
@@ -413,10 +649,19 @@ extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int
     GS_REQUIRE(cam->render_width > 0 && cam->render_height > 0 && cam->width > 0 && cam->height > 0,
                "project_forward: bad image size");
     const RasterParams p = make_raster_params(*cam, rs);
+    const bool use_bs = bin_scratch != nullptr;
+    const BinScratch bs = use_bs ? bin_scratch_layout(bin_scratch, num_visible) : BinScratch{};
+    if (use_bs) cudaMemsetAsync(bs.big_count, 0, sizeof(uint32_t), (cudaStream_t)stream);
     auto kernel = slab_rows(*g) ? project_fwd_kernel<true> : project_fwd_kernel<false>;
     kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p,
                                                                         reinterpret_cast<float4*>(splats),
-                                                                        depth_keys, tile_counts);
+                                                                        depth_keys, tile_counts, use_bs, bs);
+    if (use_bs) {
+        GS_TRY(check_launch("project_fwd_kernel"));
+        bin_count_big_kernel<<<kBigGrid, kBigThreads, 0, (cudaStream_t)stream>>>(
+            reinterpret_cast<const float4*>(splats), bs, p, tile_counts);
+        return check_launch("bin_count_big_kernel");
+    }
     return check_launch("project_fwd_kernel");
 }
 
@@ -443,15 +688,23 @@ extern "C" int gs_bin_offsets(const uint32_t* order, const uint32_t* tile_counts
 extern "C" int gs_bin_emit(const float* splats, const uint32_t* order, const uint32_t* offsets,
                            const uint32_t* tile_counts, int64_t num_visible, const gs_camera* cam,
                            const gs_raster_settings* rs, uint32_t* tile_keys, uint32_t* entry_vals, int64_t capacity,
-                           int32_t* overflow_flag, gs_stream_t stream) {
+                           int32_t* overflow_flag, void* bin_scratch, gs_stream_t stream) {
     GS_REQUIRE(cam, "bin_emit: null camera");
     if (num_visible == 0) return GS_OK;
     GS_REQUIRE(splats && order && offsets && tile_counts && overflow_flag, "bin_emit: null pointer");
     GS_REQUIRE(capacity == 0 || (tile_keys && entry_vals), "bin_emit: null output");
     const RasterParams p = make_raster_params(*cam, rs);
-    bin_emit_kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(
+    const bool use_bs = bin_scratch != nullptr;
+    const BinScratch bs = use_bs ? bin_scratch_layout(bin_scratch, num_visible) : BinScratch{};
+    bin_emit_kernel<<<grid_for(num_visible, kEmitThreads), kEmitThreads, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<const float4*>(splats), order, offsets, tile_counts, num_visible, p, tile_keys, entry_vals,
-        capacity, overflow_flag);
+        capacity, overflow_flag, use_bs, bs);
+    if (use_bs) {
+        GS_TRY(check_launch("bin_emit_kernel"));
+        bin_emit_big_kernel<<<kBigGrid, kBigThreads, 0, (cudaStream_t)stream>>>(
+            reinterpret_cast<const float4*>(splats), bs, tile_counts, p, tile_keys, entry_vals);
+        return check_launch("bin_emit_big_kernel");
+    }
     return check_launch("bin_emit_kernel");
 }
 

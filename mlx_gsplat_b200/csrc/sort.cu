@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
         const int64_t i = wbase + r * 32 + lane;
         const bool valid = i < n;
         key[r] = valid ? keys_in[i] : 0u;
-        val[r] = valid ? vals_in[i] : 0u;
+        val[r] = valid ? (vals_in ? vals_in[i] : (uint32_t)i) : 0u;  // no values: the input positions
         const int d = valid ? (int)((key[r] >> shift) & mask) : kBins;  // invalid lanes form their own group
         dig[r] = d;
         const unsigned peers = __match_any_sync(kFull, d);
@@ -144,6 +144,7 @@ int radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t*
     if (n == 0) return GS_OK;
     const int passes = (end_bit - begin_bit + 7) / 8;
     if (passes == 0) {
+        GS_REQUIRE(vals_in, "radix_sort: an empty bit range needs vals_in");
         cudaMemcpyAsync(keys_out, keys_in, n * 4, cudaMemcpyDeviceToDevice, stream);
         cudaMemcpyAsync(vals_out, vals_in, n * 4, cudaMemcpyDeviceToDevice, stream);
         return check_launch("radix_sort copy", 0);
@@ -188,7 +189,7 @@ extern "C" size_t gs_radix_sort_scratch_bytes(int64_t n) { return gs::radix_sort
 extern "C" int gs_radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                                    uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, void* scratch,
                                    size_t scratch_bytes, gs_stream_t stream) {
-    GS_REQUIRE(keys_in && vals_in && keys_out && vals_out && scratch, "radix_sort: null pointer");
+    GS_REQUIRE(keys_in && keys_out && vals_out && scratch, "radix_sort: null pointer");
     return gs::radix_sort_pairs(keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, scratch, scratch_bytes,
                                 (cudaStream_t)stream);
 }

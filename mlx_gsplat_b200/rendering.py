@@ -189,15 +189,15 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
     if V > 0:
         depth_keys = _i32(V, device)
         tile_counts = _i32(V, device)
+        bin_scratch = _scratch(lib.gs_bin_scratch_bytes(V), device)  # binning state for gs_bin_emit
         check(lib.gs_project_forward(g, ids.data_ptr(), V, cam, rs, f.splats.data_ptr(), depth_keys.data_ptr(),
-                                     tile_counts.data_ptr(), st), "gs_project_forward")
+                                     tile_counts.data_ptr(), bin_scratch.data_ptr(), st), "gs_project_forward")
         if timer:
             timer.mark("project_fwd")
-        iota = torch.arange(V, dtype=torch.int32, device=device)
         keys_sorted = _i32(V, device)
         order = _i32(V, device)
         sb = _scratch(lib.gs_radix_sort_scratch_bytes(V), device)
-        check(lib.gs_radix_sort_pairs(depth_keys.data_ptr(), iota.data_ptr(), keys_sorted.data_ptr(),
+        check(lib.gs_radix_sort_pairs(depth_keys.data_ptr(), None, keys_sorted.data_ptr(),
                                       order.data_ptr(), V, 0, 32, sb.data_ptr(), sb.numel(), st), "depth sort")
         offsets = _i32(V + 1, device)
         ob = _scratch(lib.gs_bin_offsets_scratch_bytes(V), device)
@@ -213,7 +213,8 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
             vals = _i32(K, device)
             flag = torch.zeros(1, dtype=torch.int32, device=device)
             check(lib.gs_bin_emit(f.splats.data_ptr(), order.data_ptr(), offsets.data_ptr(), tile_counts.data_ptr(),
-                                  V, cam, rs, keys.data_ptr(), vals.data_ptr(), K, flag.data_ptr(), st), "gs_bin_emit")
+                                  V, cam, rs, keys.data_ptr(), vals.data_ptr(), K, flag.data_ptr(),
+                                  bin_scratch.data_ptr(), st), "gs_bin_emit")
             tile_bits = max(1, int(T).bit_length())  # 2**bits - 1 >= T: the emit sentinel sorts last
             f.tile_keys = _i32(K, device)
             f.entry_vals = _i32(K, device)

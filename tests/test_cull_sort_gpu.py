@@ -92,3 +92,9 @@ def test_radix_sort_stable_exact(n, lo, hi, kmax):
     order = np.argsort(sortkey, kind="stable")
     np.testing.assert_array_equal(vo.cpu().numpy().view(np.uint32), vals[order])
     np.testing.assert_array_equal(ko.cpu().numpy().view(np.uint32), keys[order])
+    # no values: vals_out is the sorting permutation itself
+    if hi > lo:
+        vo.fill_(-1)
+        _lib.check(lib.gs_radix_sort_pairs(K.data_ptr(), None, ko.data_ptr(), vo.data_ptr(), n, lo, hi,
+                                           sb.data_ptr(), sb.numel(), _lib.stream_ptr()))
+        np.testing.assert_array_equal(vo.cpu().numpy(), order.astype(np.int32))

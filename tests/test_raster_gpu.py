@@ -207,3 +207,55 @@ def test_empty_and_degenerate_inputs():
     assert_image_close(A.detach().cpu().numpy(), Ar)
     for k in NAMES:
         assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what="degenerate grad " + k)
+
+
+def test_binning_scratch_matches_warp_binning():
+    """Binning with the scratch (recorded tile masks, CTA-wide counting and
+    emission of splats whose box exceeds 256 tiles) gives exactly the entries
+    of the all-warp binning, including for boxes of hundreds of tiles."""
+    lib = _lib.lib()
+    st = _lib.stream_ptr()
+    wl, g, cols = _scene("mid-200k", 20_000, seed=3)
+    g = dict(g)
+    rng = np.random.default_rng(5)
+    big = rng.random(g["scales"].shape[0]) < 0.03
+    g["scales"] = np.where(big[:, None], g["scales"] + 2.5, g["scales"]).astype(np.float32)
+    views, K = synthetic.make_cameras(wl, seed=2)
+    vm = views[0]
+    T = {k: _t(g[k]) for k in ("means", "quats", "scales", "opacities")}
+    colors = _t(cols)
+    ids = frustum_culling_mlx(T["means"], None, None, vm, K, wl.width, wl.height, opacities=T["opacities"])
+    V = int(ids.numel())
+    gst = gaussians_struct(T["means"], T["quats"], T["scales"], T["opacities"], colors)
+    cam = camera_struct(vm, K, wl.width, wl.height, wl.width, wl.height)
+    rs = DEFAULT_SETTINGS.cstruct()
+    ntx, nty = (wl.width + 15) // 16, (wl.height + 15) // 16
+    i32 = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=DEV)
+    out = {}
+    for mode in ("warp", "scratch"):
+        splats = torch.empty((V, 12), dtype=torch.float32, device=DEV)
+        dkeys, counts = i32(V), i32(V)
+        bs = torch.empty(lib.gs_bin_scratch_bytes(V), dtype=torch.uint8, device=DEV) if mode == "scratch" else None
+        _lib.check(lib.gs_project_forward(gst, ids.data_ptr(), V, cam, rs, splats.data_ptr(), dkeys.data_ptr(),
+                                          counts.data_ptr(), _lib.ptr(bs), st))
+        ks, order = i32(V), i32(V)
+        sb = torch.empty(lib.gs_radix_sort_scratch_bytes(V), dtype=torch.uint8, device=DEV)
+        _lib.check(lib.gs_radix_sort_pairs(dkeys.data_ptr(), None, ks.data_ptr(), order.data_ptr(), V, 0, 32,
+                                           sb.data_ptr(), sb.numel(), st))
+        offs = i32(V + 1)
+        ob = torch.empty(lib.gs_bin_offsets_scratch_bytes(V), dtype=torch.uint8, device=DEV)
+        _lib.check(lib.gs_bin_offsets(order.data_ptr(), counts.data_ptr(), V, offs.data_ptr(), ob.data_ptr(),
+                                      ob.numel(), st))
+        Kn = int(offs[V].item())
+        keys, vals = i32(Kn), i32(Kn)
+        flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+        _lib.check(lib.gs_bin_emit(splats.data_ptr(), order.data_ptr(), offs.data_ptr(), counts.data_ptr(), V, cam,
+                                   rs, keys.data_ptr(), vals.data_ptr(), Kn, flag.data_ptr(), _lib.ptr(bs), st))
+        out[mode] = (counts[:V].cpu().numpy(), keys[:Kn].cpu().numpy(), vals[:Kn].cpu().numpy(), int(flag.item()))
+        if bs is not None:
+            n_big = int(bs[256 * ((bs.data_ptr() + 255) // 256) - bs.data_ptr():][:4].view(torch.int32).item())
+            assert n_big > 0, "the scene should have boxes of more than 256 tiles"
+    for a, b, what in zip(out["warp"], out["scratch"], ("counts", "keys", "vals", "overflow")):
+        np.testing.assert_array_equal(a, b, err_msg=what)
+    assert out["warp"][3] == 0
+    assert (out["warp"][1] < ntx * nty).all(), "no sentinel entries"
