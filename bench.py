@@ -46,8 +46,8 @@ def peaks():
 
 # What actually limits each kernel (ncu summaries under profiles/): the compositing kernels keep
 # their splat records in L2 and are bound by FP32 instruction issue, not by HBM.
-LIMITERS = {"render_bwd": "fp32 instruction issue (ncu issue-active ~82%, DRAM <1%)",
-            "render_fwd": "fp32 instruction issue (ncu issue-active ~81%, DRAM <1%)",
+LIMITERS = {"render_bwd": "fp32 instruction issue (ncu issue-active ~78%, DRAM ~1%; paired f32x2 math)",
+            "render_fwd": "fp32 instruction issue (ncu issue-active ~75%, DRAM ~1%; paired f32x2 math)",
             "adam": "hbm"}
 
 
@@ -167,9 +167,14 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- byte model
-def kernel_bytes(name: str, N: int, V: int, K: int, P: int, tiles: int, ncols: int, stride: int) -> float:
-    """Algorithmic bytes per launch (what the kernel must move at minimum)."""
+def kernel_bytes(name: str, N: int, V: int, K: int, P: int, tiles: int, ncols: int, stride: int,
+                 sparse_grad: bool = False) -> float:
+    """Algorithmic bytes per launch (what the kernel must move at minimum).  With
+    ``sparse_grad`` Adam reads gradient rows only for the V rows the view saw
+    (the rest take the regulariser, selected by the cull's visibility bits)."""
     if name == "adam":
+        if sparse_grad:
+            return N * (ncols * 24 + 4) + V * ncols * 4 + N / 8
         return N * (ncols * 28 + 4)
     if name == "render_fwd":
         return K * (4 + 48) + tiles * 8 + P * (12 + 4 + 4 + 4 + 3)
@@ -362,7 +367,8 @@ def main():
     per = {}
     for k in kernels:
         if k in phase and phase[k] > 0:
-            b = kernel_bytes(k, N, Vm, Km, P, tx * ty, L.ncols, L.stride)
+            b = kernel_bytes(k, N, Vm, Km, P, tx * ty, L.ncols, L.stride,
+                             sparse_grad=world == 1 and runner.sparse_unseen)
             per[k] = {"ms": phase[k], "gbs": b / (phase[k] * 1e-3) / 1e9, "bytes": b}
     pk = peaks()
     dom = max(per, key=lambda k: per[k]["ms"])
