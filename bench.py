@@ -81,6 +81,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the densify and 6M-row Adam measurements")
+    ap.add_argument("--multicast", action="store_true",
+                    help="N > 1: sum the gradient rows with the NVLink multicast kernels instead of NCCL")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
     return ap.parse_args()
@@ -308,9 +310,8 @@ def main():
     # a pool with headroom (the trainer's max_gaussians), so a densify step has free slots
     runner = runner_for_workload(args.workload, max_steps=10_000, device=dev, upload_targets=False, lr=1.6e-4,
                                  eps=1e-15, n=args.gaussians, num_views=nv,
-                                 max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2))
-    runner.pg = pg
-    runner.world = world
+                                 max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2),
+                                 process_group=pg, fused_reduce=args.multicast)
     targets_host = torch.from_numpy(synthetic.make_uint8_targets(wl, nv, seed=1)).pin_memory()
     targets_dev = targets_host.to(dev)
     L = runner.layout
@@ -350,6 +351,8 @@ def main():
     t_end = time.time()
     barrier(world)
     clk = clocks.stop(t_start, t_end)
+    if runner.fused_reduce is not None:
+        runner.fused_reduce.check()  # a barrier that timed out invalidates the run
     launches = lib.gs_kernel_launches() - launches0
     ms = e0.elapsed_time(e1) / args.steps
     ms_max = max_over_ranks(ms, world)
@@ -368,7 +371,7 @@ def main():
     for k in kernels:
         if k in phase and phase[k] > 0:
             b = kernel_bytes(k, N, Vm, Km, P, tx * ty, L.ncols, L.stride,
-                             sparse_grad=world == 1 and runner.sparse_unseen)
+                             sparse_grad=runner.row_mode == "sparse")
             per[k] = {"ms": phase[k], "gbs": b / (phase[k] * 1e-3) / 1e9, "bytes": b}
     pk = peaks()
     dom = max(per, key=lambda k: per[k]["ms"])
@@ -440,6 +443,8 @@ def main():
                 "config": {"workload": args.workload, "gaussians": wl.num_gaussians, "image": f"{wl.width}x{wl.height}",
                            "sh_degree": wl.sh_degree, "views": nv, "views_per_gpu_per_step": 1,
                            "parallelism": f"views-dp{world}", "loss": "l1",
+                           "grad_reduce": ("nvlink multicast row sum" if runner.fused_reduce is not None else
+                                           ("nccl all-reduce" if world > 1 else "none")),
                            "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v/grad slabs (0.96 GB) "
                                  "every step"},
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,

@@ -75,6 +75,7 @@ typedef struct gs_gaussian_grads {
     int32_t accumulate;       /* 1: atomically add into the rows; 0: store */
     float reg;                /* constant added to every written geometry gradient (the trainer's 1e-5 * sum(params)) */
     int32_t reg_color_cols;   /* the first reg_color_cols colour columns also receive ``reg`` */
+    int32_t reg_geometry;     /* 0: the geometry columns do not receive ``reg`` (the caller adds it later) */
 } gs_gaussian_grads;
 
 /* Pinhole camera.  ``viewmat`` is the row-major world-to-camera matrix
@@ -149,13 +150,16 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
  * uses the hardware approximate square root and reciprocal (a few ulp of the
  * step, relative error below 1e-6) unless ``mode`` has GS_ADAM_EXACT, which
  * makes every operation IEEE round-to-nearest (bit-identical to
- * gs_fused_adam_group, at a higher instruction cost). */
+ * gs_fused_adam_group, at a higher instruction cost).  ``grad_bias_host``
+ * (ncols floats, or NULL) is added to every row's gradient before
+ * ``grad_scale`` (the regulariser of rows summed over GPUs, added once here
+ * instead of by every GPU). */
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                        double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                        float grad_scale, int mode, const uint32_t* visible_words, const float* unseen_grad_host,
-                       gs_stream_t stream);
+                       const float* grad_bias_host, gs_stream_t stream);
 
 /* ------------------------------------------------------------------ cull */
 
@@ -299,6 +303,30 @@ int gs_render_backward(const gs_tile_range* ranges, const int32_t* tile_order, c
 int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_visible, const gs_camera* cam,
                         const float* splat_grads, const gs_gaussian_grads* out, float* grad2d, float* count,
                         gs_stream_t stream);
+
+/* ------------------------------------------------------------------ multi-GPU */
+
+/* Barrier across the ``world`` GPUs of a group (no reference counterpart: the
+ * reference runs on one device).  ``peer_pads`` is a device array of the
+ * group's signal-pad addresses (uint32 [channels x world] in peer-mapped
+ * symmetric memory, zeroed before first use); every GPU calls with the same
+ * channel and the same epoch sequence (one more per call and channel).
+ * Orders all earlier work of every GPU (multimem gradient reductions
+ * included) before all later work.  Polling is bounded by ``max_polls``
+ * (about 100 ns each): on timeout ``*error_flag`` is set to 1 and the kernel
+ * returns. */
+int gs_group_barrier(uint32_t* const* peer_pads, int32_t rank, int32_t world, int32_t channel, uint32_t epoch,
+                     int32_t* error_flag, int64_t max_polls, gs_stream_t stream);
+
+/* Sum over the group's GPUs of rows [first_row, first_row + num_rows) of a
+ * row slab (``stride`` floats per row, a multiple of 4) in symmetric memory,
+ * through its NVLink multicast address: every 16 bytes are loaded reduced
+ * across all GPUs' copies and stored back to all of them.  Each GPU calls it
+ * on a disjoint range between two gs_group_barrier calls (after every GPU
+ * wrote its rows; before anyone reads the sums); together the calls leave the
+ * same sums in every copy. */
+int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, int64_t num_rows, int64_t stride,
+                          gs_stream_t stream);
 
 /* ------------------------------------------------------------------ pool / densify */
 

@@ -18,6 +18,7 @@ struct AdamScalars {
     float eps, wd, sqrt_bc2, grad_scale;
     float inv_sqrt_bc2;        // 1 / sqrt(1 - beta2^t) for the approximate step
     int scrub, clamp;
+    int has_bias;              // slab: add the per-column gradient bias before scaling
 };
 
 constexpr int kMaxSlabCols = 64;
@@ -26,6 +27,7 @@ struct SlabCols {
     float lo[kMaxSlabCols];
     float hi[kMaxSlabCols];
     float gdef[kMaxSlabCols];  // gradient of a row the visibility bits mark unseen
+    float gbias[kMaxSlabCols]; // added to every row's gradient before the scale
 };
 
 __device__ __forceinline__ void adam_elem(float& th, float& m, float& v, float g, const AdamScalars& s,
@@ -118,12 +120,13 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
 // copy with a lane-dependent column made every access a divergent constant
 // load (serialised in the address-divergence unit).
 struct __align__(16) ColsSmem {
-    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols];
+    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols], gbias[kMaxSlabCols];
 };
 
 template <bool kExact, bool kFused>
 __device__ __forceinline__ void slab_elem(float& th, float& m, float& v, float g, int c, int ncols,
                                           const AdamScalars& s, const ColsSmem& cs) {
+    if (s.has_bias) g = __fadd_rn(g, cs.gbias[c]);
     if (kExact) {
         if (c < ncols) adam_elem(th, m, v, g, s, cs.step[c], cs.lo[c], cs.hi[c]);
     } else {
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         cs.lo[threadIdx.x] = cols.lo[threadIdx.x];
         cs.hi[threadIdx.x] = cols.hi[threadIdx.x];
         cs.gdef[threadIdx.x] = cols.gdef[threadIdx.x];
+        cs.gbias[threadIdx.x] = cols.gbias[threadIdx.x];
     }
     __syncthreads();
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -239,6 +243,7 @@ static AdamScalars make_scalars(int mode, double beta1, double beta2, float eps,
     s.eps = eps;
     s.wd = wd;
     s.grad_scale = grad_scale;
+    s.has_bias = 0;
     if (mode == GS_ADAM_FUSED) {
         const float b1 = (float)beta1, b2 = (float)beta2;
         s.omb1 = 1.0f - b1;
@@ -297,7 +302,7 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                                   double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                                   float grad_scale, int mode, const uint32_t* visible_words,
-                                  const float* unseen_grad_host, gs_stream_t stream) {
+                                  const float* unseen_grad_host, const float* grad_bias_host, gs_stream_t stream) {
     const bool exact = (mode & GS_ADAM_EXACT) != 0;
     mode &= ~GS_ADAM_EXACT;
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
@@ -319,7 +324,9 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         cols.hi[c] = on ? col_hi[c] : 0.f;
         cols.step_size[c] = on ? step_size_for(mode, lr, col_lr_scale ? col_lr_scale[c] : 1.0f, bc1) : 0.f;
         cols.gdef[c] = (on && unseen_grad_host) ? unseen_grad_host[c] : 0.f;
+        cols.gbias[c] = (on && grad_bias_host) ? grad_bias_host[c] : 0.f;
     }
+    s.has_bias = grad_bias_host != nullptr;
     const int chunks = (int)(stride / 4);
     int shift = 0;
     while ((1 << shift) < chunks) ++shift;
@@ -354,7 +361,7 @@ extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, u
         }
         return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
                                   beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED | GS_ADAM_EXACT,
-                                  nullptr, nullptr, stream);
+                                  nullptr, nullptr, nullptr, stream);
     }
     return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
                                weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);

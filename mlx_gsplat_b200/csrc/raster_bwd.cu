@@ -439,19 +439,26 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     // ---- outputs
     const bool acc = o.accumulate != 0;
     const float reg = o.reg;
+    // written geometry gradients carry ``reg`` unless the caller adds it later;
+    // the densification statistic below always uses the full mean gradient
+    const float reg_geo = o.reg_geometry ? reg : 0.f;
+    float dmw[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) dm[k] += reg;
+    for (int k = 0; k < 3; ++k) {
+        dmw[k] = dm[k] + reg_geo;
+        dm[k] += reg;
+    }
     if (kSlabOut) {
         // the row's first 24 columns from registers, 16 bytes at a time; the
         // colour columns past SH degree 1 hold only the regulariser
         float vals[24];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) vals[k] = dquat[k] + reg;
+        for (int k = 0; k < 4; ++k) vals[k] = dquat[k] + reg_geo;
 #pragma unroll
-        for (int k = 0; k < 3; ++k) vals[kRowMean + k] = dm[k];
-        vals[kRowOpac] = dlogit + reg;
+        for (int k = 0; k < 3; ++k) vals[kRowMean + k] = dmw[k];
+        vals[kRowOpac] = dlogit + reg_geo;
 #pragma unroll
-        for (int k = 0; k < 3; ++k) vals[kRowScale + k] = dscale[k] + reg;
+        for (int k = 0; k < 3; ++k) vals[kRowScale + k] = dscale[k] + reg_geo;
 #pragma unroll
         for (int k = 0; k < 13; ++k) vals[kRowColor + k] = (k < 12 ? dcol[k] : 0.f) + (k < o.reg_color_cols ? reg : 0.f);
         float* rowp = o.quats + (int64_t)id * o.quats_stride;
@@ -482,17 +489,17 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     }
     if (!kSlabOut && o.means) {
 #pragma unroll
-        for (int k = 0; k < 3; ++k) put(o.means, (int64_t)id * o.means_stride + k, dm[k], acc);
+        for (int k = 0; k < 3; ++k) put(o.means, (int64_t)id * o.means_stride + k, dmw[k], acc);
     }
     if (!kSlabOut && o.quats) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) put(o.quats, (int64_t)id * o.quats_stride + k, dquat[k] + reg, acc);
+        for (int k = 0; k < 4; ++k) put(o.quats, (int64_t)id * o.quats_stride + k, dquat[k] + reg_geo, acc);
     }
     if (!kSlabOut && o.scales) {
 #pragma unroll
-        for (int k = 0; k < 3; ++k) put(o.scales, (int64_t)id * o.scales_stride + k, dscale[k] + reg, acc);
+        for (int k = 0; k < 3; ++k) put(o.scales, (int64_t)id * o.scales_stride + k, dscale[k] + reg_geo, acc);
     }
-    if (!kSlabOut && o.opac) put(o.opac, (int64_t)id * o.opac_stride, dlogit + reg, acc);
+    if (!kSlabOut && o.opac) put(o.opac, (int64_t)id * o.opac_stride, dlogit + reg_geo, acc);
     if (!kSlabOut && o.colors) {
         const int64_t orow = o.colors_by_visible ? vi : (int64_t)id;
         float* dst = o.colors + orow * o.colors_stride;

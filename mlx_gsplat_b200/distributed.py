@@ -1,9 +1,11 @@
 """Views data-parallel training across the GPUs of one box.
 
 Every rank holds the whole pool (the Gaussians are replicated); each step every
-rank renders its own camera view and writes its gradient rows, the rows are
-summed over ranks with one all-reduce (NCCL over NVLink), and every rank runs
-the same fused Adam on the summed rows scaled by 1/world, so the replicas stay
+rank renders its own camera view and stores the gradient rows of the
+Gaussians it saw (without the geometry regulariser) into a zeroed slab, the
+rows are summed over ranks (an NCCL all-reduce over NVLink, or the multicast
+kernels of ``FusedRowReduce``), and every rank runs the same fused Adam on the
+summed rows plus ``world * reg`` scaled by 1/world, so the replicas stay
 bit-identical without any parameter broadcast.  The densification statistics
 (grad2d, count) are summed before each densify step, and the densify noise is
 drawn from a generator seeded by the step, identically on every rank.
@@ -57,6 +59,95 @@ def densify_noise(step: int, n: int, device) -> Dict[str, torch.Tensor]:
     return {"means1": torch.randn((n, 3), generator=gen, device=device),
             "means2": torch.randn((n, 3), generator=gen, device=device),
             "quats2": torch.randn((n, 4), generator=gen, device=device)}
+
+
+class FusedRowReduce:
+    """Gradient rows summed over the GPUs of one NVSwitch domain by the GPUs
+    themselves through NVLink multicast, instead of by an NCCL all-reduce.
+
+    The row slab lives in symmetric memory with a multicast mapping.  Each GPU
+    stores its visible rows locally (without the geometry regulariser, which
+    Adam adds once for every row: ``world * reg`` before the ``1/world`` scale)
+    into a slab that is zero elsewhere.  ``sum_rows`` then waits until every
+    GPU has written (barrier), sums this GPU's 1/world slice of the rows across
+    all copies and stores the sums to all of them (``multimem.ld_reduce`` +
+    ``multimem.st``: one writer per element, so every replica gets the same
+    bits), and waits until every slice is done (barrier).  After Adam each GPU
+    zeroes its own copy; the next step's first barrier keeps peers from
+    summing before that.  Barrier waits are bounded; a timeout sets ``error``
+    (``check`` raises), it never stalls the GPU.
+
+    Use ``available`` first: it needs NCCL, more than one GPU and multicast
+    support; otherwise the trainer keeps the all-reduce path.
+    """
+
+    MAX_POLLS = 1 << 25  # about 3 s of polling per wait
+
+    def __init__(self, rows: int, cols: int, device, pg):
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        self.device = torch.device(device)
+        self.pg = pg
+        self.rank = rank_of(pg)
+        self.world = world_of(pg)
+        name = pg.group_name
+        try:
+            symm.enable_symm_mem_for_group(name)
+        except Exception:
+            pass  # newer releases enable groups on first rendezvous
+        self.rows = symm.empty((rows, cols), dtype=torch.float32, device=self.device)
+        self.rows.zero_()
+        self._rows_hdl = symm.rendezvous(self.rows, name)
+        self.multicast = int(self._rows_hdl.multicast_ptr)
+        if self.multicast == 0:
+            raise RuntimeError("no NVLink multicast mapping for the gradient rows")
+        self.pads = symm.empty((2 * self.world,), dtype=torch.int32, device=self.device)
+        self.pads.zero_()
+        self._pads_hdl = symm.rendezvous(self.pads, name)
+        self.peer_pads = torch.tensor([int(p) for p in self._pads_hdl.buffer_ptrs], dtype=torch.int64,
+                                      device=self.device)
+        self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = [0, 0]
+        self._lib = _lib
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=pg)
+
+    @staticmethod
+    def available(device, pg) -> bool:
+        if pg is None or world_of(pg) < 2 or dist.get_backend(pg) != "nccl":
+            return False
+        try:
+            import torch.distributed._symmetric_memory as symm
+            return bool(symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA,
+                                                                     torch.device(device).index or 0))
+        except Exception:
+            return False
+
+    def _barrier(self, channel: int) -> None:
+        self.epoch[channel] = (self.epoch[channel] + 1) & 0xFFFFFFFF
+        lib = self._lib.lib()
+        self._lib.check(lib.gs_group_barrier(self.peer_pads.data_ptr(), self.rank, self.world, channel,
+                                             self.epoch[channel], self.error.data_ptr(), self.MAX_POLLS,
+                                             self._lib.stream_ptr(self.device)), "group barrier")
+
+    def slice_of(self, n_rows: int):
+        """This GPU's rows of the sum: a contiguous 1/world share."""
+        per = -(-n_rows // self.world)
+        first = min(self.rank * per, n_rows)
+        return first, min(per, n_rows - first)
+
+    def sum_rows(self, n_rows: int) -> None:
+        """Rows [0, n_rows) of every GPU's copy become the sum over GPUs."""
+        self._barrier(0)
+        first, count = self.slice_of(n_rows)
+        lib = self._lib.lib()
+        self._lib.check(lib.gs_rows_sum_multicast(self.multicast, first, count, self.rows.shape[1],
+                                                  self._lib.stream_ptr(self.device)), "multicast row sum")
+        self._barrier(1)
+
+    def check(self) -> None:
+        if int(self.error.item()) != 0:
+            raise RuntimeError("multi-GPU barrier timed out (a peer did not arrive)")
 
 
 def init_from_env(backend: str = "nccl", timeout_s: float = 180.0):

@@ -106,12 +106,14 @@ class FusedMLXAdam:
     def step_slab(self, theta: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
                   table: torch.Tensor, num_active: int, ncols: int, col_lo, col_hi, quat_col: int = -1,
                   grad_scale: float = 1.0, pure: bool = False, col_lr_scale=None, visible_words: Optional[int] = None,
-                  unseen_grad=None, exact: bool = False) -> None:
+                  unseen_grad=None, exact: bool = False, grad_bias=None) -> None:
         """One launch over every group of a ``[max, stride]`` slab (fused semantics).
         With ``visible_words`` (device address of the cull's visibility bitmask) rows
         the bitmask marks unseen take ``unseen_grad`` (ncols floats) as their gradient
         instead of reading ``g``.  The step uses the hardware approximate square
-        root and reciprocal (relative error below 1e-6) unless ``exact``."""
+        root and reciprocal (relative error below 1e-6) unless ``exact``.
+        ``grad_bias`` (ncols floats) is added to every row's gradient before
+        ``grad_scale``."""
         self.t += 1
         lib = _lib.lib()
         _lib.check(lib.gs_fused_adam_slab(theta.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(),
@@ -122,4 +124,5 @@ class FusedMLXAdam:
                                           grad_scale, (_lib.GS_ADAM_PURE if pure else _lib.GS_ADAM_FUSED) |
                                           (_lib.GS_ADAM_EXACT if exact else 0),
                                           visible_words, None if unseen_grad is None else _lib.fptr(unseen_grad),
+                                          None if grad_bias is None else _lib.fptr(grad_bias),
                                           _lib.stream_ptr(theta.device)), "fused adam (slab)")

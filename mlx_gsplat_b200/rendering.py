@@ -97,7 +97,7 @@ def gaussians_struct(means, quats=None, scales=None, opacities=None, colors=None
 
 def grads_struct(means=None, quats=None, scales=None, opacities=None, colors=None, colors_write: int = 0,
                  colors_by_visible: bool = False, accumulate: bool = True, reg: float = 0.0,
-                 reg_color_cols: int = 0) -> GsGaussianGrads:
+                 reg_color_cols: int = 0, reg_geometry: bool = True) -> GsGaussianGrads:
     o = GsGaussianGrads()
     o.means, o.means_stride = _rows(means, 3, "grad means")
     o.quats, o.quats_stride = _rows(quats, 4, "grad quats")
@@ -109,6 +109,7 @@ def grads_struct(means=None, quats=None, scales=None, opacities=None, colors=Non
     o.accumulate = int(accumulate)
     o.reg = float(reg)
     o.reg_color_cols = int(reg_color_cols)
+    o.reg_geometry = int(bool(reg_geometry))
     return o
 
 

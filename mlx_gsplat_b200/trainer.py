@@ -100,7 +100,7 @@ class StepTimer:
 class RunnerMLX:
     def __init__(self, cfg: MLXConfig, init_params: Dict[str, np.ndarray], viewmats: np.ndarray, K: np.ndarray,
                  targets: Optional[torch.Tensor] = None, device: Optional[torch.device] = None,
-                 scene_scale: float = 1.0, process_group=None):
+                 scene_scale: float = 1.0, process_group=None, fused_reduce: bool = False):
         self.cfg = cfg
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.allocator = PointerStableChunkedAllocator(cfg.max_gaussians, cfg.sh_degree, device=self.device)
@@ -108,7 +108,18 @@ class RunnerMLX:
         self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
         L = self.allocator.layout
         self.layout = L
-        self.grad = torch.zeros((cfg.max_gaussians, L.stride), dtype=torch.float32, device=self.device)
+        self.pg = process_group
+        self.world = distributed.world_of(process_group)
+        # Across GPUs the gradient rows are summed by NCCL, or (``fused_reduce``)
+        # by this library's NVLink multicast kernels.
+        self.fused_reduce = None
+        if fused_reduce and distributed.FusedRowReduce.available(self.device, process_group):
+            self.fused_reduce = distributed.FusedRowReduce(cfg.max_gaussians, L.stride, self.device,
+                                                           process_group)
+        if self.fused_reduce is not None:
+            self.grad = self.fused_reduce.rows
+        else:
+            self.grad = torch.zeros((cfg.max_gaussians, L.stride), dtype=torch.float32, device=self.device)
         lo, hi = L.col_bounds()
         self.col_lo, self.col_hi = lo.tolist(), hi.tolist()
         self.viewmats = np.asarray(viewmats, np.float32)
@@ -118,11 +129,13 @@ class RunnerMLX:
         self.targets = targets
         self.settings = RasterSettings(cfg.alpha_cutoff, cfg.transmittance_min)
         self.scene_scale = scene_scale
-        self.pg = process_group
-        self.world = distributed.world_of(process_group)
         self.last_frame = None
         self.step_count = 0
-        self.sparse_unseen = True  # single GPU: unseen rows' gradients come from the visibility bits
+        # How gradient rows of unseen Gaussians are formed: "sparse" (one GPU:
+        # Adam takes the regulariser row for them from the cull's visibility
+        # bits), "dense" (every row filled with the regulariser first), "summed"
+        # (rows summed over GPUs from a zeroed slab; Adam adds world * reg).
+        self.row_mode = "summed" if self.world > 1 else "sparse"
 
     # ------------------------------------------------------------------ helpers
     def _reg_pattern(self) -> List[float]:
@@ -146,10 +159,13 @@ class RunnerMLX:
         L = self.layout
         gb = self.grad
         o = L.offsets
+        # summed rows: Adam adds the geometry regulariser once for every row
+        summed = self.row_mode == "summed"
         return grads_struct(gb[:, o["means"]:o["means"] + 3], gb[:, o["quats"]:o["quats"] + 4],
                             gb[:, o["scales"]:o["scales"] + 3], gb[:, o["opacities"]:o["opacities"] + 1],
                             gb[:, L.color_col:], colors_write=L.color_cols, colors_by_visible=False,
-                            accumulate=False, reg=self.cfg.param_reg, reg_color_cols=sh_cols_for(step, self.cfg))
+                            accumulate=False, reg=self.cfg.param_reg, reg_color_cols=sh_cols_for(step, self.cfg),
+                            reg_geometry=not summed)
 
     # ------------------------------------------------------------------ one step
     def train_step(self, view_idx: int, step: int, target: Optional[torch.Tensor] = None,
@@ -177,9 +193,13 @@ class RunnerMLX:
                                timer=timer)
         # Gradient rows of Gaussians this view does not see hold only the
         # regulariser.  On one GPU Adam takes them from the cull's visibility bits
-        # (no rows written); across GPUs the all-reduce needs every row filled.
-        dense_rows = self.world > 1 or not self.sparse_unseen
-        if dense_rows:
+        # (no rows written).  Across GPUs every GPU stores only its visible rows
+        # (without the geometry regulariser) into a slab that is zero elsewhere,
+        # the rows are summed over GPUs, and Adam adds ``world * reg`` to every
+        # row before the ``1/world`` scale.
+        mode = self.row_mode
+        fused = self.fused_reduce is not None
+        if mode == "dense":
             _lib.check(lib.gs_fill_rows(self.grad.data_ptr(), N, self.layout.stride, _lib.fptr(self._reg_pattern()),
                                         st), "grad init")
             if timer:
@@ -187,17 +207,31 @@ class RunnerMLX:
         render_backward(frame, g, self._grad_out(step), self.device, grad2d=self.allocator.grad2d,
                         count=self.allocator.count, timer=timer)
         scale = 1.0
-        if self.world > 1:
-            scale = distributed.reduce_gradient_rows(self.grad[:N], self.pg)
+        bias = None
+        if mode == "summed":
+            if fused:
+                self.fused_reduce.sum_rows(N)
+            else:
+                distributed.reduce_gradient_rows(self.grad[:N], self.pg)
+            scale = 1.0 / self.world
+            bias = [self.world * r for r in self._reg_pattern()[:self.layout.ncols]]
             if timer:
-                timer.mark("allreduce")
-        vis = None if dense_rows else (cull_scratch.data_ptr() + 255) // 256 * 256
+                timer.mark("row_sum" if fused else "allreduce")
+        sparse = mode == "sparse"
+        vis = (cull_scratch.data_ptr() + 255) // 256 * 256 if sparse else None
         self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
                                  self.allocator.indirection_table, N, self.layout.ncols, self.col_lo, self.col_hi,
                                  quat_col=self.layout.quat_col, grad_scale=scale, visible_words=vis,
-                                 unseen_grad=None if dense_rows else self._reg_pattern()[:self.layout.ncols])
+                                 unseen_grad=self._reg_pattern()[:self.layout.ncols] if sparse else None,
+                                 grad_bias=bias)
         if timer:
             timer.mark("adam")
+        if mode == "summed":
+            # this GPU's rows for the next step (with the multicast sum the peers
+            # are past it: the next step's first barrier orders the rest)
+            self.grad[:N].zero_()
+            if timer:
+                timer.mark("zero_rows")
         self.last_frame = frame
         self.step_count += 1
         return frame
@@ -275,7 +309,8 @@ class RunnerMLX:
 
 def runner_for_workload(name: str, max_steps: int = 100, num_views: Optional[int] = None, device=None,
                         n: Optional[int] = None, lr: float = 1e-3, eps: float = 1e-15, seed: int = 0,
-                        loss: str = "l1", upload_targets: bool = True, **overrides) -> RunnerMLX:
+                        loss: str = "l1", upload_targets: bool = True, process_group=None,
+                        fused_reduce: bool = False, **overrides) -> RunnerMLX:
     """A runner for one of the synthetic workloads (``synthetic.WORKLOADS``)."""
     wl = synthetic.WORKLOADS[name]
     g = synthetic.make_gaussians(wl, seed=seed, n=n)
@@ -292,7 +327,8 @@ def runner_for_workload(name: str, max_steps: int = 100, num_views: Optional[int
         targets = torch.from_numpy(synthetic.make_uint8_targets(wl, min(len(views), 8), seed=1)).to(dev)
     elif upload_targets and wl.target_kind == "render":
         targets = render_targets(wl, views, K, dev, seed=1, n=n)
-    return RunnerMLX(cfg, g, views, K, targets=targets, device=dev, scene_scale=synthetic.scene_scale(views))
+    return RunnerMLX(cfg, g, views, K, targets=targets, device=dev, scene_scale=synthetic.scene_scale(views),
+                     process_group=process_group, fused_reduce=fused_reduce)
 
 
 def render_targets(wl: synthetic.Workload, views: np.ndarray, K: np.ndarray, device, seed: int = 1,

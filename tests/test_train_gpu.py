@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("wl_name,n", [("tiny-3k", 3000), ("mid-200k", 20_000)])
 def test_train_step_matches_oracle(wl_name, n):
     r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15)
-    r.sparse_unseen = False  # write every gradient row so the test can inspect them
+    r.row_mode = "dense"  # write every gradient row so the test can inspect them
     al, L = r.allocator, r.layout
     step = 1
     theta0 = al.theta.cpu().numpy().copy()
@@ -107,19 +107,25 @@ def test_unseen_rows_from_visibility_bits_match_dense_rows():
         np.testing.assert_array_equal(a, b)
 
 
-def test_sparse_and_dense_training_agree():
-    """End to end through the trainer.  The rasterizer's gradient reductions are
-    float atomics, so two runs differ in the last bits; Adam turns that into
-    parameter differences of a few ulp (tolerance 1e-5 relative)."""
+def test_gradient_row_modes_agree():
+    """End to end through the trainer, the three ways of forming the gradient
+    rows of unseen Gaussians: "sparse" (one GPU: regulariser rows selected by
+    the visibility bits), "dense" (every row filled first) and "summed" (the
+    multi-GPU form: rows without the geometry regulariser in a zeroed slab, the
+    sum over GPUs — here one — and ``world * reg`` added by Adam).  The
+    rasterizer's gradient reductions are float atomics, so two runs differ in
+    the last bits; Adam turns that into parameter differences of a few ulp
+    (tolerance 1e-5 relative)."""
     runs = []
-    for sparse in (True, False):
+    for mode in ("sparse", "dense", "summed"):
         r = runner_for_workload("mid-200k", max_steps=50, n=30_000, num_views=4, lr=1e-3, eps=1e-15)
-        r.sparse_unseen = sparse
+        r.row_mode = mode
         for step in range(1, 4):
             r.train_step(step - 1, step)
         torch.cuda.synchronize()
         runs.append([t.cpu().numpy() for t in (r.allocator.theta, r.allocator.adam_m, r.allocator.adam_v)])
-    np.testing.assert_allclose(runs[0][0], runs[1][0], rtol=1e-5, atol=1e-6)
+    for other in runs[1:]:
+        np.testing.assert_allclose(runs[0][0], other[0], rtol=1e-5, atol=1e-6)
 
 
 def test_training_reduces_loss():
