@@ -228,6 +228,38 @@ def adam_standalone(rows: int, layout, dev, iters: int = 10):
             "bytes": b, "inputs": "5.8 GB of slabs > L2"}
 
 
+def l1_dssim_timing(color, target, dev, iters: int = 20):
+    """The L1 + D-SSIM loss kernels (loss and dL/dC) on one rendered image,
+    timed with CUDA events; bytes = what they must move (image, target,
+    gradient, the three partial maps written and read back)."""
+    from mlx_gsplat_b200 import _lib
+    lib = _lib.load()
+    H, W, _ = color.shape
+    out = torch.zeros(2, dtype=torch.float32, device=dev)
+    dC = torch.empty_like(color)
+    sb = torch.empty(lib.gs_l1_dssim_scratch_bytes(W, H), dtype=torch.uint8, device=dev)
+
+    def run():
+        _lib.check(lib.gs_l1_dssim_loss(color.data_ptr(), target.data_ptr(), int(target.dtype == torch.uint8),
+                                        W, H, 0.8, 0.2, out.data_ptr(), out[1:].data_ptr(), dC.data_ptr(),
+                                        sb.data_ptr(), sb.numel(), _lib.stream_ptr(dev)), "l1+dssim loss")
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    P = H * W
+    b = P * (12 + 3) * 2 + P * 12 + P * 36 * 2
+    return {"ms": ms, "gbs": b / (ms * 1e-3) / 1e9, "loss": float(out[0]), "ssim": float(out[1]),
+            "image": f"{W}x{H}"}
+
+
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
 def cpu_baseline(wl_name: str, seconds: float):
     """The CPU oracle on a bounded sample of the workload, scaled to full steps/s."""
@@ -427,6 +459,10 @@ def main():
             densify_ms = {"error": str(e)}
 
     # ---- the large workload's standalone fused Adam: 6M rows x 59 columns, theta/m/v/g
+    # ---- the reference trainer's L1 + D-SSIM image loss (forward + gradient) on this image size
+    l1_dssim = None
+    if not args.no_extras:
+        l1_dssim = l1_dssim_timing(runner.last_frame.color, targets_dev[0], dev)
     adam_6m = None
     if world == 1 and not args.no_extras:
         adam_6m = adam_standalone(6_000_000, L, dev)
@@ -452,7 +488,7 @@ def main():
                 "kernels_ms": {k: round(v["ms"], 4) for k, v in per.items()},
                 "phases_ms": {k: round(v, 4) for k, v in phase.items()},
                 "roofline": roof, "clocks": clk, "e2e": e2e, "cpu_baseline": base,
-                "densify": densify_ms, "adam_6m": adam_6m,
+                "densify": densify_ms, "adam_6m": adam_6m, "l1_dssim_loss": l1_dssim,
                 "gpu_launches": int(launches)}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -304,6 +304,22 @@ int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_v
                         const float* splat_grads, const gs_gaussian_grads* out, float* grad2d, float* count,
                         gs_stream_t stream);
 
+/* ------------------------------------------------------------------ loss */
+
+/* The reference trainer's image loss with a target (mlx_gsplat/trainer.py:
+ * 164-190, 276-279): l1_weight * mean|C - T| + dssim_weight * (1 - SSIM)/2,
+ * SSIM per channel with an 11 x 11 window of ones/121 and zero padding 5,
+ * averaged over pixels and channels (the trainer uses 0.8 and 0.2).  ``color``
+ * is the rendered HWC float32 image, ``target`` HWC uint8 (scaled by 1/255,
+ * ``target_is_u8`` = 1) or float32.  Writes the loss (device float) and, when
+ * not NULL, SSIM (device float) and dL/dC (HWC float32, for
+ * gs_render_backward with GS_LOSS_NONE).  Scratch:
+ * gs_l1_dssim_scratch_bytes(width, height). */
+size_t gs_l1_dssim_scratch_bytes(int32_t width, int32_t height);
+int gs_l1_dssim_loss(const float* color, const void* target, int target_is_u8, int32_t width, int32_t height,
+                     float l1_weight, float dssim_weight, float* loss_out, float* ssim_out, float* dL_dcolor,
+                     void* scratch, size_t scratch_bytes, gs_stream_t stream);
+
 /* ------------------------------------------------------------------ multi-GPU */
 
 /* Barrier across the ``world`` GPUs of a group (no reference counterpart: the

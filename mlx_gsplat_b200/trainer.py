@@ -5,15 +5,18 @@ the pooled slab — no per-step gather of the active parameters:
 
     cull over the active ids (through the indirection table)
     -> tile rasterizer forward with the L1 loss fused into its epilogue
-    -> gradient rows of unseen Gaussians filled with the regulariser pattern
+       (or the L1 + D-SSIM loss kernels after it)
     -> rasterizer backward writing one gradient row per visible Gaussian and
        accumulating the densification statistic (grad2d, count)
-    -> [views data-parallel: NCCL all-reduce of the gradient rows]
-    -> one fused Adam launch over the slab (+ quaternion renormalisation)
+    -> [views data-parallel: sum of the gradient rows over GPUs]
+    -> one fused Adam launch over the slab (+ quaternion renormalisation);
+       unseen Gaussians' rows take the regulariser inside Adam
     -> periodic opacity reset and densify/prune (``densify``).
 
 Loss: ``loss="l1"`` is mean |render - target| (the benchmark workloads);
-``loss="mean"`` is the reference's target-less ``mean(render)``.  The
+``loss="l1+dssim"`` is the reference trainer's loss with a target,
+0.8 * L1 + 0.2 * (1 - SSIM) / 2 (trainer.py:276-279, SSIM with its 11 x 11
+box window); ``loss="mean"`` is the reference's target-less ``mean(render)``.  The
 reference's ``1e-5 * sum(active params)`` term (trainer.py:283-292) is kept as
 ``param_reg``: +1e-5 on every means/quats/scales/opacities gradient of every
 active Gaussian and on the gathered colour coefficients of visible ones.
@@ -180,8 +183,15 @@ class RunnerMLX:
         cam = self.cams[view_idx % len(self.cams)]
         if target is None and self.targets is not None:
             target = self.targets[view_idx % self.targets.shape[0]]
-        loss_mode = _lib.GS_LOSS_MEAN if (cfg.loss == "mean" or target is None) else (
-            _lib.GS_LOSS_L1_U8 if target.dtype == torch.uint8 else _lib.GS_LOSS_L1_F32)
+        ssim_loss = cfg.loss == "l1+dssim" and target is not None
+        if cfg.loss not in ("l1", "mean", "l1+dssim"):
+            raise ValueError(f"unknown loss {cfg.loss!r} (l1, mean or l1+dssim)")
+        if ssim_loss:
+            loss_mode = _lib.GS_LOSS_NONE  # the image loss and dL/dC come from gs_l1_dssim_loss
+        elif cfg.loss == "mean" or target is None:
+            loss_mode = _lib.GS_LOSS_MEAN
+        else:
+            loss_mode = _lib.GS_LOSS_L1_U8 if target.dtype == torch.uint8 else _lib.GS_LOSS_L1_F32
         g = self._gaussians(step)
         if timer:
             timer.mark("start")
@@ -191,6 +201,9 @@ class RunnerMLX:
             timer.mark("cull")
         frame = render_forward(g, ids, V, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
                                timer=timer)
+        dL_dcolor = self._l1_dssim(frame, target) if ssim_loss else None
+        if ssim_loss and timer:
+            timer.mark("loss")
         # Gradient rows of Gaussians this view does not see hold only the
         # regulariser.  On one GPU Adam takes them from the cull's visibility bits
         # (no rows written).  Across GPUs every GPU stores only its visible rows
@@ -204,8 +217,8 @@ class RunnerMLX:
                                         st), "grad init")
             if timer:
                 timer.mark("grad_init")
-        render_backward(frame, g, self._grad_out(step), self.device, grad2d=self.allocator.grad2d,
-                        count=self.allocator.count, timer=timer)
+        render_backward(frame, g, self._grad_out(step), self.device, dL_dcolor=dL_dcolor,
+                        grad2d=self.allocator.grad2d, count=self.allocator.count, timer=timer)
         scale = 1.0
         bias = None
         if mode == "summed":
@@ -277,8 +290,31 @@ class RunnerMLX:
         al.count.zero_()
         return n_p, n_s
 
+    def _l1_dssim(self, frame, target: torch.Tensor) -> torch.Tensor:
+        """The reference trainer's image loss 0.8 * L1 + 0.2 * (1 - SSIM) / 2
+        (trainer.py:276-279) of the rendered frame; returns dL/dC (HWC) and
+        keeps the loss (and SSIM) on the frame."""
+        lib = _lib.lib()
+        RW, RH = frame.cam.render_width, frame.cam.render_height
+        key = (RW, RH)
+        if getattr(self, "_ssim_key", None) != key:
+            self._ssim_scratch = torch.empty(lib.gs_l1_dssim_scratch_bytes(RW, RH), dtype=torch.uint8,
+                                             device=self.device)
+            self._ssim_dc = torch.empty((RH, RW, 3), dtype=torch.float32, device=self.device)
+            self._ssim_key = key
+        frame.loss_scalar = torch.empty(2, dtype=torch.float32, device=self.device)  # loss, SSIM
+        _lib.check(lib.gs_l1_dssim_loss(frame.color.data_ptr(), target.data_ptr(),
+                                        int(target.dtype == torch.uint8), RW, RH, 0.8, 0.2,
+                                        frame.loss_scalar.data_ptr(), frame.loss_scalar[1:].data_ptr(),
+                                        self._ssim_dc.data_ptr(), self._ssim_scratch.data_ptr(),
+                                        self._ssim_scratch.numel(), _lib.stream_ptr(self.device)),
+                   "l1+dssim loss")
+        return self._ssim_dc
+
     def loss_value(self, frame=None) -> torch.Tensor:
         f = frame or self.last_frame
+        if getattr(f, "loss_scalar", None) is not None:
+            return f.loss_scalar[0]
         P = f.cam.render_width * f.cam.render_height
         return f.loss_partials.sum() / (3.0 * P)
 

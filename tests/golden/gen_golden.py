@@ -1,6 +1,7 @@
 """Generate the golden fixtures under ``tests/golden/`` by running the
 reference's own, unmodified Python (``mlx_gsplat/rendering.py``,
-``optimizer.py``, ``allocator.py``) on seeded inputs.
+``optimizer.py``, ``allocator.py``, and the ``_ssim`` method of
+``trainer.py``) on seeded inputs.
 
 MLX is not installable here, so ``tests/golden/mlx_shim`` stands in for
 ``mlx.core`` over torch-CPU (see its docstring).  The fixtures are small
@@ -198,6 +199,48 @@ def gen_alloc(A, out):
     np.savez_compressed(os.path.join(out, "allocator.npz"), **res)
 
 
+def load_ref_ssim(ref_root: str):
+    """The reference trainer's ``_ssim`` method (``mlx_gsplat/trainer.py``),
+    taken from the file's own text and executed as a plain function over the
+    shim: the trainer module itself needs its whole runtime to import."""
+    import textwrap
+    src = open(os.path.join(ref_root, "mlx_gsplat", "trainer.py")).read()
+    start = src.index("    def _ssim(")
+    end = src.index("\n    def ", start + 1)
+    ns = {"mx": mx}
+    exec(textwrap.dedent(src[start:end]), ns)
+    return ns["_ssim"]
+
+
+def gen_ssim(ref_root, out):
+    """Loss and gradient of the reference trainer's image loss with a target,
+    0.8 * mean|C - T| + 0.2 * 0.5 * (1 - SSIM(C, T)) (trainer.py:276-279), for
+    rendered images C against targets T, through the shim's value_and_grad."""
+    ssim = load_ref_ssim(ref_root)
+    res = {}
+    for i, (h, w) in enumerate([(37, 53), (90, 120), (16, 16)]):
+        rng = np.random.default_rng(40 + i)
+        c = rng.uniform(0, 1, (h, w, 3)).astype(np.float32)
+        t = np.clip(c + rng.normal(0, 0.15, (h, w, 3)), 0, 1).astype(np.float32)
+        if i == 2:
+            t = rng.uniform(0, 1, (h, w, 3)).astype(np.float32)  # unrelated images
+        tt = mx.array(t)
+
+        def loss_fn(params):
+            pred = params["c"]
+            l1 = mx.mean(mx.abs(pred - tt))
+            d_ssim = 0.5 * (1.0 - ssim(None, pred, tt))
+            return 0.8 * l1 + 0.2 * d_ssim
+
+        loss, grads = mx.value_and_grad(loss_fn)({"c": mx.array(c)})
+        res[f"c_{i}"] = c
+        res[f"t_{i}"] = t
+        res[f"ssim_{i}"] = np.asarray(ssim(None, mx.array(c), tt).detach().numpy(), np.float32)
+        res[f"loss_{i}"] = np.asarray(loss.detach().numpy(), np.float32)
+        res[f"grad_{i}"] = grads["c"].detach().numpy().astype(np.float32)
+    np.savez_compressed(os.path.join(out, "ssim.npz"), **res)
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     torch.manual_seed(0)
@@ -214,6 +257,7 @@ def main():
         gen_raster(R, HERE)
         gen_adam(O, HERE)
         gen_alloc(A, HERE)
+        gen_ssim(ref_root, HERE)
     finally:
         os.chdir(cwd)
     print("fixtures written to", HERE)

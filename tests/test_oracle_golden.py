@@ -126,3 +126,15 @@ def test_allocator_matches_reference(golden_dir):
     with pytest.raises(MemoryError):
         o.split_and_prune(np.zeros(n, bool), np.ones(n, bool), sp)
     assert bool(d["oom_raised"])
+
+
+def test_l1_dssim_loss_matches_reference(golden_dir):
+    from oracle import loss as oloss
+    d = _load(golden_dir, "ssim.npz")
+    for i in range(3):
+        c, t = d[f"c_{i}"], d[f"t_{i}"]
+        loss, s, g = oloss.l1_dssim_loss(c, t)
+        np.testing.assert_allclose(s, float(d[f"ssim_{i}"]), rtol=2e-6, atol=1e-7)
+        np.testing.assert_allclose(loss, float(d[f"loss_{i}"]), rtol=2e-6, atol=1e-7)
+        ref = d[f"grad_{i}"].astype(np.float64)
+        assert np.abs(g - ref).max() <= 1e-4 * np.abs(ref).max(), i

@@ -14,9 +14,10 @@ from oracle import rendering as orend
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("wl_name,n", [("tiny-3k", 3000), ("mid-200k", 20_000)])
-def test_train_step_matches_oracle(wl_name, n):
-    r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15)
+@pytest.mark.parametrize("wl_name,n,loss", [("tiny-3k", 3000, "l1"), ("mid-200k", 20_000, "l1"),
+                                            ("tiny-3k", 3000, "l1+dssim"), ("mid-200k", 20_000, "l1+dssim")])
+def test_train_step_matches_oracle(wl_name, n, loss):
+    r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15, loss=loss)
     r.row_mode = "dense"  # write every gradient row so the test can inspect them
     al, L = r.allocator, r.layout
     step = 1
@@ -37,7 +38,12 @@ def test_train_step_matches_oracle(wl_name, n):
     target = r.targets[0].cpu().numpy()
     tf = target.astype(np.float32) / np.float32(255.0) if target.dtype == np.uint8 else target
     P = r.cfg.render_width * r.cfg.render_height
-    dC = np.sign(C.astype(np.float64) - tf) / (3.0 * P)
+    if loss == "l1":
+        dC = np.sign(C.astype(np.float64) - tf) / (3.0 * P)
+    else:
+        from oracle import loss as oloss
+        ref_loss, _, dC = oloss.l1_dssim_loss(C, tf)
+        assert abs(float(r.loss_value()) - ref_loss) <= 1e-5 * abs(ref_loss)
     _, _, gr = orend.rasterize_dense_vjp(act["means"][ids], act["quats"][ids], act["scales"][ids],
                                          act["opacities"][ids], colors[ids], r.viewmats[0], r.K, r.cfg.width,
                                          r.cfg.height, r.cfg.render_width, r.cfg.render_height, dL_dC=dC)
