@@ -304,6 +304,18 @@ int gs_project_backward(const gs_gaussians* g, const int32_t* ids, int64_t num_v
                         const float* splat_grads, const gs_gaussian_grads* out, float* grad2d, float* count,
                         gs_stream_t stream);
 
+/* ------------------------------------------------------------------ export */
+
+/* The rows of export_to_ply (mlx_gsplat/trainer.py:570-631) for the active
+ * ids 0..num_active-1 of a pooled slab (physical row table[i], ``stride``
+ * floats per row, the given column offsets): out[i] = means(3) | 0 0 0 |
+ * colour columns | opacity logit clipped to [-5, 2] | log-scales clipped to
+ * [-10, -2] | quaternion / (|q| + 1e-8), row-major float32 with
+ * ``out_cols`` = 14 + color_cols columns (checked), the PLY vertex layout. */
+int gs_export_rows(const float* theta, int64_t stride, const int32_t* table, int64_t num_active, int mean_col,
+                   int opac_col, int scale_col, int quat_col, int color_col, int color_cols, float* out,
+                   int64_t out_cols, gs_stream_t stream);
+
 /* ------------------------------------------------------------------ loss */
 
 /* The reference trainer's image loss with a target (mlx_gsplat/trainer.py:

@@ -94,6 +94,7 @@ _SIGS = {
                                           c_vp, c_vp, c_vp, c_vp]),
     "gs_project_backward": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, i64, ctypes.POINTER(GsCamera), c_vp,
                                            ctypes.POINTER(GsGaussianGrads), c_vp, c_vp, c_vp]),
+    "gs_export_rows": (ctypes.c_int, [c_vp, i64, c_vp, i64] + [ctypes.c_int] * 6 + [c_vp, i64, c_vp]),
     "gs_l1_dssim_scratch_bytes": (ctypes.c_size_t, [i32, i32]),
     "gs_l1_dssim_loss": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, i32, i32, ctypes.c_float, ctypes.c_float, c_vp,
                                         c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),

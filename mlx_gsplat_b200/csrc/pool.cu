@@ -1,6 +1,7 @@
 // Pool maintenance kernels: row pattern fill (gradient rows of Gaussians a
-// view does not see) and single-column fill (the periodic opacity reset,
-// mlx_gsplat/trainer.py:416-419).
+// view does not see), single-column fill (the periodic opacity reset,
+// mlx_gsplat/trainer.py:416-419) and the export gather of the active rows
+// (mlx_gsplat/trainer.py:570-631).
 #include "common.cuh"
 
 namespace gs {
@@ -28,9 +29,61 @@ __global__ void fill_column_kernel(float* __restrict__ dst, int64_t n, int64_t s
     if (r < n) dst[r * stride + col] = value;
 }
 
+// One export row per active id (trainer.py:570-600): means | 0 0 0 | colour
+// columns | opacity logit clipped to [-5, 2] | log-scales clipped to
+// [-10, -2] | the quaternion divided by (|q| + 1e-8).  The float32 operations
+// follow NumPy's for the same expressions (the norm sums the four squares
+// left to right; clipping keeps NaN), so the rows match the reference's bit
+// for bit.
+__device__ __forceinline__ float clip_keep_nan(float x, float lo, float hi) {
+    return x != x ? x : fminf(fmaxf(x, lo), hi);
+}
+
+__global__ void export_rows_kernel(const float* __restrict__ theta, int64_t stride, const int32_t* __restrict__ table,
+                                   int64_t n, int mean_col, int opac_col, int scale_col, int quat_col, int color_col,
+                                   int color_cols, float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* r = theta + (int64_t)table[i] * stride;
+    const int oc = 3 + 3 + color_cols + 1 + 3 + 4;
+    float* o = out + i * oc;
+    for (int k = 0; k < 3; ++k) o[k] = r[mean_col + k];
+    for (int k = 0; k < 3; ++k) o[3 + k] = 0.f;
+    for (int k = 0; k < color_cols; ++k) o[6 + k] = r[color_col + k];
+    o[6 + color_cols] = clip_keep_nan(r[opac_col], -5.f, 2.f);
+    for (int k = 0; k < 3; ++k) o[7 + color_cols + k] = clip_keep_nan(r[scale_col + k], -10.f, -2.f);
+    const float q0 = r[quat_col], q1 = r[quat_col + 1], q2 = r[quat_col + 2], q3 = r[quat_col + 3];
+    float ss = __fmul_rn(q0, q0);
+    ss = __fadd_rn(ss, __fmul_rn(q1, q1));
+    ss = __fadd_rn(ss, __fmul_rn(q2, q2));
+    ss = __fadd_rn(ss, __fmul_rn(q3, q3));
+    const float nrm = __fadd_rn(__fsqrt_rn(ss), 1e-8f);
+    float* oq = o + 10 + color_cols;
+    oq[0] = __fdiv_rn(q0, nrm);
+    oq[1] = __fdiv_rn(q1, nrm);
+    oq[2] = __fdiv_rn(q2, nrm);
+    oq[3] = __fdiv_rn(q3, nrm);
+}
+
 }  // namespace gs
 
 using namespace gs;
+
+extern "C" int gs_export_rows(const float* theta, int64_t stride, const int32_t* table, int64_t num_active,
+                              int mean_col, int opac_col, int scale_col, int quat_col, int color_col, int color_cols,
+                              float* out, int64_t out_cols, gs_stream_t stream) {
+    GS_REQUIRE(num_active >= 0 && stride > 0 && color_cols >= 0, "export_rows: bad sizes");
+    GS_REQUIRE(out_cols == 14 + (int64_t)color_cols, "export_rows: out_cols must be 14 + color_cols");
+    GS_REQUIRE(mean_col >= 0 && mean_col + 3 <= stride && opac_col >= 0 && opac_col < stride && scale_col >= 0 &&
+                   scale_col + 3 <= stride && quat_col >= 0 && quat_col + 4 <= stride && color_col >= 0 &&
+                   color_col + color_cols <= stride,
+               "export_rows: column out of the row");
+    if (num_active == 0) return GS_OK;
+    GS_REQUIRE(theta && table && out, "export_rows: null pointer");
+    export_rows_kernel<<<grid_for(num_active, 256), 256, 0, (cudaStream_t)stream>>>(
+        theta, stride, table, num_active, mean_col, opac_col, scale_col, quat_col, color_col, color_cols, out);
+    return check_launch("export_rows_kernel");
+}
 
 extern "C" int gs_fill_rows(float* dst, int64_t n_rows, int64_t stride, const float* pattern_host,
                             gs_stream_t stream) {

@@ -318,6 +318,69 @@ class RunnerMLX:
         P = f.cam.render_width * f.cam.render_height
         return f.loss_partials.sum() / (3.0 * P)
 
+    # ------------------------------------------------------------------ export / checkpoint
+    def export_to_ply(self, filepath: str) -> int:
+        """trainer.py:570-631: the active Gaussians as a binary little-endian PLY
+        (quaternions normalised, log-scales and opacity logits clipped).  The
+        rows are gathered on the GPU (``gs_export_rows``); returns the count."""
+        L = self.layout
+        if "sh0" not in L.offsets:
+            raise NotImplementedError("PLY export needs the SH colour layout (sh0 + shN)")
+        lib = _lib.lib()
+        al = self.allocator
+        n = al.num_active
+        cols = 14 + L.color_cols  # means 3, normals 3, colours, opacity 1, scales 3, quaternion 4
+        out = torch.empty((max(n, 1), cols), dtype=torch.float32, device=self.device)
+        _lib.check(lib.gs_export_rows(al.theta.data_ptr(), L.stride, al.indirection_table.data_ptr(), n,
+                                      L.offsets["means"], L.offsets["opacities"], L.offsets["scales"], L.quat_col,
+                                      L.color_col, L.color_cols, out.data_ptr(), cols,
+                                      _lib.stream_ptr(self.device)), "export rows")
+        rows = out[:n].cpu().numpy()
+        head = [b"ply\n", b"format binary_little_endian 1.0\n", f"element vertex {n}\n".encode()]
+        head += [f"property float {p}\n".encode() for p in ("x", "y", "z", "nx", "ny", "nz")]
+        head += [f"property float f_dc_{j}\n".encode() for j in range(L.dims["sh0"])]
+        head += [f"property float f_rest_{j}\n".encode() for j in range(L.dims["shN"])]
+        head += [b"property float opacity\n"]
+        head += [f"property float scale_{i}\n".encode() for i in range(3)]
+        head += [f"property float rot_{i}\n".encode() for i in range(4)]
+        head += [b"end_header\n"]
+        with open(filepath, "wb") as f:
+            f.write(b"".join(head))
+            f.write(rows.astype("<f4").tobytes())
+        return n
+
+    _CKPT_TENSORS = ("theta", "adam_m", "adam_v", "free_stack", "active_mask", "grad2d", "count")
+
+    def save_checkpoint(self, filepath: str) -> None:
+        """The whole training state: the pooled parameter and moment slabs, the
+        indirection table, the free list, the densification statistics, the
+        Adam step and the trainer's step count (``.npz``)."""
+        al = self.allocator
+        torch.cuda.synchronize(self.device)
+        state = {k: getattr(al, k).cpu().numpy() for k in self._CKPT_TENSORS}
+        state["indirection_table"] = al.indirection_table.cpu().numpy()
+        state["free_top"] = np.int64(al.free_top)
+        state["adam_t"] = np.int64(self.optimizer.t)
+        state["step_count"] = np.int64(self.step_count)
+        state["layout"] = np.array([al.max_gaussians, al.layout.stride, al.layout.ncols], np.int64)
+        np.savez(filepath, **state)
+
+    def load_checkpoint(self, filepath: str) -> None:
+        """Restores a ``save_checkpoint`` state into this runner (same pool size
+        and layout); the pools keep their device addresses."""
+        al = self.allocator
+        d = np.load(filepath)
+        want = np.array([al.max_gaussians, al.layout.stride, al.layout.ncols], np.int64)
+        if not np.array_equal(d["layout"], want):
+            raise ValueError(f"checkpoint pool {d['layout'].tolist()} does not match {want.tolist()}")
+        for k in self._CKPT_TENSORS:
+            getattr(al, k).copy_(torch.from_numpy(d[k]))
+        al.indirection_table = torch.from_numpy(d["indirection_table"]).to(self.device)
+        al.free_top = int(d["free_top"])
+        al.update_cached_pointers()
+        self.optimizer.t = int(d["adam_t"])
+        self.step_count = int(d["step_count"])
+
     # ------------------------------------------------------------------ full loop
     def train(self, log_every: int = 20):
         cfg = self.cfg
