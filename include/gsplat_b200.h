@@ -47,6 +47,23 @@ unsigned long long gs_kernel_launches(void);
 
 /* ------------------------------------------------------------------ types */
 
+/* How the rasterizer turns a Gaussian's colour row into RGB.
+ *
+ * GS_SH_REFERENCE — mlx_gsplat/rendering.py:229-244: the DC term, plus the
+ *   degree-1 term when colors_dim >= 12, whatever the number of stored
+ *   coefficients.  Row layout: c[0..2] DC (r, g, b); channel ch's degree-1
+ *   coefficients at c[3 + 3ch + (0, 1, 2)], multiplying (y, z, x) of the unit
+ *   view direction, all with sign +.
+ * GS_SH_FULL — real spherical harmonics up to the degree d that colors_dim
+ *   holds (3 (d+1)^2 floats: 3 -> 0, 12 -> 1, 27 -> 2, 48 -> 3; at most 3).
+ *   With k = (d+1)^2 - 1, channel ch's coefficients are c[3 + k ch + j],
+ *   j < k: the first three are the degree-1 terms of the reference mode
+ *   (same order and signs, so both modes agree for d <= 1), then the five
+ *   degree-2 and the seven degree-3 basis functions (no reference
+ *   counterpart: the reference evaluates degree <= 1 only). */
+#define GS_SH_REFERENCE 0
+#define GS_SH_FULL 1
+
 /* Read-only Gaussian parameters.  Row ``r`` of a group lives at
  * ``ptr + r * stride``.  Rows are addressed by an "active id" ``i``:
  * ``r = table ? table[i] : i``.  Colours use the same row unless
@@ -58,9 +75,10 @@ typedef struct gs_gaussians {
     const float* scales; int64_t scales_stride; /* [., 3] log-scales */
     const float* opac;   int64_t opac_stride;   /* [., 1] opacity logits */
     const float* colors; int64_t colors_stride; /* [., colors_dim] SH coefficients, DC first */
-    int32_t colors_dim;                         /* stored colour floats; >= 12 enables the SH degree-1 term */
+    int32_t colors_dim;                         /* colour floats the rasterizer may read */
     int32_t colors_by_visible;
     const int32_t* table;                       /* optional active-id -> row map */
+    int32_t sh_mode;                            /* GS_SH_REFERENCE (0) or GS_SH_FULL */
 } gs_gaussians;
 
 /* Gradient outputs, one row per active id (never through ``table``). */
@@ -331,6 +349,21 @@ size_t gs_l1_dssim_scratch_bytes(int32_t width, int32_t height);
 int gs_l1_dssim_loss(const float* color, const void* target, int target_is_u8, int32_t width, int32_t height,
                      float l1_weight, float dssim_weight, float* loss_out, float* ssim_out, float* dL_dcolor,
                      void* scratch, size_t scratch_bytes, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ target image */
+
+/* bilinear_resize_mlx (mlx_gsplat/rendering.py:6-38), the trainer's resize of
+ * each step's target to the render size (mlx_gsplat/trainer.py:231-234):
+ * ``src`` HWC [height_in, width_in, channels], uint8 (``src_is_u8`` = 1: each
+ * value is first divided by 255 in float32, the trainer's ``image / 255.0``,
+ * trainer.py:369) or float32; writes float32 HWC [height_out, width_out,
+ * channels] to ``out``.  Sample x of the output reads input column
+ * x * ((width_in - 1) / max(1, width_out - 1)) (the scale rounded to float32)
+ * between its floor and the next column, likewise in y; every float32
+ * operation is the reference's, in its order, so results are bit-identical.
+ * Equal sizes give the input unchanged (scaled by 1/255 for uint8). */
+int gs_resize_bilinear(const void* src, int src_is_u8, int32_t width_in, int32_t height_in, int32_t channels,
+                       float* out, int32_t width_out, int32_t height_out, gs_stream_t stream);
 
 /* ------------------------------------------------------------------ multi-GPU */
 

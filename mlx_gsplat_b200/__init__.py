@@ -7,13 +7,17 @@ Importing the package needs no GPU; every compute call goes to
 fails loudly without it.
 """
 from .allocator import PointerStableChunkedAllocator
+from .dataset import Dataset, Parser
 from .optimizer import FusedMLXAdam
-from .rendering import RasterSettings, frustum_culling_mlx, rasterize_gaussians_mlx
+from .rendering import RasterSettings, bilinear_resize_mlx, frustum_culling_mlx, rasterize_gaussians_mlx
 
 __all__ = [
     "PointerStableChunkedAllocator",
     "FusedMLXAdam",
     "frustum_culling_mlx",
     "rasterize_gaussians_mlx",
+    "bilinear_resize_mlx",
     "RasterSettings",
+    "Parser",
+    "Dataset",
 ]

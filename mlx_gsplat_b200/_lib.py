@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(PKG, "libgsplat_b200.so")
 GS_OK, GS_ERR_INVALID, GS_ERR_CUDA, GS_ERR_CAPACITY = 0, 1, 2, 3
 GS_ADAM_FUSED, GS_ADAM_PURE, GS_ADAM_EXACT = 0, 1, 0x100
 GS_LOSS_NONE, GS_LOSS_L1_U8, GS_LOSS_L1_F32, GS_LOSS_MEAN = 0, 1, 2, 3
+GS_SH_REFERENCE, GS_SH_FULL = 0, 1
 
 c_float_p = ctypes.POINTER(ctypes.c_float)
 c_vp = ctypes.c_void_p
@@ -31,7 +32,7 @@ class GsGaussians(ctypes.Structure):
                 ("opac", c_vp), ("opac_stride", i64),
                 ("colors", c_vp), ("colors_stride", i64),
                 ("colors_dim", i32), ("colors_by_visible", i32),
-                ("table", c_vp)]
+                ("table", c_vp), ("sh_mode", i32)]
 
 
 class GsGaussianGrads(ctypes.Structure):
@@ -98,6 +99,7 @@ _SIGS = {
     "gs_l1_dssim_scratch_bytes": (ctypes.c_size_t, [i32, i32]),
     "gs_l1_dssim_loss": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, i32, i32, ctypes.c_float, ctypes.c_float, c_vp,
                                         c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "gs_resize_bilinear": (ctypes.c_int, [c_vp, ctypes.c_int, i32, i32, i32, c_vp, i32, i32, c_vp]),
     "gs_group_barrier": (ctypes.c_int, [c_vp, i32, i32, i32, ctypes.c_uint32, c_vp, i64, c_vp]),
     "gs_rows_sum_multicast": (ctypes.c_int, [c_vp, i64, i64, i64, c_vp]),
     "gs_compact_flags": (ctypes.c_int, [c_vp, i64, ctypes.c_uint8, ctypes.c_uint8, c_vp, c_vp, c_vp, c_vp,

@@ -67,13 +67,32 @@ __device__ __forceinline__ int64_t param_row(const gs_gaussians& g, int32_t id) 
     return g.table ? (int64_t)__ldg(g.table + id) : (int64_t)id;
 }
 
+// Colour rows the projection kernels are compiled for: kDeg = 1 covers the
+// reference rule (DC, plus degree 1 when colors_dim >= 12) and GS_SH_FULL at
+// degree <= 1; kDeg = 2 and 3 are GS_SH_FULL at that degree.  kPerCh is the
+// number of coefficients per channel after the DC term, kCols the colour
+// floats of a row.
+template <int kDeg>
+struct ShRow {
+    static_assert(kDeg >= 1 && kDeg <= 3, "SH degree of a kernel variant must be 1, 2 or 3");
+    static constexpr int kPerCh = (kDeg + 1) * (kDeg + 1) - 1;
+    static constexpr int kCols = 3 + 3 * kPerCh;
+};
+
+// Degree of the kernel variant that evaluates a descriptor's colours.
+inline int sh_kernel_degree(const gs_gaussians& g) {
+    if (g.sh_mode != GS_SH_FULL) return 1;
+    return g.colors_dim >= 48 ? 3 : (g.colors_dim >= 27 ? 2 : 1);
+}
+
 // The parameters the projection reads for one Gaussian.
+template <int kDeg>
 struct GaussianIn {
     float mx, my, mz;
     float qw, qx, qy, qz;
     float ls[3];    // log-scales
     float logit;    // opacity logit
-    float col[12];  // SH degree 0 (3) and, with colors_dim >= 12, degree 1 (9)
+    float col[ShRow<kDeg>::kCols];  // DC (3), then kPerCh coefficients per channel
 };
 
 // The pooled row layout, one row per Gaussian: quats (0-3) | means (4-6) |
@@ -83,19 +102,28 @@ struct GaussianIn {
 // vector accesses instead of one scalar access per value.
 constexpr int kRowMean = 4, kRowOpac = 7, kRowScale = 8, kRowColor = 11;
 
+// Colour floats a kernel variant reads from a row (the degree-1 variant reads
+// only the DC term when colors_dim < 12).
+template <int kDeg>
+__host__ __device__ __forceinline__ int sh_cols_read(const gs_gaussians& g) {
+    return kDeg == 1 ? (g.colors_dim >= 12 ? 12 : 3) : ShRow<kDeg>::kCols;
+}
+
+template <int kDeg>
 inline bool slab_rows(const gs_gaussians& g) {
     const int64_t S = g.quats_stride;
-    const int need = kRowColor + (g.colors_dim >= 12 ? 12 : 3);
+    const int need = kRowColor + sh_cols_read<kDeg>(g);
     return g.quats && g.colors_by_visible == 0 && S % 4 == 0 && S >= (need + 3) / 4 * 4 && g.means_stride == S &&
            g.scales_stride == S && g.opac_stride == S && g.colors_stride == S && g.means == g.quats + kRowMean &&
            g.opac == g.quats + kRowOpac && g.scales == g.quats + kRowScale && g.colors == g.quats + kRowColor &&
            (reinterpret_cast<uintptr_t>(g.quats) & 15u) == 0;
 }
 
-template <bool kSlab>
-__device__ __forceinline__ void load_gaussian(const gs_gaussians& g, int64_t row, int64_t crow, GaussianIn& in) {
+template <bool kSlab, int kDeg>
+__device__ __forceinline__ void load_gaussian(const gs_gaussians& g, int64_t row, int64_t crow, GaussianIn<kDeg>& in) {
+    constexpr int NC = ShRow<kDeg>::kCols;
     const bool sh1 = g.colors_dim >= 12;
-    if (kSlab) {
+    if (kSlab && kDeg == 1) {
         const float4* r = reinterpret_cast<const float4*>(g.quats + row * g.quats_stride);
         const float4 a = __ldg(r), b = __ldg(r + 1), c = __ldg(r + 2), d = __ldg(r + 3);
         in.qw = a.x, in.qx = a.y, in.qy = a.z, in.qz = a.w;
@@ -107,7 +135,26 @@ __device__ __forceinline__ void load_gaussian(const gs_gaussians& g, int64_t row
             in.col[3] = d.z, in.col[4] = d.w;
             in.col[5] = e.x, in.col[6] = e.y, in.col[7] = e.z, in.col[8] = e.w;
             in.col[9] = f.x, in.col[10] = f.y, in.col[11] = f.z;
+        } else {
+#pragma unroll
+            for (int k = 3; k < NC; ++k) in.col[k] = 0.f;
         }
+    } else if (kSlab) {
+        // the whole row up to the last colour float, 16 bytes at a time
+        constexpr int kVec = (kRowColor + NC + 3) / 4;
+        const float4* r = reinterpret_cast<const float4*>(g.quats + row * g.quats_stride);
+        float buf[4 * kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            const float4 t = __ldg(r + j);
+            buf[4 * j] = t.x, buf[4 * j + 1] = t.y, buf[4 * j + 2] = t.z, buf[4 * j + 3] = t.w;
+        }
+        in.qw = buf[0], in.qx = buf[1], in.qy = buf[2], in.qz = buf[3];
+        in.mx = buf[kRowMean], in.my = buf[kRowMean + 1], in.mz = buf[kRowMean + 2];
+        in.logit = buf[kRowOpac];
+        in.ls[0] = buf[kRowScale], in.ls[1] = buf[kRowScale + 1], in.ls[2] = buf[kRowScale + 2];
+#pragma unroll
+        for (int k = 0; k < NC; ++k) in.col[k] = buf[kRowColor + k];
     } else {
         const float* mp = g.means + row * g.means_stride;
         const float* qp = g.quats + row * g.quats_stride;
@@ -117,14 +164,74 @@ __device__ __forceinline__ void load_gaussian(const gs_gaussians& g, int64_t row
         in.qw = __ldg(qp), in.qx = __ldg(qp + 1), in.qy = __ldg(qp + 2), in.qz = __ldg(qp + 3);
         in.ls[0] = __ldg(sp), in.ls[1] = __ldg(sp + 1), in.ls[2] = __ldg(sp + 2);
         in.logit = __ldg(g.opac + row * g.opac_stride);
-        const int nc = sh1 ? 12 : 3;
+        const int nc = sh_cols_read<kDeg>(g);
 #pragma unroll
-        for (int k = 0; k < 12; ++k) in.col[k] = k < nc ? __ldg(cp + k) : 0.f;
+        for (int k = 0; k < NC; ++k) in.col[k] = k < nc ? __ldg(cp + k) : 0.f;
     }
 }
 
-// rendering.py:153-244 for one Gaussian.
-__device__ __forceinline__ void project_one(const GaussianIn& in, bool sh1, const RasterParams& p, ProjState& s) {
+// ------------------------------------------------------------------ spherical harmonics, degrees 2 and 3
+// Real SH basis functions of a unit direction (x, y, z), as polynomials with
+// their normalisation constants K_lm = sqrt((2l+1)/(4 pi) * (l-|m|)!/(l+|m|)!)
+// times the Legendre factor, in the sign convention common to 3DGS renderers:
+//   degree 2:  K0 xy, -K0 yz, K1 (2z^2 - x^2 - y^2), -K0 xz, K2 (x^2 - y^2)
+//              K0 = sqrt(15/pi)/2, K1 = sqrt(5/pi)/4, K2 = sqrt(15/pi)/4
+//   degree 3:  -K3 y(3x^2 - y^2), K4 xyz, -K5 y(4z^2 - x^2 - y^2),
+//              K6 z(2z^2 - 3x^2 - 3y^2), -K5 x(4z^2 - x^2 - y^2),
+//              K7 z(x^2 - y^2), -K3 x(x^2 - 3y^2)
+//              K3 = sqrt(35/(2pi))/4, K4 = sqrt(105/pi)/2, K5 = sqrt(21/(2pi))/4,
+//              K6 = sqrt(7/pi)/4, K7 = sqrt(105/pi)/4
+constexpr float kShK0 = 1.0925484305920792f, kShK1 = 0.31539156525252005f, kShK2 = 0.5462742152960396f;
+constexpr float kShK3 = 0.5900435899266435f, kShK4 = 2.890611442640554f, kShK5 = 0.4570457994644658f;
+constexpr float kShK6 = 0.3731763325901154f, kShK7 = 1.445305721320277f;
+
+// b[0..4] = degree-2 basis, b[5..11] = degree-3 basis (when kDeg == 3).
+template <int kDeg>
+__device__ __forceinline__ void sh_basis_hi(float x, float y, float z, float* b) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    b[0] = kShK0 * x * y;
+    b[1] = -kShK0 * y * z;
+    b[2] = kShK1 * (2.f * zz - xx - yy);
+    b[3] = -kShK0 * x * z;
+    b[4] = kShK2 * (xx - yy);
+    if (kDeg >= 3) {
+        b[5] = -kShK3 * y * (3.f * xx - yy);
+        b[6] = kShK4 * x * y * z;
+        b[7] = -kShK5 * y * (4.f * zz - xx - yy);
+        b[8] = kShK6 * z * (2.f * zz - 3.f * xx - 3.f * yy);
+        b[9] = -kShK5 * x * (4.f * zz - xx - yy);
+        b[10] = kShK7 * z * (xx - yy);
+        b[11] = -kShK3 * x * (xx - 3.f * yy);
+    }
+}
+
+// Gradient with respect to (x, y, z) of sum_j w[j] b_j(x, y, z) for the basis
+// of sh_basis_hi (the direction's components taken as independent).
+template <int kDeg>
+__device__ __forceinline__ void sh_basis_hi_grad(float x, float y, float z, const float* w, float& gx, float& gy,
+                                                 float& gz) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    gx = kShK0 * w[0] * y - kShK0 * w[3] * z - 2.f * kShK1 * w[2] * x + 2.f * kShK2 * w[4] * x;
+    gy = kShK0 * w[0] * x - kShK0 * w[1] * z - 2.f * kShK1 * w[2] * y - 2.f * kShK2 * w[4] * y;
+    gz = -kShK0 * w[1] * y - kShK0 * w[3] * x + 4.f * kShK1 * w[2] * z;
+    if (kDeg >= 3) {
+        gx += -kShK3 * w[5] * 6.f * x * y + kShK4 * w[6] * y * z + kShK5 * w[7] * 2.f * x * y -
+              kShK6 * w[8] * 6.f * x * z - kShK5 * w[9] * (4.f * zz - 3.f * xx - yy) + kShK7 * w[10] * 2.f * x * z -
+              kShK3 * w[11] * 3.f * (xx - yy);
+        gy += -kShK3 * w[5] * 3.f * (xx - yy) + kShK4 * w[6] * x * z - kShK5 * w[7] * (4.f * zz - xx - 3.f * yy) -
+              kShK6 * w[8] * 6.f * y * z + kShK5 * w[9] * 2.f * x * y - kShK7 * w[10] * 2.f * y * z +
+              kShK3 * w[11] * 6.f * x * y;
+        gz += kShK4 * w[6] * x * y - kShK5 * w[7] * 8.f * y * z + kShK6 * w[8] * (6.f * zz - 3.f * xx - 3.f * yy) -
+              kShK5 * w[9] * 8.f * x * z + kShK7 * w[10] * (xx - yy);
+    }
+}
+
+// rendering.py:153-244 for one Gaussian.  ``sh1``: the degree-1 term is
+// evaluated (kDeg = 1 only; the higher variants always evaluate every degree
+// up to kDeg).
+template <int kDeg>
+__device__ __forceinline__ void project_one(const GaussianIn<kDeg>& in, bool sh1, const RasterParams& p,
+                                            ProjState& s) {
     s.mx = in.mx;
     s.my = in.my;
     s.mz = in.mz;
@@ -200,16 +307,31 @@ __device__ __forceinline__ void project_one(const GaussianIn& in, bool sh1, cons
     s.dir[0] = dx * inv;
     s.dir[1] = dy * inv;
     s.dir[2] = dz * inv;
-    float c0 = in.col[0] * kSH_C0, c1 = in.col[1] * kSH_C0, c2 = in.col[2] * kSH_C0;
-    if (sh1) {
+    constexpr int k = ShRow<kDeg>::kPerCh;
+    float c[3] = {in.col[0] * kSH_C0, in.col[1] * kSH_C0, in.col[2] * kSH_C0};
+    if (kDeg > 1 || sh1) {
         const float xd = s.dir[0], yd = s.dir[1], zd = s.dir[2];
-        c0 += kSH_C1 * (in.col[3] * yd + in.col[4] * zd + in.col[5] * xd);
-        c1 += kSH_C1 * (in.col[6] * yd + in.col[7] * zd + in.col[8] * xd);
-        c2 += kSH_C1 * (in.col[9] * yd + in.col[10] * zd + in.col[11] * xd);
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            const float* cc = in.col + 3 + k * ch;
+            c[ch] += kSH_C1 * (cc[0] * yd + cc[1] * zd + cc[2] * xd);
+        }
+        if (kDeg > 1) {
+            float b[12];
+            sh_basis_hi<kDeg>(xd, yd, zd, b);
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                const float* cc = in.col + 3 + k * ch + 3;
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < k - 3; ++j) acc += cc[j] * b[j];
+                c[ch] += acc;
+            }
+        }
     }
-    s.pre[0] = c0 + 0.5f;
-    s.pre[1] = c1 + 0.5f;
-    s.pre[2] = c2 + 0.5f;
+    s.pre[0] = c[0] + 0.5f;
+    s.pre[1] = c[1] + 0.5f;
+    s.pre[2] = c[2] + 0.5f;
 #pragma unroll
     for (int k = 0; k < 3; ++k) s.rgb[k] = fminf(fmaxf(s.pre[k], 0.0f), 1.0f);
 }

@@ -294,7 +294,7 @@ inline bool slab_grad_rows(const gs_gaussian_grads& o) {
            (reinterpret_cast<uintptr_t>(o.quats) & 15u) == 0;
 }
 
-template <bool kSlabIn, bool kSlabOut>
+template <bool kSlabIn, bool kSlabOut, int kDeg>
 __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
                                                           RasterParams p, const float* __restrict__ splat_grads,
                                                           gs_gaussian_grads o, float* __restrict__ grad2d,
@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     if (vi >= nv) return;
     const int32_t id = ids[vi];
     const int64_t row = param_row(g, id);
-    GaussianIn in;
+    GaussianIn<kDeg> in;
     load_gaussian<kSlabIn>(g, row, g.colors_by_visible ? vi : row, in);
     ProjState s;
     project_one(in, g.colors_dim >= 12, p, s);
@@ -400,30 +400,46 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
     // ---- opacity
     const float dlogit = dop * s.opac * (1.f - s.opac);
 
-    // ---- colour: clip mask, SH0, SH1 and the direction's dependence on the mean
+    // ---- colour: clip mask, SH0, SH1 (and degrees 2-3) and the direction's dependence on the mean
+    constexpr int NC = ShRow<kDeg>::kCols, KC = ShRow<kDeg>::kPerCh;
     float dpre[3];
 #pragma unroll
     for (int k = 0; k < 3; ++k) dpre[k] = (s.pre[k] > 0.f && s.pre[k] < 1.f) ? drgb[k] : 0.f;
-    float dcol[12];
+    float dcol[NC];
 #pragma unroll
     for (int k = 0; k < 3; ++k) dcol[k] = dpre[k] * kSH_C0;
-    const bool sh1 = g.colors_dim >= 12;
+    const bool sh1 = kDeg > 1 || g.colors_dim >= 12;
     if (sh1) {
         const float xd = s.dir[0], yd = s.dir[1], zd = s.dir[2];
-#pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-            const float e = kSH_C1 * dpre[ch];
-            dcol[3 + 3 * ch + 0] = e * yd;
-            dcol[3 + 3 * ch + 1] = e * zd;
-            dcol[3 + 3 * ch + 2] = e * xd;
-        }
         float ddir[3] = {0.f, 0.f, 0.f};
 #pragma unroll
         for (int ch = 0; ch < 3; ++ch) {
             const float e = kSH_C1 * dpre[ch];
-            ddir[1] += e * in.col[3 + 3 * ch + 0];
-            ddir[2] += e * in.col[3 + 3 * ch + 1];
-            ddir[0] += e * in.col[3 + 3 * ch + 2];
+            const int c0 = 3 + KC * ch;
+            dcol[c0 + 0] = e * yd;
+            dcol[c0 + 1] = e * zd;
+            dcol[c0 + 2] = e * xd;
+            ddir[1] += e * in.col[c0 + 0];
+            ddir[2] += e * in.col[c0 + 1];
+            ddir[0] += e * in.col[c0 + 2];
+        }
+        if (kDeg > 1) {
+            float b[12], w[12];
+            sh_basis_hi<kDeg>(xd, yd, zd, b);
+#pragma unroll
+            for (int j = 0; j < KC - 3; ++j) {
+                w[j] = 0.f;
+#pragma unroll
+                for (int ch = 0; ch < 3; ++ch) {
+                    dcol[3 + KC * ch + 3 + j] = dpre[ch] * b[j];
+                    w[j] += dpre[ch] * in.col[3 + KC * ch + 3 + j];
+                }
+            }
+            float gx, gy, gz;
+            sh_basis_hi_grad<kDeg>(xd, yd, zd, w, gx, gy, gz);
+            ddir[0] += gx;
+            ddir[1] += gy;
+            ddir[2] += gz;
         }
         const float n = s.dnorm, ne = n + 1e-8f;
         const float dx = s.mx - p.campos[0], dy = s.my - p.campos[1], dzz = s.mz - p.campos[2];
@@ -433,7 +449,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
         dm[2] += ddir[2] / ne - dzz * proj;
     } else {
 #pragma unroll
-        for (int k = 3; k < 12; ++k) dcol[k] = 0.f;
+        for (int k = 3; k < NC; ++k) dcol[k] = 0.f;
     }
 
     // ---- outputs
@@ -449,9 +465,10 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
         dm[k] += reg;
     }
     if (kSlabOut) {
-        // the row's first 24 columns from registers, 16 bytes at a time; the
-        // colour columns past SH degree 1 hold only the regulariser
-        float vals[24];
+        // the row's first kVals columns from registers, 16 bytes at a time; the
+        // colour columns past the evaluated degree hold only the regulariser
+        constexpr int kVals = (kRowColor + NC + 1 + 3) / 4 * 4;
+        float vals[kVals];
 #pragma unroll
         for (int k = 0; k < 4; ++k) vals[k] = dquat[k] + reg_geo;
 #pragma unroll
@@ -460,11 +477,12 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
 #pragma unroll
         for (int k = 0; k < 3; ++k) vals[kRowScale + k] = dscale[k] + reg_geo;
 #pragma unroll
-        for (int k = 0; k < 13; ++k) vals[kRowColor + k] = (k < 12 ? dcol[k] : 0.f) + (k < o.reg_color_cols ? reg : 0.f);
+        for (int k = 0; k < kVals - kRowColor; ++k)
+            vals[kRowColor + k] = (k < NC ? dcol[k] : 0.f) + (k < o.reg_color_cols ? reg : 0.f);
         float* rowp = o.quats + (int64_t)id * o.quats_stride;
         const int W = kRowColor + o.colors_write;
 #pragma unroll
-        for (int j = 0; j < 6; ++j) {
+        for (int j = 0; j < kVals / 4; ++j) {
             if (4 * j + 3 < W) {
                 reinterpret_cast<float4*>(rowp)[j] = make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2],
                                                                  vals[4 * j + 3]);
@@ -474,7 +492,7 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
                     if (4 * j + c < W) rowp[4 * j + c] = vals[4 * j + c];
             }
         }
-        for (int c = 24; c < W; c += 4) {
+        for (int c = kVals; c < W; c += 4) {
             float t[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) t[u] = c + u - kRowColor < o.reg_color_cols ? reg : 0.f;
@@ -504,7 +522,10 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
         const int64_t orow = o.colors_by_visible ? vi : (int64_t)id;
         float* dst = o.colors + orow * o.colors_stride;
         for (int k = 0; k < o.colors_write; ++k) {
-            float val = k < 12 ? dcol[k] : 0.f;
+            float val = 0.f;
+#pragma unroll
+            for (int j = 0; j < NC; ++j)  // register-resident select instead of a dynamic index
+                if (j == k) val = dcol[j];
             if (k < o.reg_color_cols) val += reg;
             put(dst, k, val, acc);
         }
@@ -553,9 +574,15 @@ extern "C" int gs_project_backward(const gs_gaussians* g, const int32_t* ids, in
     GS_REQUIRE(!grad2d || count, "project_backward: grad2d needs count");
     GS_REQUIRE(out->colors == nullptr || out->colors_write >= 0, "project_backward: bad colors_write");
     const RasterParams p = make_raster_params(*cam, nullptr);
-    const bool in_rows = slab_rows(*g), out_rows = slab_grad_rows(*out);
-    auto kernel = in_rows ? (out_rows ? project_bwd_kernel<true, true> : project_bwd_kernel<true, false>)
-                          : (out_rows ? project_bwd_kernel<false, true> : project_bwd_kernel<false, false>);
+    GS_REQUIRE(g->sh_mode == GS_SH_REFERENCE || g->sh_mode == GS_SH_FULL, "project_backward: bad sh_mode");
+    const int deg = sh_kernel_degree(*g);
+    const bool out_rows = slab_grad_rows(*out);
+    const bool in_rows = deg == 3 ? slab_rows<3>(*g) : deg == 2 ? slab_rows<2>(*g) : slab_rows<1>(*g);
+#define GS_PBWD(D)                                                                                   \
+    (in_rows ? (out_rows ? project_bwd_kernel<true, true, D> : project_bwd_kernel<true, false, D>) \
+             : (out_rows ? project_bwd_kernel<false, true, D> : project_bwd_kernel<false, false, D>))
+    auto kernel = deg == 3 ? GS_PBWD(3) : deg == 2 ? GS_PBWD(2) : GS_PBWD(1);
+#undef GS_PBWD
     kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p, splat_grads, *out,
                                                                          grad2d, count);
     return check_launch("project_bwd_kernel");

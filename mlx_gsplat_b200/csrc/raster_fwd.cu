@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kBigThreads) bin_emit_big_kernel(const float4*
 }
 
 // ---------------------------------------------------------------- projection + tile count
-template <bool kSlab>
+template <bool kSlab, int kDeg>
 __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids,
                                                           int64_t nv, RasterParams p, float4* __restrict__ splats,
                                                           uint32_t* __restrict__ depth_keys,
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const 
     if (active) {
         const int32_t id = ids[vi];
         const int64_t row = param_row(g, id);
-        GaussianIn in;
+        GaussianIn<kDeg> in;
         load_gaussian<kSlab>(g, row, g.colors_by_visible ? vi : row, in);
         ProjState s;
         project_one(in, g.colors_dim >= 12, p, s);
@@ -645,6 +645,7 @@ extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int
     GS_REQUIRE(ids && splats && depth_keys && tile_counts && g->means && g->quats && g->scales && g->opac && g->colors,
                "project_forward: null pointer");
     GS_REQUIRE(g->colors_dim >= 3, "project_forward: colors_dim must be >= 3");
+    GS_REQUIRE(g->sh_mode == GS_SH_REFERENCE || g->sh_mode == GS_SH_FULL, "project_forward: bad sh_mode");
     GS_REQUIRE(aligned16(splats), "project_forward: splats must be 16-byte aligned");
     GS_REQUIRE(cam->render_width > 0 && cam->render_height > 0 && cam->width > 0 && cam->height > 0,
                "project_forward: bad image size");
@@ -652,7 +653,10 @@ extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int
     const bool use_bs = bin_scratch != nullptr;
     const BinScratch bs = use_bs ? bin_scratch_layout(bin_scratch, num_visible) : BinScratch{};
     if (use_bs) cudaMemsetAsync(bs.big_count, 0, sizeof(uint32_t), (cudaStream_t)stream);
-    auto kernel = slab_rows(*g) ? project_fwd_kernel<true> : project_fwd_kernel<false>;
+    const int deg = sh_kernel_degree(*g);
+    auto kernel = deg == 3   ? (slab_rows<3>(*g) ? project_fwd_kernel<true, 3> : project_fwd_kernel<false, 3>)
+                  : deg == 2 ? (slab_rows<2>(*g) ? project_fwd_kernel<true, 2> : project_fwd_kernel<false, 2>)
+                             : (slab_rows<1>(*g) ? project_fwd_kernel<true, 1> : project_fwd_kernel<false, 1>);
     kernel<<<grid_for(num_visible, 128), 128, 0, (cudaStream_t)stream>>>(*g, ids, num_visible, p,
                                                                         reinterpret_cast<float4*>(splats),
                                                                         depth_keys, tile_counts, use_bs, bs);

@@ -80,8 +80,22 @@ def _rows(t: Optional[torch.Tensor], cols: int, name: str):
     return t2.data_ptr(), t2.stride(0)
 
 
+SH_MODES = {"reference": _lib.GS_SH_REFERENCE, "full": _lib.GS_SH_FULL}
+
+
+def sh_mode_code(sh_mode) -> int:
+    """``"reference"`` (mlx_gsplat/rendering.py:229-244: SH degree <= 1) or
+    ``"full"`` (real SH up to the degree the colour rows hold, at most 3)."""
+    if isinstance(sh_mode, str):
+        if sh_mode not in SH_MODES:
+            raise ValueError(f"sh_mode must be one of {sorted(SH_MODES)}, got {sh_mode!r}")
+        return SH_MODES[sh_mode]
+    return int(sh_mode)
+
+
 def gaussians_struct(means, quats=None, scales=None, opacities=None, colors=None, colors_dim: Optional[int] = None,
-                     colors_by_visible: bool = False, table: Optional[torch.Tensor] = None) -> GsGaussians:
+                     colors_by_visible: bool = False, table: Optional[torch.Tensor] = None,
+                     sh_mode="reference") -> GsGaussians:
     g = GsGaussians()
     g.means, g.means_stride = _rows(means, 3, "means")
     g.quats, g.quats_stride = _rows(quats, 4, "quats")
@@ -92,6 +106,7 @@ def gaussians_struct(means, quats=None, scales=None, opacities=None, colors=None
         g.colors_dim = int(colors_dim if colors_dim is not None else colors.reshape(colors.shape[0], -1).shape[1])
     g.colors_by_visible = int(colors_by_visible)
     g.table = None if table is None else table.data_ptr()
+    g.sh_mode = sh_mode_code(sh_mode)
     return g
 
 
@@ -119,6 +134,24 @@ def _scratch(nbytes: int, device) -> torch.Tensor:
 
 def _i32(n: int, device) -> torch.Tensor:
     return torch.empty(max(int(n), 1), dtype=torch.int32, device=device)
+
+
+# ----------------------------------------------------------------------------- target image
+def bilinear_resize_mlx(img: torch.Tensor, H_out: int, W_out: int) -> torch.Tensor:
+    """mlx_gsplat/rendering.py:6-38 on the GPU (``gs_resize_bilinear``): HWC
+    float32 ``img`` resized to ``[H_out, W_out, C]``, bit-identical to the
+    reference.  A uint8 ``img`` is taken as ``img / 255.0`` first (the
+    trainer's target scaling), so a cached uint8 image becomes the float
+    target in one pass.  The result is not differentiable (the trainer resizes
+    targets only)."""
+    if not img.is_cuda or img.dtype not in (torch.uint8, torch.float32) or img.dim() != 3:
+        raise TypeError("bilinear_resize_mlx: img must be a CUDA uint8 or float32 HWC tensor")
+    H, W, C = img.shape
+    src = img.contiguous()
+    out = torch.empty((int(H_out), int(W_out), C), dtype=torch.float32, device=img.device)
+    check(_lib.lib().gs_resize_bilinear(src.data_ptr(), int(src.dtype == torch.uint8), W, H, C, out.data_ptr(),
+                                        int(W_out), int(H_out), _lib.stream_ptr(img.device)), "gs_resize_bilinear")
+    return out
 
 
 # ----------------------------------------------------------------------------- cull
@@ -274,9 +307,10 @@ def render_backward(f: TileFrame, g: GsGaussians, out: GsGaussianGrads, device,
 # ----------------------------------------------------------------------------- autograd entry
 class _RasterizeFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, means, quats, scales, opacities, colors, ids, cam, settings, colors_by_visible):
+    def forward(ctx, means, quats, scales, opacities, colors, ids, cam, settings, colors_by_visible, sh_mode):
         device = means.device
-        g = gaussians_struct(means, quats, scales, opacities, colors, colors_by_visible=colors_by_visible)
+        g = gaussians_struct(means, quats, scales, opacities, colors, colors_by_visible=colors_by_visible,
+                             sh_mode=sh_mode)
         V = int(ids.shape[0])
         f = render_forward(g, ids, V, cam, settings, device)
         ctx.frame = f
@@ -300,14 +334,14 @@ class _RasterizeFn(torch.autograd.Function):
         dC = torch.zeros_like(ctx.frame.color) if dC is None else dC.contiguous()
         dA = None if dA is None else dA.contiguous()
         render_backward(ctx.frame, ctx.g, out, device, dL_dcolor=dC, dL_dalpha=dA)
-        return gm, gq, gsc, go, gc, None, None, None, None
+        return gm, gq, gsc, go, gc, None, None, None, None, None
 
 
 def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K, width: int, height: int,
                             active_indices, means_active=None, quats_active=None, scales_active=None,
                             opacities_active=None, render_width: int = 120, render_height: int = 90,
                             pixel_chunk_size: int = 1024, mask=None, raster_settings: Optional[RasterSettings] = None,
-                            **kwargs):
+                            sh_mode: str = "reference", **kwargs):
     """mlx_gsplat/rendering.py:97-308.  Renders the Gaussians selected by
     ``active_indices`` (rows of ``means``/``quats``/``scales``/``opacities``, or
     of their ``*_active`` replacements when given) and returns
@@ -315,7 +349,11 @@ def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K,
     with respect to the five parameter tensors.  ``colors`` is used row per
     visible Gaussian when it has one row per index, otherwise gathered too.
     ``pixel_chunk_size`` is accepted for compatibility (the tiled kernels need
-    no pixel chunking); the per-Gaussian ``mask`` multiplier is not supported."""
+    no pixel chunking); the per-Gaussian ``mask`` multiplier is not supported.
+    ``sh_mode="full"`` evaluates real spherical harmonics up to the degree the
+    colour rows hold (3, 12, 27 or 48 floats: degree 0-3; the reference,
+    ``"reference"``, stops at degree 1), with channel ch's coefficients at
+    ``colors[:, 3 + k*ch : 3 + k*(ch+1)]``, k = (degree+1)**2 - 1."""
     if mask is not None:
         raise NotImplementedError("rasterize_gaussians_mlx: the alpha mask argument is not supported")
     m = means if means_active is None else means_active
@@ -329,4 +367,5 @@ def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K,
                 torch.zeros((render_height, render_width, 1), dtype=torch.float32, device=m.device))
     cam = camera_struct(viewmat, K, width, height, render_width, render_height)
     by_visible = int(colors.shape[0]) == V
-    return _RasterizeFn.apply(m, q, s, o, colors, ids, cam, raster_settings or DEFAULT_SETTINGS, by_visible)
+    return _RasterizeFn.apply(m, q, s, o, colors, ids, cam, raster_settings or DEFAULT_SETTINGS, by_visible,
+                              sh_mode_code(sh_mode))

@@ -23,6 +23,7 @@ active Gaussian and on the gathered colour coefficients of visible ones.
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Tuple
@@ -67,6 +68,16 @@ class MLXConfig:
     near_plane: float = 0.01
     far_plane: float = 1e10
     opacity_threshold: float = -5.3
+    # "reference": colour from SH degree <= 1 as the reference rasterizer does
+    # (rendering.py:229-244); "full": real SH up to the scheduled degree (<= 3)
+    sh_eval: str = "reference"
+    # real-data mode: the reference passes the camera-to-world matrix where the
+    # rasterizer expects world-to-camera (trainer.py:365); True reproduces that
+    c2w_as_viewmat: bool = False
+    # real-data mode: keep the uint8 training images in HBM (else each step
+    # uploads its image from pinned host memory)
+    images_on_device: bool = True
+    seed: int = 0
 
 
 def lr_at(lr: float, step: int, max_steps: int) -> float:
@@ -100,12 +111,77 @@ class StepTimer:
         return out
 
 
+def reference_init(cfg: MLXConfig):
+    """The reference trainer's start (trainer.py:50-136) without MLX: with
+    ``use_real_data`` and a COLMAP model under ``data_dir/sparse/0``, the
+    normalised scene (``Parser(factor=data_factor, normalize=True)``), its train
+    split and Gaussians initialised from the SfM points (log-scale log 0.01,
+    random unit quaternions, opacity logit 0.1, SH DC from the point colours,
+    higher SH zero; at most ``init_gaussians`` points, chosen with seed 42);
+    otherwise the reference's synthetic mode (3,000 random Gaussians seen by
+    an identity camera, K = [[500, 0, 400], [0, 500, 300]], no target).
+    Returns ``(init_params, viewmats, Ks, sizes, scene_scale, train_dataset)``;
+    random draws use ``cfg.seed`` (the reference uses the global NumPy state).
+    A relative ``data_dir`` is taken from the current directory."""
+    from . import dataset as D
+    rng = np.random.default_rng(cfg.seed)
+    data_dir = os.path.abspath(cfg.data_dir)
+    shn_dim = ((cfg.sh_degree + 1) ** 2 - 1) * 3
+    if cfg.use_real_data and os.path.exists(os.path.join(data_dir, "sparse/0")):
+        parser = D.Parser(data_dir=data_dir, factor=cfg.data_factor, normalize=True)
+        ds = D.Dataset(parser, split="train", preload_images=cfg.preload_images, seed=cfg.seed)
+        points = np.array(parser.points, dtype=np.float32)
+        rgbs = np.array(parser.points_rgb / 255.0, dtype=np.float32)
+        n = len(points)
+        if cfg.init_gaussians is not None and cfg.init_gaussians < n:
+            keep = np.random.default_rng(42).choice(n, size=cfg.init_gaussians, replace=False)
+            points, rgbs, n = points[keep], rgbs[keep], cfg.init_gaussians
+        quats = rng.standard_normal((n, 4)).astype(np.float32)
+        quats /= np.linalg.norm(quats, axis=-1, keepdims=True)
+        init = {"means": points,
+                "scales": np.full((n, 3), np.log(np.float32(0.01)), np.float32),
+                "quats": quats,
+                "opacities": np.full((n, 1), 0.1, np.float32),
+                "sh0": ((rgbs - 0.5) / np.float32(synthetic.SH_C0)).astype(np.float32),
+                "shN": np.zeros((n, shn_dim), np.float32)}
+        viewmats, Ks, sizes = [], [], []
+        for i in ds.indices:
+            c2w = parser.camtoworlds[i]
+            viewmats.append(c2w if cfg.c2w_as_viewmat else np.linalg.inv(c2w))
+            cid = parser.camera_ids[i]
+            Ks.append(parser.Ks_dict[cid])
+            sizes.append(parser.imsize_dict[cid])
+        return init, np.stack(viewmats), np.stack(Ks), sizes, float(parser.scene_scale), ds
+    n = 3000
+    init = {"means": rng.standard_normal((n, 3)).astype(np.float32),
+            "scales": np.full((n, 3), np.log(np.float32(0.01)), np.float32),
+            "quats": rng.standard_normal((n, 4)).astype(np.float32),
+            "opacities": np.full((n, 1), 0.1, np.float32),
+            "sh0": rng.standard_normal((n, 3)).astype(np.float32),
+            "shN": rng.standard_normal((n, shn_dim)).astype(np.float32)}
+    K = np.array([[500, 0, 400], [0, 500, 300], [0, 0, 1]], np.float32)
+    return init, np.eye(4, dtype=np.float32)[None], K[None], [(cfg.width, cfg.height)], 1.0, None
+
+
 class RunnerMLX:
-    def __init__(self, cfg: MLXConfig, init_params: Dict[str, np.ndarray], viewmats: np.ndarray, K: np.ndarray,
+    """The training loop of mlx_gsplat/trainer.py:44-631 on B200.
+    ``RunnerMLX(cfg)`` starts as the reference does (``reference_init``: a
+    COLMAP scene, or the synthetic mode); the other arguments give the scene
+    directly (initial Gaussians, world-to-camera ``viewmats`` [V, 4, 4], one
+    ``K`` [3, 3] or one per view, device targets [V, H, W, 3])."""
+
+    def __init__(self, cfg: MLXConfig, init_params: Optional[Dict[str, np.ndarray]] = None,
+                 viewmats: Optional[np.ndarray] = None, K: Optional[np.ndarray] = None,
                  targets: Optional[torch.Tensor] = None, device: Optional[torch.device] = None,
                  scene_scale: float = 1.0, process_group=None, fused_reduce: bool = False):
         self.cfg = cfg
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.train_dataset = None
+        sizes = None
+        if init_params is None:
+            init_params, viewmats, K, sizes, scene_scale, self.train_dataset = reference_init(cfg)
+            if self.train_dataset is not None and cfg.images_on_device and cfg.preload_images:
+                self.train_dataset.to_device(self.device)
         self.allocator = PointerStableChunkedAllocator(cfg.max_gaussians, cfg.sh_degree, device=self.device)
         self.allocator.set_initial_gaussians(init_params)
         self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
@@ -127,9 +203,15 @@ class RunnerMLX:
         self.col_lo, self.col_hi = lo.tolist(), hi.tolist()
         self.viewmats = np.asarray(viewmats, np.float32)
         self.K = np.asarray(K, np.float32)
-        self.cams = [camera_struct(vm, self.K, cfg.width, cfg.height, cfg.render_width, cfg.render_height)
-                     for vm in self.viewmats]
+        Ks = self.K if self.K.ndim == 3 else [self.K] * len(self.viewmats)
+        if self.K.ndim == 3 and len(self.K) == 1:
+            self.K = self.K[0]
+            Ks = [self.K] * len(self.viewmats)
+        sizes = sizes or [(cfg.width, cfg.height)] * len(self.viewmats)
+        self.cams = [camera_struct(vm, k, w, h, cfg.render_width, cfg.render_height)
+                     for vm, k, (w, h) in zip(self.viewmats, Ks, sizes)]
         self.targets = targets
+        self.rng = np.random.default_rng(cfg.seed)
         self.settings = RasterSettings(cfg.alpha_cutoff, cfg.transmittance_min)
         self.scene_scale = scene_scale
         self.last_frame = None
@@ -156,7 +238,7 @@ class RunnerMLX:
         pools = self.allocator.physical_pools
         return gaussians_struct(pools["means"], pools["quats"], pools["scales"], pools["opacities"],
                                 th[:, L.color_col:], colors_dim=sh_cols_for(step, self.cfg),
-                                table=self.allocator.indirection_table)
+                                table=self.allocator.indirection_table, sh_mode=self.cfg.sh_eval)
 
     def _grad_out(self, step: int):
         L = self.layout
@@ -183,6 +265,8 @@ class RunnerMLX:
         cam = self.cams[view_idx % len(self.cams)]
         if target is None and self.targets is not None:
             target = self.targets[view_idx % self.targets.shape[0]]
+        elif target is None and self.train_dataset is not None:
+            target = self.dataset_target(view_idx % len(self.train_dataset))
         ssim_loss = cfg.loss == "l1+dssim" and target is not None
         if cfg.loss not in ("l1", "mean", "l1+dssim"):
             raise ValueError(f"unknown loss {cfg.loss!r} (l1, mean or l1+dssim)")
@@ -248,6 +332,18 @@ class RunnerMLX:
         self.last_frame = frame
         self.step_count += 1
         return frame
+
+    def dataset_target(self, item: int) -> torch.Tensor:
+        """The training image of dataset item ``item`` as this step's target:
+        the uint8 image itself when it has the render size, else
+        ``bilinear_resize_mlx(image / 255.0)`` to the render size
+        (trainer.py:231-234, 369), both on the GPU."""
+        from .rendering import bilinear_resize_mlx
+        img = self.train_dataset.device_image(item, self.device)
+        RH, RW = self.cfg.render_height, self.cfg.render_width
+        if tuple(img.shape[:2]) == (RH, RW):
+            return img
+        return bilinear_resize_mlx(img, RH, RW)
 
     # ------------------------------------------------------------------ densify / prune
     def densify(self, step: int, noise: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[int, int]:
@@ -386,7 +482,10 @@ class RunnerMLX:
         cfg = self.cfg
         t0 = time.time()
         for step in range(1, cfg.max_steps + 1):
-            v = (step - 1) % len(self.cams)
+            if self.train_dataset is not None:
+                v = int(self.rng.integers(0, len(self.train_dataset)))  # trainer.py:362
+            else:
+                v = (step - 1) % len(self.cams)
             self.train_step(v, step)
             if cfg.opacity_reset:
                 interval = 1000 if cfg.max_steps <= 3000 else 3000

@@ -7,6 +7,10 @@ Follows ``mlx_gsplat/rendering.py`` line by line:
   decision is reproducible bit for bit.
 * ``project``          — rendering.py:153-244 (camera transform, covariance,
   EWA projection, depth argsort, conic, sigmoid opacity, SH<=1 colour).
+  ``sh_mode="full"`` extends the colour to real spherical harmonics of
+  degree 2 and 3 (``sh_color_full``); the reference has no such mode, so this
+  part is the library's own definition restated, checked against the
+  reference mode at degree <= 1 and by autograd.
 * ``rasterize_dense``  — rendering.py:246-308, the dense per-pixel compositing
   over *every* visible Gaussian in depth order (exclusive cumprod
   transmittance, weights, colour and alpha sums).  Differentiable through
@@ -32,6 +36,50 @@ import torch
 
 SH_C0 = 0.28209479177387814
 SH_C1 = 0.4886025119029199
+
+
+def _sh_hi_basis(x, y, z, deg):
+    """Real SH basis of degrees 2 (and 3) at unit direction components
+    (x, y, z), normalisation constants computed from their closed forms."""
+    pi = np.pi
+    k0, k1, k2 = 0.5 * np.sqrt(15 / pi), 0.25 * np.sqrt(5 / pi), 0.25 * np.sqrt(15 / pi)
+    xx, yy, zz = x * x, y * y, z * z
+    out = [k0 * x * y, -k0 * y * z, k1 * (2 * zz - xx - yy), -k0 * x * z, k2 * (xx - yy)]
+    if deg >= 3:
+        k3, k4 = 0.25 * np.sqrt(35 / (2 * pi)), 0.5 * np.sqrt(105 / pi)
+        k5, k6, k7 = 0.25 * np.sqrt(21 / (2 * pi)), 0.25 * np.sqrt(7 / pi), 0.25 * np.sqrt(105 / pi)
+        out += [-k3 * y * (3 * xx - yy), k4 * x * y * z, -k5 * y * (4 * zz - xx - yy),
+                k6 * z * (2 * zz - 3 * xx - 3 * yy), -k5 * x * (4 * zz - xx - yy), k7 * z * (xx - yy),
+                -k3 * x * (xx - 3 * yy)]
+    return out
+
+
+def sh_full_degree(ncols: int) -> int:
+    """Degree held by ``ncols`` colour floats in the full mode (3 (d+1)^2, d <= 3)."""
+    return 3 if ncols >= 48 else 2 if ncols >= 27 else 1 if ncols >= 12 else 0
+
+
+def sh_color_full(cs, dirs):
+    """RGB before the +0.5 / clip of the full SH mode: channel ch's
+    coefficients are ``cs[:, 3 + k*ch : 3 + k*(ch+1)]`` with k = (d+1)^2 - 1;
+    the first three multiply (y, z, x) with the reference's degree-1 constant
+    and sign (rendering.py:232-242), then the degree-2 and -3 basis."""
+    d = sh_full_degree(cs.shape[1])
+    rgb = cs[:, :3] * SH_C0
+    if d == 0:
+        return rgb
+    k = (d + 1) ** 2 - 1
+    x, y, z = dirs[:, 0], dirs[:, 1], dirs[:, 2]
+    hi = _sh_hi_basis(x, y, z, d) if d >= 2 else []
+    chans = []
+    for ch in range(3):
+        c0 = 3 + k * ch
+        # the degree-1 term exactly as rendering.py:237-241 forms it
+        acc = SH_C1 * (cs[:, c0] * y + cs[:, c0 + 1] * z + cs[:, c0 + 2] * x)
+        for j, b in enumerate(hi):
+            acc = acc + cs[:, c0 + 3 + j] * b
+        chans.append(acc)
+    return rgb + torch.stack(chans, 1)
 
 
 # ----------------------------------------------------------------------------- cull
@@ -87,7 +135,7 @@ def _clip(x, lo, hi):
 
 
 def project(means, quats, scales, opacities, colors, viewmat, K, width, height,
-            render_width, render_height) -> Dict[str, torch.Tensor]:
+            render_width, render_height, sh_mode: str = "reference") -> Dict[str, torch.Tensor]:
     """rendering.py:153-244 on already-gathered active rows (all torch, one dtype).
 
     Returns per-Gaussian quantities in **depth order**: ``u, v, a, b, c, d``
@@ -148,7 +196,9 @@ def project(means, quats, scales, opacities, colors, viewmat, K, width, height,
     dirs = dirs / (torch.sqrt(torch.sum(dirs ** 2, -1, keepdim=True)) + 1e-8)
     cs = colors[order]
     rgb = cs[:, :3] * SH_C0
-    if cs.shape[1] >= 12:
+    if sh_mode == "full":
+        rgb = sh_color_full(cs, dirs)
+    elif cs.shape[1] >= 12:
         xd, yd, zd = dirs[:, 0], dirs[:, 1], dirs[:, 2]
         rgb = rgb + SH_C1 * torch.stack([
             cs[:, 3] * yd + cs[:, 4] * zd + cs[:, 5] * xd,
@@ -195,14 +245,14 @@ def _as_t(x, dtype):
 
 def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, height,
                     render_width, render_height, dtype=torch.float64, chunk: int = 512,
-                    pixel_ids: Optional[np.ndarray] = None):
+                    pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference"):
     """Forward only.  Inputs are the gathered active rows (numpy or torch).
     Returns ``(colors [H,W,3], alphas [H,W,1])`` as numpy arrays, or
     ``[P,3], [P,1]`` when ``pixel_ids`` selects a subset."""
     with torch.no_grad():
         args = [_as_t(a, dtype) for a in (means, quats, scales, opacities, colors)]
         pg = project(*args, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
-                     render_width, render_height)
+                     render_width, render_height, sh_mode=sh_mode)
         pix = pixel_centers(width, height, render_width, render_height, dtype)
         if pixel_ids is not None:
             pix = pix[torch.as_tensor(np.asarray(pixel_ids, np.int64))]
@@ -225,7 +275,7 @@ def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, 
 
 def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, width, height,
                         render_width, render_height, dL_dC, dL_dA=None, dtype=torch.float64,
-                        chunk: int = 256, pixel_ids: Optional[np.ndarray] = None):
+                        chunk: int = 256, pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference"):
     """Forward plus vector-Jacobian product of the dense rasterizer.
 
     ``dL_dC``/``dL_dA`` are ``[H,W,3]``/``[H,W,1]`` (or ``[P,3]``/``[P,1]`` for
@@ -234,7 +284,7 @@ def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, wid
     """
     leaves = [_as_t(a, dtype).requires_grad_(True) for a in (means, quats, scales, opacities, colors)]
     pg = project(*leaves, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
-                 render_width, render_height)
+                 render_width, render_height, sh_mode=sh_mode)
     keys = ["u", "v", "a", "b", "c", "d", "opac", "rgb"]
     det = {k: pg[k].detach().clone().requires_grad_(True) for k in keys}
     acc = {k: torch.zeros_like(det[k]) for k in keys}

@@ -241,6 +241,119 @@ def gen_ssim(ref_root, out):
     np.savez_compressed(os.path.join(out, "ssim.npz"), **res)
 
 
+def gen_resize(R, out):
+    """The reference's own ``bilinear_resize_mlx`` on seeded images (the
+    trainer's ``image / 255.0`` first): downscale, upscale, identity, odd
+    ratios and single-row/column outputs."""
+    rng = np.random.default_rng(7)
+    res = {}
+    cases = [(37, 23, 16, 11), (37, 23, 64, 40), (37, 23, 37, 23), (50, 31, 7, 5), (20, 9, 1, 1), (33, 17, 33, 1)]
+    for i, (wi, hi, wo, ho) in enumerate(cases):
+        img = rng.integers(0, 256, (hi, wi, 3), dtype=np.uint8)
+        pix = mx.array(img.astype(np.float32)) / 255.0
+        res[f"img_{i}"] = img
+        res[f"size_{i}"] = np.array([ho, wo], np.int32)
+        res[f"out_{i}"] = np.asarray(R.bilinear_resize_mlx(pix, ho, wo)).astype(np.float32)
+    np.savez_compressed(os.path.join(out, "resize.npz"), **res)
+
+
+COLMAP_SCENE = os.path.join(HERE, "colmap_scene")
+
+
+def write_colmap_scene(path):
+    """A small seeded COLMAP scene: two cameras (PINHOLE, SIMPLE_RADIAL), ten
+    images on a ring (ids and file order shuffled, so that name sorting
+    matters), 300 points with tracks, 40x30 PNGs in images/ and 20x15 PNGs in
+    images_2/."""
+    from PIL import Image
+
+    from mlx_gsplat_b200 import dataset as D
+    rng = np.random.default_rng(11)
+    os.makedirs(os.path.join(path, "sparse", "0"), exist_ok=True)
+    cams = [D.Camera(1, "PINHOLE", 40, 30, [37.0, 36.0, 20.0, 15.0]),
+            D.Camera(2, "SIMPLE_RADIAL", 40, 30, [35.5, 19.5, 14.5, 0.01])]
+    D.write_cameras_binary(cams, os.path.join(path, "sparse", "0", "cameras.bin"))
+    images = []
+    order = rng.permutation(10)
+    for j in order:
+        ang = 2 * np.pi * j / 10
+        cpos = np.array([4 * np.cos(ang), 0.5 + 0.2 * rng.normal(), 4 * np.sin(ang)])
+        fwd = -cpos / np.linalg.norm(cpos)
+        right = np.cross(fwd, [0.0, -1.0, 0.0])
+        right /= np.linalg.norm(right)
+        down = np.cross(fwd, right)
+        Rw2c = np.stack([right, down, fwd])
+        t = -Rw2c @ cpos
+        # quaternion (w, x, y, z) of Rw2c, scaled by a non-unit factor (the reader normalises)
+        w = np.sqrt(max(1e-12, 1 + np.trace(Rw2c))) / 2
+        q = np.array([w, (Rw2c[2, 1] - Rw2c[1, 2]) / (4 * w), (Rw2c[0, 2] - Rw2c[2, 0]) / (4 * w),
+                      (Rw2c[1, 0] - Rw2c[0, 1]) / (4 * w)]) * 1.3
+        pts = np.stack([rng.uniform(0, 40, 5), rng.uniform(0, 30, 5), rng.integers(-1, 300, 5)], 1)
+        images.append((int(100 + 7 * j), q, t, 1 + int(j % 2), f"img_{j:03d}.png", pts))
+    D.write_images_binary(images, os.path.join(path, "sparse", "0", "images.bin"))
+    xyz = rng.normal(0, 1, (300, 3))
+    rgb = rng.integers(0, 256, (300, 3))
+    err = rng.uniform(0, 2, 300)
+    tracks = [np.stack([rng.integers(100, 170, k), rng.integers(0, 5, k)], 1) for k in rng.integers(0, 6, 300)]
+    D.write_points3D_binary(xyz, rgb, err, tracks, os.path.join(path, "sparse", "0", "points3D.bin"))
+    for sub, (w, h) in (("images", (40, 30)), ("images_2", (20, 15))):
+        os.makedirs(os.path.join(path, sub), exist_ok=True)
+        for j in range(10):
+            yy, xx = np.mgrid[0:h, 0:w]
+            base = np.stack([xx * 255 // w, yy * 255 // h, (xx + yy + 25 * j) % 256], -1)
+            img = (base + rng.integers(0, 16, (h, w, 3))).clip(0, 255).astype(np.uint8)
+            Image.fromarray(img).save(os.path.join(path, sub, f"img_{j:03d}.png"))
+
+
+def _imageio_stand_in():
+    """``imageio.v2`` (absent here) for the reference's dataset module: reads
+    and writes through Pillow, which is what imageio uses for PNG/JPEG."""
+    import types
+
+    from PIL import Image
+    v2 = types.ModuleType("imageio.v2")
+    v2.imread = lambda p: np.asarray(Image.open(p))
+    v2.imwrite = lambda p, a: Image.fromarray(np.asarray(a)).save(p)
+    top = types.ModuleType("imageio")
+    top.v2 = v2
+    sys.modules["imageio"] = top
+    sys.modules["imageio.v2"] = v2
+
+
+def gen_colmap(ref_root, out):
+    """The reference's own ``Parser`` and ``Dataset`` (dataset.py:258-479) on the
+    fixture scene, normalised and not, at factor 1 and 2."""
+    write_colmap_scene(COLMAP_SCENE)
+    _imageio_stand_in()
+    Dm = load_ref(ref_root, "dataset")
+    res = {}
+    for normalize in (False, True):
+        for factor in (1, 2):
+            key = f"n{int(normalize)}_f{factor}"
+            p = Dm.Parser(COLMAP_SCENE, factor=factor, normalize=normalize)
+            res[key + "_names"] = np.array(p.image_names)
+            res[key + "_paths"] = np.array([os.path.relpath(x, COLMAP_SCENE) for x in p.image_paths])
+            res[key + "_c2w"] = p.camtoworlds
+            res[key + "_camera_ids"] = np.array(p.camera_ids)
+            for cid, K in p.Ks_dict.items():
+                res[f"{key}_K{cid}"] = K
+                res[f"{key}_imsize{cid}"] = np.array(p.imsize_dict[cid])
+                res[f"{key}_params{cid}"] = p.params_dict[cid]
+            res[key + "_points"] = p.points
+            res[key + "_points_rgb"] = p.points_rgb
+            res[key + "_points_err"] = p.points_err
+            res[key + "_transform"] = p.transform
+            res[key + "_scene_scale"] = np.float64(p.scene_scale)
+            for split in ("train", "test"):
+                d = Dm.Dataset(p, split=split, preload_images=True)
+                res[f"{key}_{split}_indices"] = d.indices
+                item = d[1]
+                res[f"{key}_{split}_item1_K"] = np.asarray(item["K"])
+                res[f"{key}_{split}_item1_c2w"] = np.asarray(item["camtoworld"])
+                res[f"{key}_{split}_item1_image"] = np.asarray(item["image"])
+    np.savez_compressed(os.path.join(out, "colmap.npz"), **res)
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     torch.manual_seed(0)
@@ -258,6 +371,8 @@ def main():
         gen_adam(O, HERE)
         gen_alloc(A, HERE)
         gen_ssim(ref_root, HERE)
+        gen_resize(R, HERE)
+        gen_colmap(ref_root, HERE)
     finally:
         os.chdir(cwd)
     print("fixtures written to", HERE)
