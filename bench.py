@@ -170,14 +170,17 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- byte model
 def kernel_bytes(name: str, N: int, V: int, K: int, P: int, tiles: int, ncols: int, stride: int,
-                 sparse_grad: bool = False) -> float:
+                 sparse_grad: bool = False, grad_row_bytes: float = None) -> float:
     """Algorithmic bytes per launch (what the kernel must move at minimum).  With
     ``sparse_grad`` Adam reads gradient rows only for the V rows the view saw
-    (the rest take the regulariser, selected by the cull's visibility bits)."""
+    (the rest take the regulariser, selected by the cull's visibility bits).
+    ``grad_row_bytes``: bytes of one gradient row Adam reads (narrow rows: the
+    23 gradient columns and the view count; default full rows)."""
     if name == "adam":
+        gb = ncols * 4 if grad_row_bytes is None else grad_row_bytes
         if sparse_grad:
-            return N * (ncols * 24 + 4) + V * ncols * 4 + N / 8
-        return N * (ncols * 28 + 4)
+            return N * (ncols * 24 + 4) + V * gb + N / 8
+        return N * (ncols * 24 + 4) + N * gb
     if name == "render_fwd":
         return K * (4 + 48) + tiles * 8 + P * (12 + 4 + 4 + 4 + 3)
     if name == "render_bwd":
@@ -403,7 +406,8 @@ def main():
     for k in kernels:
         if k in phase and phase[k] > 0:
             b = kernel_bytes(k, N, Vm, Km, P, tx * ty, L.ncols, L.stride,
-                             sparse_grad=runner.row_mode == "sparse")
+                             sparse_grad=runner.row_mode == "sparse", grad_row_bytes=4 * (runner.g_cols + 1)
+                             if runner.g_cols < L.ncols else None)
             per[k] = {"ms": phase[k], "gbs": b / (phase[k] * 1e-3) / 1e9, "bytes": b}
     pk = peaks()
     dom = max(per, key=lambda k: per[k]["ms"])
@@ -494,6 +498,7 @@ def main():
                            "parallelism": f"views-dp{world}", "loss": "l1",
                            "grad_reduce": ("nvlink multicast row sum" if runner.fused_reduce is not None else
                                            ("nccl all-reduce" if world > 1 else "none")),
+                           "grad_row_floats": runner.g_stride,
                            "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v/grad slabs (0.96 GB) "
                                  "every step"},
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,

@@ -94,6 +94,9 @@ typedef struct gs_gaussian_grads {
     float reg;                /* constant added to every written geometry gradient (the trainer's 1e-5 * sum(params)) */
     int32_t reg_color_cols;   /* the first reg_color_cols colour columns also receive ``reg`` */
     int32_t reg_geometry;     /* 0: the geometry columns do not receive ``reg`` (the caller adds it later) */
+    int32_t count_col;        /* > 0: every written row also gets 1.0 in this column of the pooled gradient
+                                 rows (``quats`` base, ``quats_stride``; pooled row layout only) — the number
+                                 of views that saw the row, once rows are summed over GPUs; 0: none */
 } gs_gaussian_grads;
 
 /* Pinhole camera.  ``viewmat`` is the row-major world-to-camera matrix
@@ -171,13 +174,20 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
  * gs_fused_adam_group, at a higher instruction cost).  ``grad_bias_host``
  * (ncols floats, or NULL) is added to every row's gradient before
  * ``grad_scale`` (the regulariser of rows summed over GPUs, added once here
- * instead of by every GPU). */
+ * instead of by every GPU).
+ * Narrow gradient rows: with ``g_cols`` < ncols only columns [0, g_cols) of a
+ * gradient row hold gradients; column c >= g_cols takes
+ * g[count_col] * count_coef_host[c] (ncols floats) instead — a column whose
+ * gradient is only the constant regulariser of each view that saw the row,
+ * rebuilt from the row's view count (``count_col`` of gs_gaussian_grads).
+ * g_cols = ncols (count_col, count_coef_host unused) reads full rows. */
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                        double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                        float grad_scale, int mode, const uint32_t* visible_words, const float* unseen_grad_host,
-                       const float* grad_bias_host, gs_stream_t stream);
+                       const float* grad_bias_host, int g_cols, int count_col, const float* count_coef_host,
+                       gs_stream_t stream);
 
 /* ------------------------------------------------------------------ cull */
 

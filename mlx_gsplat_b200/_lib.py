@@ -42,7 +42,7 @@ class GsGaussianGrads(ctypes.Structure):
                 ("opac", c_vp), ("opac_stride", i64),
                 ("colors", c_vp), ("colors_stride", i64),
                 ("colors_write", i32), ("colors_by_visible", i32), ("accumulate", i32),
-                ("reg", ctypes.c_float), ("reg_color_cols", i32), ("reg_geometry", i32)]
+                ("reg", ctypes.c_float), ("reg_color_cols", i32), ("reg_geometry", i32), ("count_col", i32)]
 
 
 class GsCamera(ctypes.Structure):
@@ -68,7 +68,8 @@ _SIGS = {
                             [ctypes.c_float] * 2 + [ctypes.c_int] + [ctypes.c_float] * 4 + [ctypes.c_int, c_vp]),
     "gs_fused_adam_slab": (ctypes.c_int, [c_vp] * 5 + [i64, ctypes.c_int, i64, i64, c_float_p, c_float_p, c_float_p,
                                                        ctypes.c_int] + [ctypes.c_double] * 3 + [ctypes.c_float] * 2 +
-                           [ctypes.c_int, ctypes.c_float, ctypes.c_int, c_vp, c_float_p, c_float_p, c_vp]),
+                           [ctypes.c_int, ctypes.c_float, ctypes.c_int, c_vp, c_float_p, c_float_p,
+                            ctypes.c_int, ctypes.c_int, c_float_p, c_vp]),
     "gs_cull_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_cull": (ctypes.c_int, [ctypes.POINTER(GsGaussians), i64, ctypes.POINTER(GsCamera), ctypes.c_float,
                                ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),

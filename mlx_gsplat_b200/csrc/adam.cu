@@ -28,6 +28,7 @@ struct SlabCols {
     float hi[kMaxSlabCols];
     float gdef[kMaxSlabCols];  // gradient of a row the visibility bits mark unseen
     float gbias[kMaxSlabCols]; // added to every row's gradient before the scale
+    float gcoef[kMaxSlabCols]; // narrow gradient rows: column c >= g_cols is count * gcoef[c]
 };
 
 __device__ __forceinline__ void adam_elem(float& th, float& m, float& v, float g, const AdamScalars& s,
@@ -120,8 +121,20 @@ __global__ void adam_group_kernel(float* __restrict__ theta, const float* __rest
 // copy with a lane-dependent column made every access a divergent constant
 // load (serialised in the address-divergence unit).
 struct __align__(16) ColsSmem {
-    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols], gbias[kMaxSlabCols];
+    float step[kMaxSlabCols], lo[kMaxSlabCols], hi[kMaxSlabCols], gdef[kMaxSlabCols], gbias[kMaxSlabCols],
+        gcoef[kMaxSlabCols];
 };
+
+// A seen row's gradient chunk c4 from a narrow gradient row: columns below
+// g_cols as loaded, the others rebuilt as count * gcoef[c].
+__device__ __forceinline__ float4 narrow_grad(float4 g, int c4, int g_cols, float count, const ColsSmem& cs) {
+    const int c = 4 * c4;
+    g.x = c + 0 < g_cols ? g.x : count * cs.gcoef[c + 0];
+    g.y = c + 1 < g_cols ? g.y : count * cs.gcoef[c + 1];
+    g.z = c + 2 < g_cols ? g.z : count * cs.gcoef[c + 2];
+    g.w = c + 3 < g_cols ? g.w : count * cs.gcoef[c + 3];
+    return g;
+}
 
 template <bool kExact, bool kFused>
 __device__ __forceinline__ void slab_elem(float& th, float& m, float& v, float g, int c, int ncols,
@@ -166,13 +179,21 @@ __device__ __forceinline__ void slab_update(float4& th, float4& mm, float4& vv, 
     }
 }
 
-template <bool kExact, bool kFused>
-__global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
+__device__ __forceinline__ float float4_comp(const float4& v, int k) {
+    return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+}
+
+// kNarrow: gradient rows hold only columns [0, g_cols) and a view count at
+// count_col; the lane of a row whose chunk holds the count broadcasts it to the
+// row's other lanes (one shuffle), and columns from g_cols on are rebuilt as
+// count * gcoef[c].  Every lane stays in the kernel until after the shuffle.
+template <bool kExact, bool kFused, bool kNarrow>
+__global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ theta, const float4* __restrict__ g,
                                                         float4* __restrict__ m, float4* __restrict__ v,
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
                                                         int lane_shift, int g_chunks, int ncols, int quat_chunk,
                                                         int64_t half, const uint32_t* __restrict__ vis,
-                                                        AdamScalars s, SlabCols cols) {
+                                                        int g_cols, int count_col, AdamScalars s, SlabCols cols) {
     __shared__ ColsSmem cs;
     if (threadIdx.x < kMaxSlabCols) {
         cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
@@ -180,14 +201,16 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         cs.hi[threadIdx.x] = cols.hi[threadIdx.x];
         cs.gdef[threadIdx.x] = cols.gdef[threadIdx.x];
         cs.gbias[threadIdx.x] = cols.gbias[threadIdx.x];
+        cs.gcoef[threadIdx.x] = cols.gcoef[threadIdx.x];
     }
     __syncthreads();
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int mask = (1 << lane_shift) - 1;
     const int c4 = (int)(t0 & mask);  // half is a multiple of 2^lane_shift: both items share the chunk
-    if (c4 >= chunks || 4 * c4 >= ncols) return;
+    const bool live = c4 < chunks && 4 * c4 < ncols;
+    if (!kNarrow && !live) return;
     const int64_t ra = t0 >> lane_shift, rb = (t0 + half) >> lane_shift;
-    const bool va = ra < n_rows, vb = rb < n_rows;
+    const bool va = live && ra < n_rows, vb = live && rb < n_rows;
     // Two dependency levels, each issued for both items before anything waits:
     // the indirection entries and visibility words, then every data load.
     int64_t offa = 0, offb = 0;
@@ -201,7 +224,7 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         if (vis) wb = __ldg(vis + (rb >> 5));
     }
     const bool ga_seen = va && ((wa >> (ra & 31)) & 1u), gb_seen = vb && ((wb >> (rb & 31)) & 1u);
-    const float4 gdef = reinterpret_cast<const float4*>(cs.gdef)[c4];
+    const float4 gdef = reinterpret_cast<const float4*>(cs.gdef)[min(c4, kMaxSlabCols / 4 - 1)];
     float4 tha = gdef, ma = gdef, vva = gdef, ga = gdef, thb = gdef, mb = gdef, vvb = gdef, gb = gdef;
     if (va) {
         tha = __ldcs(theta + offa);
@@ -213,8 +236,20 @@ __global__ void __launch_bounds__(256) adam_slab_kernel(float4* __restrict__ the
         mb = __ldcs(m + offb);
         vvb = __ldcs(v + offb);
     }
-    if (ga_seen) ga = __ldcs(g + ra * g_chunks + c4);
-    if (gb_seen) gb = __ldcs(g + rb * g_chunks + c4);
+    const bool load_g = !kNarrow || 4 * c4 < g_cols || c4 == (count_col >> 2);
+    if (ga_seen && load_g) ga = __ldcs(g + ra * g_chunks + c4);
+    if (gb_seen && load_g) gb = __ldcs(g + rb * g_chunks + c4);
+    if (kNarrow) {
+        const int src = count_col >> 2, k = count_col & 3, width = 1 << lane_shift;
+        const float cnt_a = __shfl_sync(kFull, float4_comp(ga, k), src, width);
+        const float cnt_b = __shfl_sync(kFull, float4_comp(gb, k), src, width);
+        if (!live) return;
+        if (4 * c4 + 3 >= g_cols) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ga_seen) ga = narrow_grad(4 * c4 < g_cols ? ga : z, c4, g_cols, cnt_a, cs);
+            if (gb_seen) gb = narrow_grad(4 * c4 < g_cols ? gb : z, c4, g_cols, cnt_b, cs);
+        }
+    }
     const bool renorm = c4 == quat_chunk;
     if (va) {
         slab_update<kExact, kFused>(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
@@ -302,14 +337,20 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                                   double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                                   float grad_scale, int mode, const uint32_t* visible_words,
-                                  const float* unseen_grad_host, const float* grad_bias_host, gs_stream_t stream) {
+                                  const float* unseen_grad_host, const float* grad_bias_host, int g_cols,
+                                  int count_col, const float* count_coef_host, gs_stream_t stream) {
     const bool exact = (mode & GS_ADAM_EXACT) != 0;
     mode &= ~GS_ADAM_EXACT;
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
     GS_REQUIRE(!visible_words || unseen_grad_host, "adam_slab: visible_words needs unseen_grad_host");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
-    GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && g_stride >= ncols,
-               "adam_slab: strides must be multiples of 4 and >= ncols");
+    GS_REQUIRE(g_cols > 0 && g_cols <= ncols, "adam_slab: g_cols must be in [1, ncols]");
+    GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && g_stride >= g_cols,
+               "adam_slab: strides must be multiples of 4, stride >= ncols and g_stride >= g_cols");
+    GS_REQUIRE(g_cols == ncols || (count_coef_host && count_col >= g_cols && count_col < g_stride &&
+                                   count_col < stride && (count_col & ~3) < ncols && stride <= 128),
+               "adam_slab: narrow gradient rows need count_coef_host, a count column in [g_cols, g_stride) "
+               "inside a parameter chunk, and stride <= 128");
     GS_REQUIRE(step >= 1 && num_active >= 0, "adam_slab: bad step/num_active");
     GS_REQUIRE(quat_col < 0 || (quat_col % 4 == 0 && quat_col + 4 <= ncols), "adam_slab: bad quat_col");
     if (num_active == 0) return GS_OK;
@@ -325,6 +366,7 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         cols.step_size[c] = on ? step_size_for(mode, lr, col_lr_scale ? col_lr_scale[c] : 1.0f, bc1) : 0.f;
         cols.gdef[c] = (on && unseen_grad_host) ? unseen_grad_host[c] : 0.f;
         cols.gbias[c] = (on && grad_bias_host) ? grad_bias_host[c] : 0.f;
+        cols.gcoef[c] = (on && c >= g_cols) ? count_coef_host[c] : 0.f;
     }
     s.has_bias = grad_bias_host != nullptr;
     const int chunks = (int)(stride / 4);
@@ -334,12 +376,16 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
     // multiple of 256, hence of 2^shift) after the first
     const int64_t n = num_active << shift;
     const int64_t half = (n + 511) / 512 * 256;
-    auto kernel = exact ? (mode == GS_ADAM_FUSED ? adam_slab_kernel<true, true> : adam_slab_kernel<true, false>)
-                        : (mode == GS_ADAM_FUSED ? adam_slab_kernel<false, true> : adam_slab_kernel<false, false>);
+    const bool narrow = g_cols < ncols;
+#define GS_ADAM_SLAB(N)                                                                                     \
+    (exact ? (mode == GS_ADAM_FUSED ? adam_slab_kernel<true, true, N> : adam_slab_kernel<true, false, N>) \
+           : (mode == GS_ADAM_FUSED ? adam_slab_kernel<false, true, N> : adam_slab_kernel<false, false, N>))
+    auto kernel = narrow ? GS_ADAM_SLAB(true) : GS_ADAM_SLAB(false);
+#undef GS_ADAM_SLAB
     kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
-        quat_col < 0 ? -1 : quat_col / 4, half, visible_words, s, cols);
+        quat_col < 0 ? -1 : quat_col / 4, half, visible_words, g_cols, g_cols < ncols ? count_col : 0, s, cols);
     return check_launch("adam_slab_kernel");
 }
 
@@ -361,7 +407,7 @@ extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, u
         }
         return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
                                   beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED | GS_ADAM_EXACT,
-                                  nullptr, nullptr, nullptr, stream);
+                                  nullptr, nullptr, nullptr, dim, 0, nullptr, stream);
     }
     return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
                                weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);

@@ -231,7 +231,14 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             c.opac = q1.z;
             float2 sd = f2(0.f), sy = f2(0.f), syy = f2(0.f), sr = f2(0.f), sg = f2(0.f), sb = f2(0.f);
 #pragma unroll
-            for (int q = 0; q < kPairs; ++q) pair_bwd_step(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+            for (int q = 0; q < kPairs; ++q) {
+#ifndef GS_BWD_NO_PAIR_SKIP
+                // a pair row of the warp block that the splat misses entirely
+                // contributes exactly nothing (alpha = 0 leaves T and B as they are)
+                if (!__any_sync(kFull, v0[q] | v1[q])) continue;
+#endif
+                pair_bwd_step(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+            }
             float g[9];
             g[5] = sd.x + sd.y;
             g[1] = sy.x + sy.y;
@@ -479,8 +486,13 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
 #pragma unroll
         for (int k = 0; k < kVals - kRowColor; ++k)
             vals[kRowColor + k] = (k < NC ? dcol[k] : 0.f) + (k < o.reg_color_cols ? reg : 0.f);
+        // the view count column (narrow gradient rows summed over GPUs)
+        const int cc = o.count_col;
+#pragma unroll
+        for (int k = 0; k < kVals; ++k)
+            if (cc > 0 && k == cc) vals[k] = 1.0f;
         float* rowp = o.quats + (int64_t)id * o.quats_stride;
-        const int W = kRowColor + o.colors_write;
+        const int W = max(kRowColor + o.colors_write, cc + 1);
 #pragma unroll
         for (int j = 0; j < kVals / 4; ++j) {
             if (4 * j + 3 < W) {
@@ -495,7 +507,8 @@ __global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const 
         for (int c = kVals; c < W; c += 4) {
             float t[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) t[u] = c + u - kRowColor < o.reg_color_cols ? reg : 0.f;
+            for (int u = 0; u < 4; ++u)
+                t[u] = cc > 0 && c + u == cc ? 1.0f : (c + u - kRowColor < o.reg_color_cols ? reg : 0.f);
             if (c + 3 < W) {
                 reinterpret_cast<float4*>(rowp + c)[0] = make_float4(t[0], t[1], t[2], t[3]);
             } else {
@@ -573,6 +586,9 @@ extern "C" int gs_project_backward(const gs_gaussians* g, const int32_t* ids, in
     GS_REQUIRE(ids && splat_grads, "project_backward: null pointer");
     GS_REQUIRE(!grad2d || count, "project_backward: grad2d needs count");
     GS_REQUIRE(out->colors == nullptr || out->colors_write >= 0, "project_backward: bad colors_write");
+    GS_REQUIRE(out->count_col <= 0 || (slab_grad_rows(*out) && out->count_col < out->quats_stride &&
+                                       out->count_col >= kRowColor + out->colors_write),
+               "project_backward: a count column needs pooled gradient rows with room past the colours");
     const RasterParams p = make_raster_params(*cam, nullptr);
     GS_REQUIRE(g->sh_mode == GS_SH_REFERENCE || g->sh_mode == GS_SH_FULL, "project_backward: bad sh_mode");
     const int deg = sh_kernel_degree(*g);

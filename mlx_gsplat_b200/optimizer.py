@@ -106,14 +106,17 @@ class FusedMLXAdam:
     def step_slab(self, theta: torch.Tensor, g: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
                   table: torch.Tensor, num_active: int, ncols: int, col_lo, col_hi, quat_col: int = -1,
                   grad_scale: float = 1.0, pure: bool = False, col_lr_scale=None, visible_words: Optional[int] = None,
-                  unseen_grad=None, exact: bool = False, grad_bias=None) -> None:
+                  unseen_grad=None, exact: bool = False, grad_bias=None, g_cols: Optional[int] = None,
+                  count_col: int = 0, count_coef=None) -> None:
         """One launch over every group of a ``[max, stride]`` slab (fused semantics).
         With ``visible_words`` (device address of the cull's visibility bitmask) rows
         the bitmask marks unseen take ``unseen_grad`` (ncols floats) as their gradient
         instead of reading ``g``.  The step uses the hardware approximate square
         root and reciprocal (relative error below 1e-6) unless ``exact``.
         ``grad_bias`` (ncols floats) is added to every row's gradient before
-        ``grad_scale``."""
+        ``grad_scale``.  Narrow gradient rows: only the first ``g_cols`` columns
+        of ``g`` hold gradients; column c >= g_cols is ``g[count_col] *
+        count_coef[c]`` (the regulariser of each view that saw the row)."""
         self.t += 1
         lib = _lib.lib()
         _lib.check(lib.gs_fused_adam_slab(theta.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(),
@@ -125,4 +128,6 @@ class FusedMLXAdam:
                                           (_lib.GS_ADAM_EXACT if exact else 0),
                                           visible_words, None if unseen_grad is None else _lib.fptr(unseen_grad),
                                           None if grad_bias is None else _lib.fptr(grad_bias),
+                                          ncols if g_cols is None else int(g_cols), int(count_col),
+                                          None if count_coef is None else _lib.fptr(count_coef),
                                           _lib.stream_ptr(theta.device)), "fused adam (slab)")

@@ -112,7 +112,7 @@ def gaussians_struct(means, quats=None, scales=None, opacities=None, colors=None
 
 def grads_struct(means=None, quats=None, scales=None, opacities=None, colors=None, colors_write: int = 0,
                  colors_by_visible: bool = False, accumulate: bool = True, reg: float = 0.0,
-                 reg_color_cols: int = 0, reg_geometry: bool = True) -> GsGaussianGrads:
+                 reg_color_cols: int = 0, reg_geometry: bool = True, count_col: int = 0) -> GsGaussianGrads:
     o = GsGaussianGrads()
     o.means, o.means_stride = _rows(means, 3, "grad means")
     o.quats, o.quats_stride = _rows(quats, 4, "grad quats")
@@ -125,6 +125,7 @@ def grads_struct(means=None, quats=None, scales=None, opacities=None, colors=Non
     o.reg = float(reg)
     o.reg_color_cols = int(reg_color_cols)
     o.reg_geometry = int(bool(reg_geometry))
+    o.count_col = int(count_col)
     return o
 
 

@@ -174,3 +174,34 @@ def test_rank_failure_surfaces_as_error():
     assert got[1][0] is False and "injected failure" in got[1][1]
     # rank 0 either saw its collective fail or failed at the final barrier; it did not hang
     assert got[0][0] is False or got[0][1] == "collective failed as expected"
+
+
+def _narrow_rows(rank, world):
+    """Each rank's gradient rows for the Gaussians its view saw, full width and
+    narrow (23 gradient columns + a view-count column), summed over ranks."""
+    from mlx_gsplat_b200 import distributed as D
+    rng = np.random.default_rng(10 + rank)
+    n, ncols, reg = 64, 59, 1e-5
+    seen = rng.uniform(0, 1, n) < 0.6
+    full = np.zeros((n, 60), np.float32)
+    full[seen, :23] = rng.normal(0, 1, (int(seen.sum()), 23))
+    full[seen, 11:23] += np.float32(reg)   # colour columns the rasterizer reads carry reg + gradient
+    full[seen, 23:ncols] = np.float32(reg)  # the rest only the regulariser
+    narrow = np.zeros((n, 24), np.float32)
+    narrow[:, :23] = full[:, :23]
+    narrow[seen, 23] = 1.0
+    F, N = torch.from_numpy(full), torch.from_numpy(narrow)
+    D.reduce_gradient_rows(F, dist.group.WORLD)
+    D.reduce_gradient_rows(N, dist.group.WORLD)
+    return {"full": F.numpy(), "narrow": N.numpy()}
+
+
+def test_narrow_gradient_rows_sum_like_full_rows():
+    """The all-reduce of narrow rows, expanded as Adam expands them (column
+    c >= 23 = view count * reg), equals the all-reduce of full rows."""
+    a, b = _run(_narrow_rows)
+    np.testing.assert_array_equal(a["narrow"], b["narrow"])
+    nar, full = a["narrow"], a["full"]
+    expanded = np.concatenate([nar[:, :23], nar[:, 23:24] * np.float32(1e-5) * np.ones((1, 36), np.float32)], 1)
+    np.testing.assert_allclose(expanded, full[:, :59], rtol=1e-6, atol=0)
+    assert nar[:, 23].max() <= 2 and nar[:, 23].sum() > 0

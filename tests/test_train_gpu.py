@@ -14,19 +14,40 @@ from oracle import rendering as orend
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("wl_name,n,loss", [("tiny-3k", 3000, "l1"), ("mid-200k", 20_000, "l1"),
-                                            ("tiny-3k", 3000, "l1+dssim"), ("mid-200k", 20_000, "l1+dssim")])
-def test_train_step_matches_oracle(wl_name, n, loss):
+def _small_outdoor(monkeypatch):
+    """The outdoor scene's distributions (SH degree 3 stored) at 8,000
+    Gaussians and 216x140, small enough for the dense oracle."""
+    import dataclasses
+    wl = dataclasses.replace(synthetic.WORKLOADS["outdoor-1m"], name="outdoor-small", num_gaussians=8000,
+                             width=216, height=140, focal=1150.0 / 6)
+    monkeypatch.setitem(synthetic.WORKLOADS, wl.name, wl)
+    return wl.name
+
+
+@pytest.mark.parametrize("wl_name,n,loss,step", [("tiny-3k", 3000, "l1", 1), ("mid-200k", 20_000, "l1", 1),
+                                                 ("tiny-3k", 3000, "l1+dssim", 1),
+                                                 ("mid-200k", 20_000, "l1+dssim", 1),
+                                                 ("outdoor-small", None, "l1", 1),
+                                                 ("outdoor-small", None, "l1", 3)])
+def test_train_step_matches_oracle(monkeypatch, wl_name, n, loss, step):
+    """One step's gradient rows and Adam update against the oracle.  The
+    outdoor-small cases store SH degree 3 (48 colour floats) and run with
+    narrow gradient rows (23 gradient columns + the view count; Adam rebuilds
+    the regulariser-only colour columns) at SH degree 1 (step 1, 12 colour
+    columns read) and degree 3 (step 3: 48 colour columns get the regulariser)."""
+    if wl_name == "outdoor-small":
+        _small_outdoor(monkeypatch)
     r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15, loss=loss)
     r.row_mode = "dense"  # write every gradient row so the test can inspect them
     al, L = r.allocator, r.layout
-    step = 1
+    if wl_name == "outdoor-small":
+        assert r.g_cols == 23 and r.g_stride == 24
     theta0 = al.theta.cpu().numpy().copy()
     table = al.indirection_table.cpu().numpy()
     frame = r.train_step(0, step)
     torch.cuda.synchronize()
     N = al.num_active
-    grad = r.grad[:N].cpu().numpy()
+    grad = r.full_gradient_rows(step, N).cpu().numpy()
     # --- oracle gradients: dense VJP over the visible rows, cotangent from the GPU image
     act = {k: theta0[table][:, o:o + L.dims[k]] for k, o in L.offsets.items()}
     ids = frame.ids[:frame.V].cpu().numpy().astype(np.int64)
