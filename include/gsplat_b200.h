@@ -180,14 +180,22 @@ int gs_fused_adam_group(float* theta, const float* g, float* m, float* v, const 
  * g[count_col] * count_coef_host[c] (ncols floats) instead — a column whose
  * gradient is only the constant regulariser of each view that saw the row,
  * rebuilt from the row's view count (``count_col`` of gs_gaussian_grads).
- * g_cols = ncols (count_col, count_coef_host unused) reads full rows. */
+ * g_cols = ncols (count_col, count_coef_host unused) reads full rows.
+ * ``row_select`` (needs visible_words): GS_ROWS_ALL updates every row;
+ * GS_ROWS_SEEN only the rows whose visibility bit is set, GS_ROWS_UNSEEN only
+ * the others — two launches with the same ``step``, one per set, give the
+ * update of one launch over all rows, and the unseen set needs nothing of
+ * the rasterizer's output (it can run as soon as the cull has run). */
+#define GS_ROWS_ALL 0
+#define GS_ROWS_SEEN 1
+#define GS_ROWS_UNSEEN 2
 int gs_fused_adam_slab(float* theta, const float* g, float* m, float* v, const int32_t* indices,
                        int64_t num_active, int ncols, int64_t stride, int64_t g_stride,
                        const float* col_lo, const float* col_hi, const float* col_lr_scale, int quat_col,
                        double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                        float grad_scale, int mode, const uint32_t* visible_words, const float* unseen_grad_host,
                        const float* grad_bias_host, int g_cols, int count_col, const float* count_coef_host,
-                       gs_stream_t stream);
+                       int row_select, gs_stream_t stream);
 
 /* ------------------------------------------------------------------ cull */
 

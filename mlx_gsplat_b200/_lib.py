@@ -18,6 +18,7 @@ GS_OK, GS_ERR_INVALID, GS_ERR_CUDA, GS_ERR_CAPACITY = 0, 1, 2, 3
 GS_ADAM_FUSED, GS_ADAM_PURE, GS_ADAM_EXACT = 0, 1, 0x100
 GS_LOSS_NONE, GS_LOSS_L1_U8, GS_LOSS_L1_F32, GS_LOSS_MEAN = 0, 1, 2, 3
 GS_SH_REFERENCE, GS_SH_FULL = 0, 1
+GS_ROWS_ALL, GS_ROWS_SEEN, GS_ROWS_UNSEEN = 0, 1, 2
 
 c_float_p = ctypes.POINTER(ctypes.c_float)
 c_vp = ctypes.c_void_p
@@ -69,7 +70,7 @@ _SIGS = {
     "gs_fused_adam_slab": (ctypes.c_int, [c_vp] * 5 + [i64, ctypes.c_int, i64, i64, c_float_p, c_float_p, c_float_p,
                                                        ctypes.c_int] + [ctypes.c_double] * 3 + [ctypes.c_float] * 2 +
                            [ctypes.c_int, ctypes.c_float, ctypes.c_int, c_vp, c_float_p, c_float_p,
-                            ctypes.c_int, ctypes.c_int, c_float_p, c_vp]),
+                            ctypes.c_int, ctypes.c_int, c_float_p, ctypes.c_int, c_vp]),
     "gs_cull_scratch_bytes": (ctypes.c_size_t, [i64]),
     "gs_cull": (ctypes.c_int, [ctypes.POINTER(GsGaussians), i64, ctypes.POINTER(GsCamera), ctypes.c_float,
                                ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),

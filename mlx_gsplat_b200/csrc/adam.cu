@@ -193,7 +193,8 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
                                                         int lane_shift, int g_chunks, int ncols, int quat_chunk,
                                                         int64_t half, const uint32_t* __restrict__ vis,
-                                                        int g_cols, int count_col, AdamScalars s, SlabCols cols) {
+                                                        int g_cols, int count_col, int row_select, AdamScalars s,
+                                                        SlabCols cols) {
     __shared__ ColsSmem cs;
     if (threadIdx.x < kMaxSlabCols) {
         cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
     const bool live = c4 < chunks && 4 * c4 < ncols;
     if (!kNarrow && !live) return;
     const int64_t ra = t0 >> lane_shift, rb = (t0 + half) >> lane_shift;
-    const bool va = live && ra < n_rows, vb = live && rb < n_rows;
+    bool va = live && ra < n_rows, vb = live && rb < n_rows;
     // Two dependency levels, each issued for both items before anything waits:
     // the indirection entries and visibility words, then every data load.
     int64_t offa = 0, offb = 0;
@@ -223,7 +224,15 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
         offb = (int64_t)__ldg(idx + rb) * chunks + c4;
         if (vis) wb = __ldg(vis + (rb >> 5));
     }
-    const bool ga_seen = va && ((wa >> (ra & 31)) & 1u), gb_seen = vb && ((wb >> (rb & 31)) & 1u);
+    bool ga_seen = va && ((wa >> (ra & 31)) & 1u), gb_seen = vb && ((wb >> (rb & 31)) & 1u);
+    if (row_select != GS_ROWS_ALL) {
+        // a row outside the selected set is neither read nor written
+        const bool want_seen = row_select == GS_ROWS_SEEN;
+        va = va && (((wa >> (ra & 31)) & 1u) != 0) == want_seen;
+        vb = vb && (((wb >> (rb & 31)) & 1u) != 0) == want_seen;
+        ga_seen = ga_seen && va;
+        gb_seen = gb_seen && vb;
+    }
     const float4 gdef = reinterpret_cast<const float4*>(cs.gdef)[min(c4, kMaxSlabCols / 4 - 1)];
     float4 tha = gdef, ma = gdef, vva = gdef, ga = gdef, thb = gdef, mb = gdef, vvb = gdef, gb = gdef;
     if (va) {
@@ -338,13 +347,16 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   double lr, double beta1, double beta2, float eps, float weight_decay, int step,
                                   float grad_scale, int mode, const uint32_t* visible_words,
                                   const float* unseen_grad_host, const float* grad_bias_host, int g_cols,
-                                  int count_col, const float* count_coef_host, gs_stream_t stream) {
+                                  int count_col, const float* count_coef_host, int row_select,
+                                  gs_stream_t stream) {
     const bool exact = (mode & GS_ADAM_EXACT) != 0;
     mode &= ~GS_ADAM_EXACT;
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
     GS_REQUIRE(!visible_words || unseen_grad_host, "adam_slab: visible_words needs unseen_grad_host");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
     GS_REQUIRE(g_cols > 0 && g_cols <= ncols, "adam_slab: g_cols must be in [1, ncols]");
+    GS_REQUIRE(row_select >= GS_ROWS_ALL && row_select <= GS_ROWS_UNSEEN, "adam_slab: bad row_select");
+    GS_REQUIRE(row_select == GS_ROWS_ALL || visible_words, "adam_slab: row_select needs visible_words");
     GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && g_stride >= g_cols,
                "adam_slab: strides must be multiples of 4, stride >= ncols and g_stride >= g_cols");
     GS_REQUIRE(g_cols == ncols || (count_coef_host && count_col >= g_cols && count_col < g_stride &&
@@ -385,7 +397,8 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
     kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
-        quat_col < 0 ? -1 : quat_col / 4, half, visible_words, g_cols, g_cols < ncols ? count_col : 0, s, cols);
+        quat_col < 0 ? -1 : quat_col / 4, half, visible_words, g_cols, g_cols < ncols ? count_col : 0, row_select,
+        s, cols);
     return check_launch("adam_slab_kernel");
 }
 
@@ -407,7 +420,7 @@ extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, u
         }
         return gs_fused_adam_slab(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lo, hi, nullptr, -1, lr,
                                   beta1, beta2, eps, weight_decay, step, 1.0f, GS_ADAM_FUSED | GS_ADAM_EXACT,
-                                  nullptr, nullptr, nullptr, dim, 0, nullptr, stream);
+                                  nullptr, nullptr, nullptr, dim, 0, nullptr, GS_ROWS_ALL, stream);
     }
     return gs_fused_adam_group(theta, g, m, v, idx, (int64_t)num_active, dim, dim, dim, lr, beta1, beta2, eps,
                                weight_decay, step, a_min, a_max, 1.0f, 1.0f, GS_ADAM_FUSED, stream);

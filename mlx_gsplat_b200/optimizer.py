@@ -107,7 +107,7 @@ class FusedMLXAdam:
                   table: torch.Tensor, num_active: int, ncols: int, col_lo, col_hi, quat_col: int = -1,
                   grad_scale: float = 1.0, pure: bool = False, col_lr_scale=None, visible_words: Optional[int] = None,
                   unseen_grad=None, exact: bool = False, grad_bias=None, g_cols: Optional[int] = None,
-                  count_col: int = 0, count_coef=None) -> None:
+                  count_col: int = 0, count_coef=None, row_select: int = 0, advance: bool = True) -> None:
         """One launch over every group of a ``[max, stride]`` slab (fused semantics).
         With ``visible_words`` (device address of the cull's visibility bitmask) rows
         the bitmask marks unseen take ``unseen_grad`` (ncols floats) as their gradient
@@ -116,8 +116,12 @@ class FusedMLXAdam:
         ``grad_bias`` (ncols floats) is added to every row's gradient before
         ``grad_scale``.  Narrow gradient rows: only the first ``g_cols`` columns
         of ``g`` hold gradients; column c >= g_cols is ``g[count_col] *
-        count_coef[c]`` (the regulariser of each view that saw the row)."""
-        self.t += 1
+        count_coef[c]`` (the regulariser of each view that saw the row).
+        ``row_select`` (with ``visible_words``) updates only the seen
+        (``GS_ROWS_SEEN``) or unseen (``GS_ROWS_UNSEEN``) rows; the second
+        launch of such a pair passes ``advance=False`` to keep the step count."""
+        if advance:
+            self.t += 1
         lib = _lib.lib()
         _lib.check(lib.gs_fused_adam_slab(theta.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(),
                                           table.data_ptr(), num_active, ncols, theta.stride(0), g.stride(0),
@@ -129,5 +133,5 @@ class FusedMLXAdam:
                                           visible_words, None if unseen_grad is None else _lib.fptr(unseen_grad),
                                           None if grad_bias is None else _lib.fptr(grad_bias),
                                           ncols if g_cols is None else int(g_cols), int(count_col),
-                                          None if count_coef is None else _lib.fptr(count_coef),
+                                          None if count_coef is None else _lib.fptr(count_coef), int(row_select),
                                           _lib.stream_ptr(theta.device)), "fused adam (slab)")

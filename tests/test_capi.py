@@ -45,7 +45,7 @@ def test_cpu_only_calls():
     assert lib.gs_cull_scratch_bytes(5000) > 0
     # argument validation happens before any CUDA call
     st = lib.gs_fused_adam_slab(None, None, None, None, None, 10, 70, 60, 60, None, None, None, -1,
-                                1e-3, 0.9, 0.999, 1e-8, 0.0, 1, 1.0, 0, None, None, None, 70, 0, None, None)
+                                1e-3, 0.9, 0.999, 1e-8, 0.0, 1, 1.0, 0, None, None, None, 70, 0, None, 0, None)
     assert st == _lib.GS_ERR_INVALID
     assert b"ncols" in lib.gs_last_error()
 

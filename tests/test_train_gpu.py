@@ -134,6 +134,54 @@ def test_unseen_rows_from_visibility_bits_match_dense_rows():
         np.testing.assert_array_equal(a, b)
 
 
+def test_adam_split_by_visibility_equals_one_launch():
+    """Adam over the unseen rows (what the trainer runs on a side stream right
+    after the cull) then over the seen rows, with one step count, gives the
+    one-launch update bit for bit (narrow gradient rows included)."""
+    from mlx_gsplat_b200 import _lib
+    from mlx_gsplat_b200.allocator import SlabLayout
+    from mlx_gsplat_b200.optimizer import FusedMLXAdam
+    L = SlabLayout(3)
+    rng = np.random.default_rng(4)
+    n, maxg = 40_000, 50_000
+    theta = rng.normal(0, 1, (maxg, L.stride)).astype(np.float32)
+    table = rng.permutation(maxg)[:n].astype(np.int32)
+    seen = rng.uniform(0, 1, n) < 0.5
+    words = np.zeros((n + 31) // 32, np.uint32)
+    for r in np.nonzero(seen)[0]:
+        words[r >> 5] |= np.uint32(1) << np.uint32(r & 31)
+    g = rng.normal(0, 0.1, (maxg, 24)).astype(np.float32)
+    g[:, 23] = 1.0
+    unseen = np.zeros(L.ncols, np.float32)
+    unseen[:11] = 1e-5
+    coef = [1e-5 if c >= 23 else 0.0 for c in range(L.ncols)]
+    lo, hi = L.col_bounds()
+    out = []
+    for split in (False, True):
+        th = torch.from_numpy(theta.copy()).cuda()
+        gg = torch.from_numpy(g).cuda()
+        m = torch.zeros_like(th)
+        v = torch.zeros_like(th)
+        tab = torch.from_numpy(table).cuda()
+        W = torch.from_numpy(words.view(np.int32)).cuda()
+        opt = FusedMLXAdam(lr=1e-3, eps=1e-15)
+        kw = dict(quat_col=0, visible_words=W.data_ptr(), unseen_grad=unseen.tolist(), g_cols=23, count_col=23,
+                  count_coef=coef)
+        for _ in range(2):
+            if split:
+                opt.step_slab(th, gg, m, v, tab, n, L.ncols, lo.tolist(), hi.tolist(),
+                              row_select=_lib.GS_ROWS_UNSEEN, **kw)
+                opt.step_slab(th, gg, m, v, tab, n, L.ncols, lo.tolist(), hi.tolist(),
+                              row_select=_lib.GS_ROWS_SEEN, advance=False, **kw)
+            else:
+                opt.step_slab(th, gg, m, v, tab, n, L.ncols, lo.tolist(), hi.tolist(), **kw)
+        torch.cuda.synchronize()
+        out.append([x.cpu().numpy() for x in (th, m, v)])
+    for a, b in zip(*out):
+        np.testing.assert_array_equal(a, b)
+    assert not np.array_equal(out[0][0], theta)
+
+
 def test_gradient_row_modes_agree():
     """End to end through the trainer, the three ways of forming the gradient
     rows of unseen Gaussians: "sparse" (one GPU: regulariser rows selected by
