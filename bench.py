@@ -46,7 +46,7 @@ def peaks():
 
 # What actually limits each kernel (ncu summaries under profiles/): the compositing kernels keep
 # their splat records in L2 and are bound by FP32 instruction issue, not by HBM.
-LIMITERS = {"render_bwd": "fp32 instruction issue (ncu issue-active ~78%, DRAM ~1%; paired f32x2 math)",
+LIMITERS = {"render_bwd": "fp32 instruction issue (ncu issue-active ~79%, DRAM ~1%; paired f32x2 math)",
             "render_fwd": "fp32 instruction issue (ncu issue-active ~75%, DRAM ~1%; paired f32x2 math)",
             "adam": "hbm"}
 

@@ -114,7 +114,7 @@ typedef struct gs_camera {
  * only when some pixel centre of the tile can see alpha >= alpha_cutoff, and
  * stop a pixel once its transmittance falls below transmittance_min. */
 typedef struct gs_raster_settings {
-    float alpha_cutoff;      /* e.g. 1e-8 (parity) */
+    float alpha_cutoff;      /* e.g. 1e-7 (the default: parity with the dense reference to ~1e-6) */
     float transmittance_min; /* e.g. 1e-6 (parity) */
 } gs_raster_settings;
 

@@ -38,7 +38,7 @@ inline RasterParams make_raster_params(const gs_camera& c, const gs_raster_setti
     p.rh = c.render_height;
     p.tiles_x = (c.render_width + kTile - 1) / kTile;
     p.tiles_y = (c.render_height + kTile - 1) / kTile;
-    p.alpha_cut = rs ? rs->alpha_cutoff : 1e-8f;
+    p.alpha_cut = rs ? rs->alpha_cutoff : 1e-7f;
     p.t_min = rs ? rs->transmittance_min : 1e-6f;
     p.loss_scale = (float)(1.0 / (3.0 * (double)c.render_width * (double)c.render_height));
     return p;

@@ -37,7 +37,7 @@ TILE = 16
 
 @dataclass
 class RasterSettings:
-    alpha_cutoff: float = 1e-8
+    alpha_cutoff: float = 1e-7
     transmittance_min: float = 1e-6
 
     def cstruct(self) -> GsRasterSettings:
