@@ -205,7 +205,14 @@ class TileFrame:
 
 def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, settings: RasterSettings,
                    device, loss_mode: int = _lib.GS_LOSS_NONE, target: Optional[torch.Tensor] = None,
-                   out_color: Optional[torch.Tensor] = None, timer=None) -> TileFrame:
+                   out_color: Optional[torch.Tensor] = None, timer=None, v_count: Optional[torch.Tensor] = None,
+                   k_hint: int = 0) -> TileFrame:
+    """The forward of one view.  With ``v_count`` (the cull's device count, not
+    yet read back) ``V`` is an upper bound of the visible count: every
+    per-view buffer is allocated before the count is read, and the tile-entry
+    buffers before the entry count is read (``k_hint`` entries, enlarged only
+    when a view has more), so the host goes from each read-back straight to
+    the next kernel launch."""
     lib = _lib.lib()
     st = _lib.stream_ptr(device)
     rs = settings.cstruct()
@@ -213,47 +220,56 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
     tx, ty = num_tiles(RW, RH)
     T = tx * ty
     f = TileFrame()
-    f.V, f.cam, f.rs, f.ids, f.loss_mode, f.target = V, cam, rs, ids, loss_mode, target
+    Vb = int(V)  # buffer bound
+    f.cam, f.rs, f.ids, f.loss_mode, f.target = cam, rs, ids, loss_mode, target
     f.color = out_color if out_color is not None else torch.empty((RH, RW, 3), dtype=torch.float32, device=device)
     f.alpha = torch.empty((RH, RW, 1), dtype=torch.float32, device=device)
     f.final_T = torch.empty((RH, RW), dtype=torch.float32, device=device)
     f.n_contrib = torch.empty((RH, RW), dtype=torch.int32, device=device)
     f.loss_partials = torch.empty(T, dtype=torch.float32, device=device) if loss_mode != _lib.GS_LOSS_NONE else None
-    f.splats = torch.empty((max(V, 1), 12), dtype=torch.float32, device=device)
+    f.splats = torch.empty((max(Vb, 1), 12), dtype=torch.float32, device=device)
     f.ranges = torch.empty((T, 2), dtype=torch.int32, device=device)
+    if Vb > 0:
+        depth_keys = _i32(Vb, device)
+        tile_counts = _i32(Vb, device)
+        bin_scratch = _scratch(lib.gs_bin_scratch_bytes(Vb), device)  # binning state for gs_bin_emit
+        keys_sorted = _i32(Vb, device)
+        order = _i32(Vb, device)
+        sb = _scratch(lib.gs_radix_sort_scratch_bytes(Vb), device)
+        offsets = _i32(Vb + 1, device)
+        ob = _scratch(lib.gs_bin_offsets_scratch_bytes(Vb), device)
+    V = int(v_count.item()) if v_count is not None else Vb
+    f.V = V
     if V > 0:
-        depth_keys = _i32(V, device)
-        tile_counts = _i32(V, device)
-        bin_scratch = _scratch(lib.gs_bin_scratch_bytes(V), device)  # binning state for gs_bin_emit
         check(lib.gs_project_forward(g, ids.data_ptr(), V, cam, rs, f.splats.data_ptr(), depth_keys.data_ptr(),
                                      tile_counts.data_ptr(), bin_scratch.data_ptr(), st), "gs_project_forward")
         if timer:
             timer.mark("project_fwd")
-        keys_sorted = _i32(V, device)
-        order = _i32(V, device)
-        sb = _scratch(lib.gs_radix_sort_scratch_bytes(V), device)
         check(lib.gs_radix_sort_pairs(depth_keys.data_ptr(), None, keys_sorted.data_ptr(),
                                       order.data_ptr(), V, 0, 32, sb.data_ptr(), sb.numel(), st), "depth sort")
-        offsets = _i32(V + 1, device)
-        ob = _scratch(lib.gs_bin_offsets_scratch_bytes(V), device)
         check(lib.gs_bin_offsets(order.data_ptr(), tile_counts.data_ptr(), V, offsets.data_ptr(), ob.data_ptr(),
                                  ob.numel(), st), "gs_bin_offsets")
         if timer:
             timer.mark("depth_sort+offsets")
+
+        def entry_buffers(cap):
+            flag = torch.zeros(1, dtype=torch.int32, device=device)
+            return (_i32(cap, device), _i32(cap, device), _i32(cap, device), _i32(cap, device),
+                    _scratch(lib.gs_radix_sort_scratch_bytes(cap), device), flag)
+
+        kcap = int(k_hint)
+        bufs = entry_buffers(kcap) if kcap > 0 else None
         K = int(offsets[V].item())
         f.K = K
         f.order = order
         if K > 0:
-            keys = _i32(K, device)
-            vals = _i32(K, device)
-            flag = torch.zeros(1, dtype=torch.int32, device=device)
+            if bufs is None or K > kcap:
+                bufs = entry_buffers(K)
+            keys, vals, f.tile_keys, f.entry_vals, sb2, flag = bufs
             check(lib.gs_bin_emit(f.splats.data_ptr(), order.data_ptr(), offsets.data_ptr(), tile_counts.data_ptr(),
                                   V, cam, rs, keys.data_ptr(), vals.data_ptr(), K, flag.data_ptr(),
                                   bin_scratch.data_ptr(), st), "gs_bin_emit")
             tile_bits = max(1, int(T).bit_length())  # 2**bits - 1 >= T: the emit sentinel sorts last
-            f.tile_keys = _i32(K, device)
-            f.entry_vals = _i32(K, device)
-            sb2 = _scratch(lib.gs_radix_sort_scratch_bytes(K), device)
             check(lib.gs_radix_sort_pairs(keys.data_ptr(), vals.data_ptr(), f.tile_keys.data_ptr(),
                                           f.entry_vals.data_ptr(), K, 0, tile_bits, sb2.data_ptr(), sb2.numel(), st),
                   "tile sort")

@@ -232,6 +232,7 @@ class RunnerMLX:
         self.scene_scale = scene_scale
         self.last_frame = None
         self.step_count = 0
+        self._k_hint = 0  # tile-entry buffer size for the next view (grows with the views seen)
         # How gradient rows of unseen Gaussians are formed: "sparse" (one GPU:
         # Adam takes the regulariser row for them from the cull's visibility
         # bits), "dense" (every row filled with the regulariser first), "summed"
@@ -320,12 +321,15 @@ class RunnerMLX:
         g = self._gaussians(step)
         if timer:
             timer.mark("start")
-        ids, _, V, cull_scratch = cull_ids(g, N, cam, self.device, cfg.near_plane, cfg.far_plane,
-                                           cfg.opacity_threshold, return_scratch=True)
+        ids, vcount, _, cull_scratch = cull_ids(g, N, cam, self.device, cfg.near_plane, cfg.far_plane,
+                                                cfg.opacity_threshold, sync=False, return_scratch=True)
         if timer:
             timer.mark("cull")
-        frame = render_forward(g, ids, V, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
-                               timer=timer)
+        # buffers are sized from N and the entry counts of earlier views, before
+        # the counts are read back
+        frame = render_forward(g, ids, N, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
+                               timer=timer, v_count=vcount, k_hint=self._k_hint)
+        self._k_hint = max(self._k_hint, frame.K + frame.K // 8)
         dL_dcolor = self._l1_dssim(frame, target) if ssim_loss else None
         if ssim_loss and timer:
             timer.mark("loss")
