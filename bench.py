@@ -509,8 +509,8 @@ def main():
                            "grad_reduce": ("nvlink multicast row sum" if runner.fused_reduce is not None else
                                            ("nccl all-reduce" if world > 1 else "none")),
                            "grad_row_floats": runner.g_stride,
-                           "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v/grad slabs (0.96 GB) "
-                                 "every step"},
+                           "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v slabs (0.72 GB) and "
+                                 "the seen gradient rows every step"},
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,
                 "adam_gbs": per.get("adam", {}).get("gbs"),
                 "kernels_ms": {k: round(v["ms"], 4) for k, v in per.items()},
