@@ -172,6 +172,10 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
     if (mylast > 0) atomicMax(&smax, mylast);
     __syncthreads();
     const int max_last = smax;
+    // this warp's own last used entry: staged splats past it reach none of its pixels
+    int wlast = mylast;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wlast = max(wlast, __shfl_xor_sync(kFull, wlast, o));
 
     for (int bend = rg.start + max_last; bend > rg.start; bend -= kBatch) {
         const int bstart = max(bend - kBatch, rg.start);
@@ -186,14 +190,16 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             s2[j] = splats[3 * vi + 2];
         }
         __syncthreads();
-        // which staged splats can reach this warp's pixel block (same test as the forward)
+        // which staged splats can reach this warp's pixel block (same test as the forward),
+        // among those before the warp's last used entry
+        const int kend = min(cnt, wlast - (bstart - rg.start));
         unsigned hits[kBatch / 32];
 #pragma unroll
         for (int i = 0; i < kBatch / 32; ++i) {
             const int k = 32 * i + lane;
             const bool h =
-                k < cnt && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + Layout::cols - 1, by0,
-                                            by0 + Layout::rows - 1, p);
+                k < kend && splat_hits_block(s0[k], s1[k], s2[k].z, bx0, bx0 + Layout::cols - 1, by0,
+                                             by0 + Layout::rows - 1, p);
             hits[i] = __ballot_sync(kFull, h);
         }
 #pragma unroll
