@@ -115,3 +115,47 @@ def test_densify_out_of_capacity_raises():
     al.count.fill_(1.0)
     with pytest.raises(MemoryError):
         r.densify(3000)
+
+
+def test_densify_rounds_on_the_stress_workload():
+    """The densify/prune stress workload's shape: 300,000 Gaussians in the
+    4,000,000-slot pool, 1920x1080 views, a densify step every 100 training
+    steps.  The first two rounds use the statistics the training accumulated;
+    the third scales them up (mean view-space gradient around the 2e-4
+    threshold) so that the split/clone path runs on the grown pool.  Each
+    round's decisions, children, pool rows, moments, table and free list are
+    compared bit for bit with the oracle given the same statistics and noise."""
+    r = runner_for_workload("densify-4m", max_steps=3000, num_views=16)
+    al = r.allocator
+    assert al.max_gaussians == 4_000_000 and al.num_active == 300_000
+    step = 0
+    refined = 0
+    for rnd in range(3):
+        for _ in range(100):
+            step += 1
+            r.train_step(step % 16, step)
+        torch.cuda.synchronize()
+        if rnd == 2:
+            live = al.count > 0
+            al.grad2d.copy_(torch.where(live, al.grad2d / al.grad2d[live].mean() * 2e-4 * al.count, al.grad2d))
+        o = snapshot(al)
+        N = al.num_active
+        noise = {"means1": torch.randn((N, 3), device=DEV), "means2": torch.randn((N, 3), device=DEV),
+                 "quats2": torch.randn((N, 4), device=DEV)}
+        n_p, n_s = r.densify(step, noise=noise)
+        torch.cuda.synchronize()
+        act = {k: o.active(k) for k in o.pools}
+        refine, split, prune = odens.densify_masks(o.grad2d[o.table], o.count[o.table], act["scales"],
+                                                   act["opacities"], act["means"], act["quats"], r.scene_scale, N)
+        flags = r.last_densify["flags"].cpu().numpy()
+        np.testing.assert_array_equal((flags & 1) != 0, prune, err_msg=f"round {rnd} prune")
+        np.testing.assert_array_equal((flags & 2) != 0, refine, err_msg=f"round {rnd} refine")
+        np.testing.assert_array_equal((flags & 4) != 0, split, err_msg=f"round {rnd} split")
+        ns = int(refine.sum())
+        nz = {k: v[:ns].cpu().numpy() for k, v in noise.items()}
+        sp = odens.child_params(act, refine, split, nz["means1"], nz["means2"], nz["quats2"])
+        exp_p, exp_s = o.split_and_prune(prune, refine, sp)
+        assert (n_p, n_s) == (exp_p, exp_s), f"round {rnd}"
+        assert_same(al, o, f"round {rnd}")
+        refined += n_s
+    assert refined > 0  # the rounds exercised the split/clone path
