@@ -43,6 +43,38 @@ inline int check_launch(const char* what, int launched = 1) {
 
 inline unsigned grid_for(int64_t n, int block) { return (unsigned)((n + block - 1) / block); }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with launch_pdl may
+// be scheduled as soon as every block of the previous kernel in its stream has
+// exited, before that grid's completion has been processed, which removes most
+// of the gap between short dependent kernels.  Such a kernel must call
+// pdl_wait() before it reads or writes any global memory that earlier work in
+// the stream touches: the wait returns once the previous grid has completed
+// and its memory operations are visible (in a kernel launched without the
+// attribute it returns at once).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                      Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    note_launches(1);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(GS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    }
+    return GS_OK;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- device helpers

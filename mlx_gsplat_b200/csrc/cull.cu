@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(kCullThreads) cull_write(const uint32_t* __res
                                                            const uint32_t* __restrict__ chunk_offsets,
                                                            const int32_t* __restrict__ gather,
                                                            int32_t* __restrict__ out_ids) {
+    pdl_wait();
     __shared__ uint32_t woff[kCullChunk / 32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t base = (int64_t)blockIdx.x * kCullChunk;
@@ -151,9 +152,9 @@ int cull(const gs_gaussians& g, int64_t n, const gs_camera& cam, float near_p, f
     cull_flags<<<(unsigned)chunks, kCullThreads, 0, stream>>>(g, n, cp, words, counts);
     GS_TRY(check_launch("cull_flags"));
     // counts -> offsets in place; the total lands in counts[chunks]
-    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream));
-    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, nullptr, out_ids);
-    GS_TRY(check_launch("cull_write"));
+    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream, true));
+    GS_TRY(launch_pdl("cull_write", cull_write, dim3((unsigned)chunks), dim3(kCullThreads), stream,
+                      (const uint32_t*)words, n, (const uint32_t*)counts, (const int32_t*)nullptr, out_ids));
     cudaMemcpyAsync(out_count, counts + chunks, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
     return check_launch("cull count copy", 0);
 }
@@ -202,9 +203,9 @@ int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, 
     p += align_up((size_t)(chunks + 1) * 4, 256);
     flag_words<<<(unsigned)chunks, kCullThreads, 0, stream>>>(flags, n, mask, value, words, counts);
     GS_TRY(check_launch("flag_words"));
-    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream));
-    cull_write<<<(unsigned)chunks, kCullThreads, 0, stream>>>(words, n, counts, gather, out);
-    GS_TRY(check_launch("compact write"));
+    GS_TRY(scan_exclusive(counts, counts, chunks, p, scan_scratch_bytes(chunks), stream, true));
+    GS_TRY(launch_pdl("compact write", cull_write, dim3((unsigned)chunks), dim3(kCullThreads), stream,
+                      (const uint32_t*)words, n, (const uint32_t*)counts, gather, out));
     cudaMemcpyAsync(out_count, counts + chunks, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
     return check_launch("compact count copy", 0);
 }

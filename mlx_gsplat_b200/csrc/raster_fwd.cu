@@ -161,6 +161,7 @@ __device__ __forceinline__ uint32_t block_flag_prefix(bool f, uint32_t* wsum, ui
 __global__ void __launch_bounds__(kBigThreads) bin_count_big_kernel(const float4* __restrict__ splats, BinScratch bs,
                                                                     RasterParams p,
                                                                     uint32_t* __restrict__ tile_counts) {
+    pdl_wait();
     const uint32_t n = *bs.big_count;
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
         const uint32_t vi = bs.big_list[i];
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(kBigThreads) bin_emit_big_kernel(const float4*
                                                                    const uint32_t* __restrict__ tile_counts,
                                                                    RasterParams p, uint32_t* __restrict__ tile_keys,
                                                                    uint32_t* __restrict__ vals) {
+    pdl_wait();
     __shared__ uint32_t wsum[kBigThreads / 32];
     const uint32_t n = *bs.big_count;
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
@@ -662,9 +664,8 @@ extern "C" int gs_project_forward(const gs_gaussians* g, const int32_t* ids, int
                                                                         depth_keys, tile_counts, use_bs, bs);
     if (use_bs) {
         GS_TRY(check_launch("project_fwd_kernel"));
-        bin_count_big_kernel<<<kBigGrid, kBigThreads, 0, (cudaStream_t)stream>>>(
-            reinterpret_cast<const float4*>(splats), bs, p, tile_counts);
-        return check_launch("bin_count_big_kernel");
+        return launch_pdl("bin_count_big_kernel", bin_count_big_kernel, dim3(kBigGrid), dim3(kBigThreads),
+                          (cudaStream_t)stream, reinterpret_cast<const float4*>(splats), bs, p, tile_counts);
     }
     return check_launch("project_fwd_kernel");
 }
@@ -686,7 +687,8 @@ extern "C" int gs_bin_offsets(const uint32_t* order, const uint32_t* tile_counts
                                                                                            num_visible, gathered);
         GS_TRY(check_launch("gather_counts_kernel"));
     }
-    return scan_exclusive(gathered, offsets, num_visible, p, scan_scratch_bytes(num_visible), (cudaStream_t)stream);
+    return scan_exclusive(gathered, offsets, num_visible, p, scan_scratch_bytes(num_visible), (cudaStream_t)stream,
+                          true);
 }
 
 extern "C" int gs_bin_emit(const float* splats, const uint32_t* order, const uint32_t* offsets,
@@ -705,9 +707,9 @@ extern "C" int gs_bin_emit(const float* splats, const uint32_t* order, const uin
         capacity, overflow_flag, use_bs, bs);
     if (use_bs) {
         GS_TRY(check_launch("bin_emit_kernel"));
-        bin_emit_big_kernel<<<kBigGrid, kBigThreads, 0, (cudaStream_t)stream>>>(
-            reinterpret_cast<const float4*>(splats), bs, tile_counts, p, tile_keys, entry_vals);
-        return check_launch("bin_emit_big_kernel");
+        return launch_pdl("bin_emit_big_kernel", bin_emit_big_kernel, dim3(kBigGrid), dim3(kBigThreads),
+                          (cudaStream_t)stream, reinterpret_cast<const float4*>(splats), bs, tile_counts, p, tile_keys,
+                          entry_vals);
     }
     return check_launch("bin_emit_kernel");
 }

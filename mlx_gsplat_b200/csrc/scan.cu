@@ -2,7 +2,9 @@
 //   1. per 2048-element tile: tile sums
 //   2. one CTA: exclusive scan of the tile sums (loops when there are many)
 //   3. per tile: block scan plus the tile's offset.
-// No inter-CTA waiting, so nothing can spin.
+// No inter-CTA waiting, so nothing can spin.  The second and third kernels
+// (and the first, when the caller's previous operation was one of this
+// library's kernels) use programmatic dependent launches.
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -42,6 +44,7 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* s
 
 __global__ void __launch_bounds__(kScanThreads) scan_tile_sums(const uint32_t* __restrict__ in, int64_t n,
                                                                uint32_t* __restrict__ tile_sums) {
+    pdl_wait();
     __shared__ uint32_t sw[33];
     const int64_t base = (int64_t)blockIdx.x * kScanTile + (int64_t)threadIdx.x * kScanItems;
     uint32_t s = 0;
@@ -55,6 +58,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_tile_sums(const uint32_t* _
 
 __global__ void __launch_bounds__(kScanThreads) scan_tile_offsets(uint32_t* __restrict__ sums, int64_t n_tiles,
                                                                   uint32_t* __restrict__ total_out) {
+    pdl_wait();
     __shared__ uint32_t sw[33];
     uint32_t carry = 0;
     for (int64_t base = 0; base < n_tiles; base += kScanThreads) {
@@ -70,6 +74,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_tile_offsets(uint32_t* __re
 
 __global__ void __launch_bounds__(kScanThreads) scan_tiles(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
                                                            int64_t n, const uint32_t* __restrict__ tile_offsets) {
+    pdl_wait();
     __shared__ uint32_t sw[33];
     const int64_t base = (int64_t)blockIdx.x * kScanTile + (int64_t)threadIdx.x * kScanItems;
     uint32_t v[kScanItems];
@@ -93,7 +98,7 @@ size_t scan_scratch_bytes(int64_t n) {
 }
 
 int scan_exclusive(const uint32_t* in, uint32_t* out, int64_t n, void* scratch, size_t scratch_bytes,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, bool after_kernel) {
     GS_REQUIRE(n >= 0, "scan: negative n");
     GS_REQUIRE(scratch_bytes >= scan_scratch_bytes(n), "scan: scratch too small");
     if (n == 0) {
@@ -102,10 +107,17 @@ int scan_exclusive(const uint32_t* in, uint32_t* out, int64_t n, void* scratch, 
     }
     const int64_t tiles = (n + kScanTile - 1) / kScanTile;
     uint32_t* sums = reinterpret_cast<uint32_t*>(scratch);
-    scan_tile_sums<<<(unsigned)tiles, kScanThreads, 0, stream>>>(in, n, sums);
-    scan_tile_offsets<<<1, kScanThreads, 0, stream>>>(sums, tiles, out + n);
-    scan_tiles<<<(unsigned)tiles, kScanThreads, 0, stream>>>(in, out, n, sums);
-    return check_launch("scan_exclusive", 3);
+    if (after_kernel) {
+        GS_TRY(launch_pdl("scan_tile_sums", scan_tile_sums, dim3((unsigned)tiles), dim3(kScanThreads), stream, in, n,
+                          sums));
+    } else {
+        scan_tile_sums<<<(unsigned)tiles, kScanThreads, 0, stream>>>(in, n, sums);
+        GS_TRY(check_launch("scan_tile_sums"));
+    }
+    GS_TRY(launch_pdl("scan_tile_offsets", scan_tile_offsets, dim3(1), dim3(kScanThreads), stream, sums, tiles,
+                      out + n));
+    return launch_pdl("scan_tiles", scan_tiles, dim3((unsigned)tiles), dim3(kScanThreads), stream, in, out, n,
+                      (const uint32_t*)sums);
 }
 
 }  // namespace gs

@@ -23,6 +23,7 @@ constexpr int kBins = 256;
 __global__ void __launch_bounds__(kSortThreads) radix_upsweep(const uint32_t* __restrict__ keys, int64_t n, int shift,
                                                               uint32_t mask, uint32_t* __restrict__ counts,
                                                               int64_t n_tiles) {
+    pdl_wait();
     __shared__ uint32_t hist[kBins];
     hist[threadIdx.x] = 0;
     __syncthreads();
@@ -42,6 +43,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
                                                                 uint32_t* __restrict__ vals_out, int64_t n, int shift,
                                                                 uint32_t mask, const uint32_t* __restrict__ offsets,
                                                                 int64_t n_tiles) {
+    pdl_wait();
     __shared__ uint32_t goff[kBins];
     __shared__ uint32_t lstart[kBins];  // tile-local start of each digit
     __shared__ uint32_t wtot[kSortWarps];
@@ -171,11 +173,18 @@ int radix_sort_pairs(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t*
         const bool to_out = ((passes - 1 - pass) % 2) == 0;
         uint32_t* dk = to_out ? keys_out : alt_k;
         uint32_t* dv = to_out ? vals_out : alt_v;
-        radix_upsweep<<<(unsigned)tiles, kSortThreads, 0, stream>>>(src_k, n, shift, mask, counts, tiles);
-        GS_TRY(scan_exclusive(counts, counts, nc, scan_scratch, scan_bytes, stream));
-        radix_downsweep<<<(unsigned)tiles, kSortThreads, 0, stream>>>(src_k, src_v, dk, dv, n, shift, mask, counts,
-                                                                      tiles);
-        GS_TRY(check_launch("radix pass", 2));
+        // every kernel after the first follows one of this sort's own kernels:
+        // programmatic dependent launches (each kernel waits for its predecessor)
+        if (pass == 0) {
+            radix_upsweep<<<(unsigned)tiles, kSortThreads, 0, stream>>>(src_k, n, shift, mask, counts, tiles);
+            GS_TRY(check_launch("radix_upsweep"));
+        } else {
+            GS_TRY(launch_pdl("radix_upsweep", radix_upsweep, dim3((unsigned)tiles), dim3(kSortThreads), stream, src_k,
+                              n, shift, mask, counts, tiles));
+        }
+        GS_TRY(scan_exclusive(counts, counts, nc, scan_scratch, scan_bytes, stream, true));
+        GS_TRY(launch_pdl("radix_downsweep", radix_downsweep, dim3((unsigned)tiles), dim3(kSortThreads), stream, src_k,
+                          src_v, dk, dv, n, shift, mask, (const uint32_t*)counts, tiles));
         src_k = dk;
         src_v = dv;
     }
