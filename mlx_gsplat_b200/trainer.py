@@ -261,8 +261,10 @@ class RunnerMLX:
                 for c in range(L.ncols)]
 
     def full_gradient_rows(self, step: int, n: Optional[int] = None) -> torch.Tensor:
-        """The gradient rows as ``[n, ncols]`` parameter columns (narrow rows
-        expanded as Adam expands them); for inspection."""
+        """The gradient rows as ``[n, ncols]`` parameter columns, for inspection:
+        narrow rows get their regulariser-only colour columns rebuilt from the
+        view count as Adam rebuilds them (the cross-GPU bias and 1/world scale
+        Adam also applies in the summed row mode are not)."""
         L = self.layout
         n = self.allocator.num_active if n is None else n
         G = self.grad[:n]
