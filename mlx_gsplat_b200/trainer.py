@@ -59,7 +59,9 @@ class MLXConfig:
     # B200 additions
     betas: Tuple[float, float] = (0.9, 0.999)
     eps: float = 1e-8
-    loss: str = "l1"
+    # "l1+dssim": the reference trainer's loss with a target (trainer.py:276-279);
+    # "l1": mean |render - target| (the benchmark workloads); "mean": mean(render)
+    loss: str = "l1+dssim"
     param_reg: float = 1e-5
     densify: bool = True
     opacity_reset: bool = True
@@ -83,6 +85,9 @@ class MLXConfig:
     # rows keep the 23 columns with gradients plus a view count and Adam
     # rebuilds the rest (2.5x fewer bytes summed over GPUs)
     compact_grad_rows: bool = True
+    # write ``<scene>_mlx_custom_3dgs.ply`` when train() finishes, as the
+    # reference's train() does (trainer.py:566-568)
+    export_ply_on_finish: bool = False
 
 
 def lr_at(lr: float, step: int, max_steps: int) -> float:
@@ -550,7 +555,14 @@ class RunnerMLX:
             if log_every and (step % log_every == 0 or step == 1):
                 print(f"Step {step:5d} | Active: {self.allocator.num_active} | loss {float(self.loss_value()):.5f}")
         torch.cuda.synchronize(self.device)
-        return time.time() - t0
+        elapsed = time.time() - t0
+        if log_every:
+            print(f"\n[Finished] 3DGS training complete in {elapsed:.2f} seconds.")
+            print(f"Average speed: {elapsed / max(cfg.max_steps, 1) * 1000:.2f} ms/iter.")
+        if cfg.export_ply_on_finish:
+            name = os.path.basename(os.path.abspath(cfg.data_dir).rstrip("/\\"))
+            self.export_to_ply(f"{name}_mlx_custom_3dgs.ply")
+        return elapsed
 
 
 def runner_for_workload(name: str, max_steps: int = 100, num_views: Optional[int] = None, device=None,

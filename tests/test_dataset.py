@@ -212,3 +212,16 @@ def test_trainer_reference_synthetic_mode():
     f = r.last_frame
     assert (f.cam.render_width, f.cam.render_height) == (200, 150) and f.V > 0
     assert abs(float(r.loss_value()) - float(f.color.mean())) < 1e-6
+
+
+@pytest.mark.gpu
+def test_command_line_trains_and_exports(tmp_path, monkeypatch):
+    """``python -m mlx_gsplat_b200.train`` on the fixture scene: trains with the
+    reference's loss and writes ``<scene>_mlx_custom_3dgs.ply`` at the end."""
+    from mlx_gsplat_b200 import train
+    monkeypatch.chdir(tmp_path)
+    r = train.main(["--data_dir", SCENE, "--max_steps", "5", "--data_factor", "1", "--render_width", "24",
+                    "--render_height", "18", "--max_gaussians", "2000"])
+    out = tmp_path / "colmap_scene_mlx_custom_3dgs.ply"
+    assert out.exists() and out.stat().st_size > 300 * 14 * 4
+    assert r.cfg.loss == "l1+dssim" and np.isfinite(float(r.loss_value()))
