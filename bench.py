@@ -82,7 +82,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the densify and 6M-row Adam measurements")
     ap.add_argument("--multicast", action="store_true",
-                    help="N > 1: sum the gradient rows with the NVLink multicast kernels instead of NCCL")
+                    help="N > 1: the sharded Adam fused with the NVLink multicast gradient sum and parameter "
+                         "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
     return ap.parse_args()
@@ -506,8 +507,9 @@ def main():
                 "config": {"workload": args.workload, "gaussians": wl.num_gaussians, "image": f"{wl.width}x{wl.height}",
                            "sh_degree": wl.sh_degree, "views": nv, "views_per_gpu_per_step": 1,
                            "parallelism": f"views-dp{world}", "loss": "l1",
-                           "grad_reduce": ("nvlink multicast row sum" if runner.fused_reduce is not None else
-                                           ("nccl all-reduce" if world > 1 else "none")),
+                           "grad_reduce": ("nvlink multicast sum fused into the sharded adam" if runner.sharded else
+                                           ("nvlink multicast row sum" if runner.fused_reduce is not None else
+                                            ("nccl all-reduce" if world > 1 else "none"))),
                            "grad_row_floats": runner.g_stride,
                            "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v slabs (0.72 GB) and "
                                  "the seen gradient rows every step"},

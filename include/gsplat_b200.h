@@ -407,6 +407,27 @@ int gs_group_barrier(uint32_t* const* peer_pads, int32_t rank, int32_t world, in
 int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, int64_t num_rows, int64_t stride,
                           gs_stream_t stream);
 
+/* The slab Adam of one GPU of a views-data-parallel group, fused with the
+ * group's gradient sum and parameter broadcast (no reference counterpart: the
+ * reference runs on one device).  The GPU updates the rows whose physical slot
+ * it owns (slot % world == rank): it reads each such row's gradient summed over
+ * every GPU's copy of the gradient rows through their NVLink multicast address
+ * ``g_multicast`` (rows by active id, ``g_stride`` floats, narrow rows as in
+ * gs_fused_adam_slab), updates theta, m and v in its own memory, and stores the
+ * first ``hot_cols`` columns of the new theta row to every GPU through the
+ * parameter slab's multicast address ``theta_multicast`` (the columns the
+ * rasterizer reads every step; the other columns and the moments stay with the
+ * owner until the caller gathers them).  Fused semantics with the approximate
+ * step; ``grad_scale`` and ``grad_bias_host`` as in gs_fused_adam_slab.  Call
+ * it between two gs_group_barrier calls: after every GPU wrote its gradient
+ * rows, before any GPU reads parameters again. */
+int gs_fused_adam_slab_sharded(float* theta, float* theta_multicast, const float* g_multicast, float* m, float* v,
+                               const int32_t* indices, int64_t num_active, int ncols, int64_t stride,
+                               int64_t g_stride, const float* col_lo, const float* col_hi, int quat_col, double lr,
+                               double beta1, double beta2, float eps, float weight_decay, int step, float grad_scale,
+                               const float* grad_bias_host, int g_cols, int count_col, const float* count_coef_host,
+                               int rank, int world, int hot_cols, gs_stream_t stream);
+
 /* ------------------------------------------------------------------ pool / densify */
 
 /* Row flags of the densify step. */

@@ -83,7 +83,10 @@ class SlabLayout:
 
 class PointerStableChunkedAllocator:
     def __init__(self, max_gaussians: int, sh_degree: int = 3, feature_dim: Optional[int] = None,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, theta_storage: Optional[torch.Tensor] = None):
+        """``theta_storage``: a caller-owned ``[max_gaussians, stride]`` float32
+        device tensor to hold the parameter slab (e.g. symmetric memory with a
+        multicast mapping for the sharded multi-GPU Adam)."""
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.max_gaussians = int(max_gaussians)
         self.sh_degree = sh_degree
@@ -96,7 +99,12 @@ class PointerStableChunkedAllocator:
         self.shN_dim = ((sh_degree + 1) ** 2 - 1) * 3
 
         L = self.layout
-        self.theta = torch.empty((self.max_gaussians, L.stride), dtype=torch.float32, device=self.device)
+        if theta_storage is not None:
+            if tuple(theta_storage.shape) != (self.max_gaussians, L.stride) or theta_storage.dtype != torch.float32:
+                raise ValueError(f"theta_storage must be float32 [{self.max_gaussians}, {L.stride}]")
+            self.theta = theta_storage
+        else:
+            self.theta = torch.empty((self.max_gaussians, L.stride), dtype=torch.float32, device=self.device)
         self.theta.copy_(torch.from_numpy(L.init_row()).to(self.device).expand_as(self.theta))
         self.adam_m = torch.zeros_like(self.theta)
         self.adam_v = torch.zeros_like(self.theta)

@@ -274,6 +274,107 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
     }
 }
 
+// ---------------------------------------------------------------- sharded multi-GPU Adam
+// The slab Adam of one GPU of a views-data-parallel group, fused with the
+// group's gradient sum and parameter broadcast over NVLink multicast: the GPU
+// updates only the rows whose physical slot it owns (slot % world == rank).
+// For such a row it loads the gradient row summed across every GPU's copy
+// (multimem.ld_reduce: the switch adds them), updates theta, m and v in its own
+// memory, and stores the first ``hot_chunks`` 16-byte chunks of the new theta
+// row to every GPU's copy (multimem.st) — the columns the rasterizer reads each
+// step; the other columns and the moments stay with the owner until the caller
+// consolidates them.  Gradient rows are indexed by active id, theta/m/v rows by
+// physical slot.  Semantics: the fused kernel's (scrub and clamp) with the
+// approximate step, as adam_slab_kernel<false, true, .>.
+__device__ __forceinline__ float4 mc_ld_reduce(const float4* p) {
+    float4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void mc_st(float4* p, const float4& r) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(r.x), "f"(r.y),
+                 "f"(r.z), "f"(r.w)
+                 : "memory");
+}
+
+template <bool kNarrow>
+__global__ void __launch_bounds__(256, 4) adam_sharded_kernel(
+    float4* __restrict__ theta, float4* __restrict__ theta_mc, const float4* __restrict__ g_mc,
+    float4* __restrict__ m, float4* __restrict__ v, const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
+    int lane_shift, int g_chunks, int ncols, int quat_chunk, int64_t half, int g_cols, int count_col, int rank,
+    int world, int hot_chunks, AdamScalars s, SlabCols cols) {
+    __shared__ ColsSmem cs;
+    if (threadIdx.x < kMaxSlabCols) {
+        cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
+        cs.lo[threadIdx.x] = cols.lo[threadIdx.x];
+        cs.hi[threadIdx.x] = cols.hi[threadIdx.x];
+        cs.gdef[threadIdx.x] = cols.gdef[threadIdx.x];
+        cs.gbias[threadIdx.x] = cols.gbias[threadIdx.x];
+        cs.gcoef[threadIdx.x] = cols.gcoef[threadIdx.x];
+    }
+    __syncthreads();
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int c4 = (int)(t0 & ((1 << lane_shift) - 1));
+    const bool live = c4 < chunks && 4 * c4 < ncols;
+    const int64_t ra = t0 >> lane_shift, rb = (t0 + half) >> lane_shift;
+    int64_t sa = 0, sb = 0;
+    bool va = live && ra < n_rows, vb = live && rb < n_rows;
+    if (va) sa = __ldg(idx + ra);
+    if (vb) sb = __ldg(idx + rb);
+    va = va && (sa % world) == rank;
+    vb = vb && (sb % world) == rank;
+    const int64_t offa = sa * chunks + c4, offb = sb * chunks + c4;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 tha = z, ma = z, vva = z, ga = z, thb = z, mb = z, vvb = z, gb = z;
+    const bool load_g = !kNarrow || 4 * c4 < g_cols || c4 == (count_col >> 2);
+    if (va) {
+        tha = __ldcs(theta + offa);
+        ma = __ldcs(m + offa);
+        vva = __ldcs(v + offa);
+        if (load_g) ga = mc_ld_reduce(g_mc + ra * g_chunks + c4);
+    }
+    if (vb) {
+        thb = __ldcs(theta + offb);
+        mb = __ldcs(m + offb);
+        vvb = __ldcs(v + offb);
+        if (load_g) gb = mc_ld_reduce(g_mc + rb * g_chunks + c4);
+    }
+    if (kNarrow) {
+        // the summed view count of the row, from the lane whose chunk holds it
+        const int src = count_col >> 2, k = count_col & 3, width = 1 << lane_shift;
+        const float cnt_a = __shfl_sync(kFull, float4_comp(ga, k), src, width);
+        const float cnt_b = __shfl_sync(kFull, float4_comp(gb, k), src, width);
+        if (4 * c4 + 3 >= g_cols) {
+            if (va) ga = narrow_grad(4 * c4 < g_cols ? ga : z, c4, g_cols, cnt_a, cs);
+            if (vb) gb = narrow_grad(4 * c4 < g_cols ? gb : z, c4, g_cols, cnt_b, cs);
+        }
+    }
+    const bool renorm = c4 == quat_chunk, hot = c4 < hot_chunks;
+    if (va) {
+        slab_update<false, true>(tha, ma, vva, ga, 4 * c4, ncols, renorm, s, cs);
+        __stcs(m + offa, ma);
+        __stcs(v + offa, vva);
+        if (hot)
+            mc_st(theta_mc + offa, tha);
+        else
+            __stcs(theta + offa, tha);
+    }
+    if (vb) {
+        slab_update<false, true>(thb, mb, vvb, gb, 4 * c4, ncols, renorm, s, cs);
+        __stcs(m + offb, mb);
+        __stcs(v + offb, vvb);
+        if (hot)
+            mc_st(theta_mc + offb, thb);
+        else
+            __stcs(theta + offb, thb);
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // publish before the group's barrier
+}
+
 // Host-side scalars for each semantics.  ``lr``/``beta1``/``beta2`` arrive in
 // float64 (the Python values): the fused mode rounds them to float32 first, as
 // the Metal kernel receives them (src/mlx_extensions.cpp:259-263); the pure
@@ -400,6 +501,58 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         quat_col < 0 ? -1 : quat_col / 4, half, visible_words, g_cols, g_cols < ncols ? count_col : 0, row_select,
         s, cols);
     return check_launch("adam_slab_kernel");
+}
+
+extern "C" int gs_fused_adam_slab_sharded(float* theta, float* theta_multicast, const float* g_multicast,
+                                          float* m, float* v, const int32_t* indices, int64_t num_active, int ncols,
+                                          int64_t stride, int64_t g_stride, const float* col_lo, const float* col_hi,
+                                          int quat_col, double lr, double beta1, double beta2, float eps,
+                                          float weight_decay, int step, float grad_scale,
+                                          const float* grad_bias_host, int g_cols, int count_col,
+                                          const float* count_coef_host, int rank, int world, int hot_cols,
+                                          gs_stream_t stream) {
+    GS_REQUIRE(world >= 1 && rank >= 0 && rank < world, "adam_sharded: bad rank/world");
+    GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_sharded: ncols must be in [1, %d]", kMaxSlabCols);
+    GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && stride <= 128 && g_stride >= g_cols,
+               "adam_sharded: strides must be multiples of 4, ncols <= stride <= 128, g_stride >= g_cols");
+    GS_REQUIRE(g_cols > 0 && g_cols <= ncols, "adam_sharded: g_cols must be in [1, ncols]");
+    GS_REQUIRE(g_cols == ncols || (count_coef_host && count_col >= g_cols && count_col < g_stride &&
+                                   count_col < stride && (count_col & ~3) < ncols),
+               "adam_sharded: narrow gradient rows need count_coef_host and a count column in [g_cols, g_stride)");
+    GS_REQUIRE(hot_cols >= 0 && hot_cols % 4 == 0 && hot_cols <= stride, "adam_sharded: hot_cols must be a "
+               "multiple of 4 within the row");
+    GS_REQUIRE(quat_col < 0 || (quat_col % 4 == 0 && quat_col + 4 <= ncols), "adam_sharded: bad quat_col");
+    GS_REQUIRE(step >= 1 && num_active >= 0, "adam_sharded: bad step/num_active");
+    if (num_active == 0) return GS_OK;
+    GS_REQUIRE(theta && theta_multicast && g_multicast && m && v && indices && col_lo && col_hi,
+               "adam_sharded: null pointer");
+    GS_REQUIRE(aligned16(theta) && aligned16(theta_multicast) && aligned16(g_multicast) && aligned16(m) &&
+               aligned16(v), "adam_sharded: bases must be 16-byte aligned");
+    double bc1;
+    AdamScalars s = make_scalars(GS_ADAM_FUSED, beta1, beta2, eps, weight_decay, step, grad_scale, &bc1);
+    SlabCols cols;
+    for (int c = 0; c < kMaxSlabCols; ++c) {
+        const bool on = c < ncols;
+        cols.lo[c] = on ? col_lo[c] : 0.f;
+        cols.hi[c] = on ? col_hi[c] : 0.f;
+        cols.step_size[c] = on ? step_size_for(GS_ADAM_FUSED, lr, 1.0, bc1) : 0.f;
+        cols.gdef[c] = 0.f;
+        cols.gbias[c] = (on && grad_bias_host) ? grad_bias_host[c] : 0.f;
+        cols.gcoef[c] = (on && c >= g_cols) ? count_coef_host[c] : 0.f;
+    }
+    s.has_bias = grad_bias_host != nullptr;
+    const int chunks = (int)(stride / 4);
+    int shift = 0;
+    while ((1 << shift) < chunks) ++shift;
+    const int64_t n = num_active << shift;
+    const int64_t half = (n + 511) / 512 * 256;
+    auto kernel = g_cols < ncols ? adam_sharded_kernel<true> : adam_sharded_kernel<false>;
+    kernel<<<grid_for(half, 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<float4*>(theta), reinterpret_cast<float4*>(theta_multicast),
+        reinterpret_cast<const float4*>(g_multicast), reinterpret_cast<float4*>(m), reinterpret_cast<float4*>(v),
+        indices, num_active, chunks, shift, (int)(g_stride / 4), ncols, quat_col < 0 ? -1 : quat_col / 4, half,
+        g_cols, g_cols < ncols ? count_col : 0, rank, world, hot_cols / 4, s, cols);
+    return check_launch("adam_sharded_kernel");
 }
 
 extern "C" int gs_launch_fused_adam_step(uint64_t theta_addr, uint64_t g_addr, uint64_t m_addr, uint64_t v_addr,

@@ -83,7 +83,10 @@ class FusedRowReduce:
 
     MAX_POLLS = 1 << 25  # about 3 s of polling per wait
 
-    def __init__(self, rows: int, cols: int, device, pg):
+    def __init__(self, rows: int, cols: int, device, pg, theta_cols: Optional[int] = None):
+        """``theta_cols``: also allocate the ``[rows, theta_cols]`` parameter
+        slab in symmetric memory with a multicast mapping (``theta``,
+        ``theta_multicast``) for the sharded Adam (``gs_fused_adam_slab_sharded``)."""
         import torch.distributed._symmetric_memory as symm
         from . import _lib
         self.device = torch.device(device)
@@ -101,6 +104,14 @@ class FusedRowReduce:
         self.multicast = int(self._rows_hdl.multicast_ptr)
         if self.multicast == 0:
             raise RuntimeError("no NVLink multicast mapping for the gradient rows")
+        self.theta = None
+        self.theta_multicast = 0
+        if theta_cols is not None:
+            self.theta = symm.empty((rows, theta_cols), dtype=torch.float32, device=self.device)
+            self._theta_hdl = symm.rendezvous(self.theta, name)
+            self.theta_multicast = int(self._theta_hdl.multicast_ptr)
+            if self.theta_multicast == 0:
+                raise RuntimeError("no NVLink multicast mapping for the parameter slab")
         self.pads = symm.empty((2 * self.world,), dtype=torch.int32, device=self.device)
         self.pads.zero_()
         self._pads_hdl = symm.rendezvous(self.pads, name)
@@ -129,6 +140,24 @@ class FusedRowReduce:
         self._lib.check(lib.gs_group_barrier(self.peer_pads.data_ptr(), self.rank, self.world, channel,
                                              self.epoch[channel], self.error.data_ptr(), self.MAX_POLLS,
                                              self._lib.stream_ptr(self.device)), "group barrier")
+
+    def barrier(self, channel: int) -> None:
+        """Group barrier on ``channel`` (0 or 1), enqueued on the current stream."""
+        self._barrier(channel)
+
+    def owned_slots(self, rows: int) -> torch.Tensor:
+        """Boolean mask of the physical slots whose rows this GPU updates in the
+        sharded Adam (slot % world == rank)."""
+        return (torch.arange(rows, device=self.device) % self.world) == self.rank
+
+    def gather_owned_rows(self, t: torch.Tensor, owned: torch.Tensor) -> None:
+        """Every GPU's copy of the slot-indexed rows of ``t`` becomes the owners'
+        rows: the rows this GPU does not own are zeroed, then summed over the
+        group (an NCCL all-reduce); used before densify, export and
+        checkpoints, which read the columns and moments the sharded Adam
+        leaves with the owners."""
+        t[~owned] = 0
+        dist.all_reduce(t, group=self.pg)
 
     def slice_of(self, n_rows: int):
         """This GPU's rows of the sum: a contiguous 1/world share."""

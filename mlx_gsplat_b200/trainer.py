@@ -32,7 +32,7 @@ import numpy as np
 import torch
 
 from . import _lib, distributed, synthetic
-from .allocator import PointerStableChunkedAllocator
+from .allocator import PointerStableChunkedAllocator, SlabLayout
 from .optimizer import FusedMLXAdam
 from .rendering import (DEFAULT_SETTINGS, RasterSettings, camera_struct, cull_ids, gaussians_struct, grads_struct,
                         render_backward, render_forward)
@@ -85,6 +85,10 @@ class MLXConfig:
     # rows keep the 23 columns with gradients plus a view count and Adam
     # rebuilds the rest (2.5x fewer bytes summed over GPUs)
     compact_grad_rows: bool = True
+    # with the multicast gradient sum (fused_reduce): each GPU runs Adam only for
+    # the rows of the pool slots it owns, fused with the sum and the broadcast
+    # of the updated parameters (else the rows are summed and Adam replicated)
+    sharded_adam: bool = True
     # write ``<scene>_mlx_custom_3dgs.ply`` when train() finishes, as the
     # reference's train() does (trainer.py:566-568)
     export_ply_on_finish: bool = False
@@ -192,15 +196,10 @@ class RunnerMLX:
             init_params, viewmats, K, sizes, scene_scale, self.train_dataset = reference_init(cfg)
             if self.train_dataset is not None and cfg.images_on_device and cfg.preload_images:
                 self.train_dataset.to_device(self.device)
-        self.allocator = PointerStableChunkedAllocator(cfg.max_gaussians, cfg.sh_degree, device=self.device)
-        self.allocator.set_initial_gaussians(init_params)
-        self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
-        L = self.allocator.layout
+        L = SlabLayout(cfg.sh_degree)
         self.layout = L
         self.pg = process_group
         self.world = distributed.world_of(process_group)
-        # Across GPUs the gradient rows are summed by NCCL, or (``fused_reduce``)
-        # by this library's NVLink multicast kernels.
         # Gradient rows: the layout of the pooled rows, or narrow rows — the
         # geometry and the 12 colour columns the reference rasterizer evaluates
         # (SH degree <= 1), then one view-count column; every colour column past
@@ -212,10 +211,26 @@ class RunnerMLX:
             self.g_stride = (self.g_cols + 1 + 3) // 4 * 4
         else:
             self.g_cols, self.count_col, self.g_stride = L.ncols, 0, L.stride
+        # Across GPUs the gradient rows are summed by NCCL, or (``fused_reduce``)
+        # through NVLink multicast: by this library's row-sum kernel before a
+        # replicated Adam, or (``cfg.sharded_adam``) inside the sharded Adam,
+        # which updates the rows of the slots this GPU owns and broadcasts the
+        # columns the rasterizer reads (``hot_cols``) to every GPU.
         self.fused_reduce = None
+        self.sharded = False
         if fused_reduce and distributed.FusedRowReduce.available(self.device, process_group):
+            self.sharded = bool(cfg.sharded_adam)
             self.fused_reduce = distributed.FusedRowReduce(cfg.max_gaussians, self.g_stride, self.device,
-                                                           process_group)
+                                                           process_group,
+                                                           theta_cols=L.stride if self.sharded else None)
+        self.allocator = PointerStableChunkedAllocator(
+            cfg.max_gaussians, cfg.sh_degree, device=self.device,
+            theta_storage=self.fused_reduce.theta if self.sharded else None)
+        self.allocator.set_initial_gaussians(init_params)
+        self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
+        # columns every GPU needs each step: what the rasterizer reads
+        self.hot_cols = L.stride if cfg.sh_eval == "full" else (L.color_col + 12 + 3) // 4 * 4
+        self._owned = self.fused_reduce.owned_slots(cfg.max_gaussians) if self.sharded else None
         if self.fused_reduce is not None:
             self.grad = self.fused_reduce.rows
         else:
@@ -358,24 +373,29 @@ class RunnerMLX:
         scale = 1.0
         bias = None
         if mode == "summed":
-            if fused:
+            scale = 1.0 / self.world
+            bias = [self.world * r for r in self._reg_pattern(self.layout.ncols)]
+            if self.sharded:
+                self._sharded_adam(N, step, scale, bias)
+                if timer:
+                    timer.mark("sharded_adam")
+            elif fused:
                 self.fused_reduce.sum_rows(N)
             else:
                 distributed.reduce_gradient_rows(self.grad[:N], self.pg)
-            scale = 1.0 / self.world
-            bias = [self.world * r for r in self._reg_pattern(self.layout.ncols)]
-            if timer:
+            if timer and not self.sharded:
                 timer.mark("row_sum" if fused else "allreduce")
         sparse = mode == "sparse"
         vis = (cull_scratch.data_ptr() + 255) // 256 * 256 if sparse else None
-        self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
-                                 self.allocator.indirection_table, N, self.layout.ncols, self.col_lo, self.col_hi,
-                                 quat_col=self.layout.quat_col, grad_scale=scale, visible_words=vis,
-                                 unseen_grad=self._reg_pattern(self.layout.ncols) if sparse else None,
-                                 grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
-                                 count_coef=self.count_coef(step) if self.g_cols < self.layout.ncols else None)
-        if timer:
-            timer.mark("adam")
+        if not self.sharded:
+            self.optimizer.step_slab(self.allocator.theta, self.grad, self.allocator.adam_m, self.allocator.adam_v,
+                                     self.allocator.indirection_table, N, self.layout.ncols, self.col_lo, self.col_hi,
+                                     quat_col=self.layout.quat_col, grad_scale=scale, visible_words=vis,
+                                     unseen_grad=self._reg_pattern(self.layout.ncols) if sparse else None,
+                                     grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
+                                     count_coef=self.count_coef(step) if self.g_cols < self.layout.ncols else None)
+            if timer:
+                timer.mark("adam")
         if mode == "summed":
             # this GPU's rows for the next step (with the multicast sum the peers
             # are past it: the next step's first barrier orders the rest)
@@ -398,6 +418,33 @@ class RunnerMLX:
             return img
         return bilinear_resize_mlx(img, RH, RW)
 
+    def _sharded_adam(self, N: int, step: int, scale: float, bias) -> None:
+        """Barrier (every GPU wrote its gradient rows), the sharded Adam over the
+        slots this GPU owns, barrier (every broadcast landed and every sum was
+        read, so the rows may be zeroed and the next cull sees the parameters)."""
+        fr = self.fused_reduce
+        al, L = self.allocator, self.layout
+        fr.barrier(0)
+        self.optimizer.step_slab_sharded(al.theta, fr.theta_multicast, fr.multicast, self.g_stride, al.adam_m,
+                                         al.adam_v, al.indirection_table, N, L.ncols, self.col_lo, self.col_hi,
+                                         fr.rank, fr.world, self.hot_cols, quat_col=L.quat_col, grad_scale=scale,
+                                         grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
+                                         count_coef=self.count_coef(step) if self.g_cols < L.ncols else None)
+        fr.barrier(1)
+
+    def gather_sharded_state(self, moments: bool = True) -> None:
+        """With the sharded Adam, the parameter columns past ``hot_cols`` and the
+        moments are current only on the GPU that owns each slot: every GPU's
+        copy becomes the owners' (the parameters, and ``moments`` too).  The
+        densify step, the PLY export and checkpoints call it first."""
+        if not self.sharded:
+            return
+        al = self.allocator
+        self.fused_reduce.gather_owned_rows(al.theta, self._owned)
+        if moments:
+            self.fused_reduce.gather_owned_rows(al.adam_m, self._owned)
+            self.fused_reduce.gather_owned_rows(al.adam_v, self._owned)
+
     # ------------------------------------------------------------------ densify / prune
     def densify(self, step: int, noise: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[int, int]:
         """trainer.py:425-519 on the GPU: decisions from the pooled rows and the
@@ -412,6 +459,7 @@ class RunnerMLX:
         al = self.allocator
         L = self.layout
         N = al.num_active
+        self.gather_sharded_state(moments=False)  # children copy whole parent rows
         distributed.reduce_densify_stats(al.grad2d, al.count, self.pg)
         g = self._gaussians(step)
         flags = torch.empty(max(N, 1), dtype=torch.uint8, device=self.device)
@@ -478,6 +526,7 @@ class RunnerMLX:
         lib = _lib.lib()
         al = self.allocator
         n = al.num_active
+        self.gather_sharded_state(moments=False)
         cols = 14 + L.color_cols  # means 3, normals 3, colours, opacity 1, scales 3, quaternion 4
         out = torch.empty((max(n, 1), cols), dtype=torch.float32, device=self.device)
         _lib.check(lib.gs_export_rows(al.theta.data_ptr(), L.stride, al.indirection_table.data_ptr(), n,
@@ -505,6 +554,7 @@ class RunnerMLX:
         indirection table, the free list, the densification statistics, the
         Adam step and the trainer's step count (``.npz``)."""
         al = self.allocator
+        self.gather_sharded_state()
         torch.cuda.synchronize(self.device)
         state = {k: getattr(al, k).cpu().numpy() for k in self._CKPT_TENSORS}
         state["indirection_table"] = al.indirection_table.cpu().numpy()

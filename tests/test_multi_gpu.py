@@ -1,8 +1,10 @@
-"""Gradient rows summed over GPUs by this library's NVLink multicast kernels
-(bounded device barrier, multimem load-reduce + store of each GPU's slice)
-against the NCCL all-reduce path: a few training steps from the same start
-give the same parameters (rtol 1e-5; the two sums differ only in their
-order).  Needs at least two GPUs of one NVSwitch domain."""
+"""The multi-GPU paths of the training step on two GPUs (``tests/dp_worker.py``):
+the sharded Adam fused with the NVLink multicast gradient sum and parameter
+broadcast, the multicast row sum with a replicated Adam, and the NCCL
+all-reduce of narrow and of full-width gradient rows give the same parameters
+and moments after a few steps and after a densify step (rtol 1e-5; the sums
+differ only in their order).  Needs at least two GPUs of one NVSwitch
+domain."""
 import os
 import subprocess
 import sys
