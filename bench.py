@@ -52,15 +52,12 @@ LIMITERS = {"render_bwd": "fp32 instruction issue (ncu issue-active ~79%, DRAM ~
 
 
 def measured_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch from the committed one-pass ncu capture of this workload."""
-    path = os.path.join(ROOT, "profiles", f"dram_traffic_{workload}.md")
+    """DRAM bytes per launch of ``kernel`` from the committed one-pass ncu capture
+    of this workload (``profiles/dram_traffic.json``), or None."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     if not os.path.exists(path):
         return None
-    key = f"traffic_bytes_per_launch {'adam_slab' if kernel == 'adam' else kernel}_kernel:"
-    for line in open(path):
-        if line.startswith(key):
-            return float(line.split(":")[1])
-    return None
+    return json.load(open(path)).get(workload, {}).get("bytes_per_launch", {}).get(kernel)
 
 
 def metric_name(workload: str) -> str:
@@ -86,6 +83,8 @@ def parse():
                          "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
+    ap.add_argument("--clocks-csv", default=None,
+                    help="keep the nvidia-smi clock samples in this file ({rank} is replaced; default: a temp file)")
     return ap.parse_args()
 
 
@@ -118,14 +117,19 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, path: str = None):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        self.path = path
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            if self.path is None:
+                import tempfile
+                fd, self.path = tempfile.mkstemp(prefix=f"clocks_gpu{self.gpu}_", suffix=".csv")
+                os.close(fd)
+            else:
+                os.makedirs(os.path.dirname(os.path.abspath(self.path)), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
@@ -265,63 +269,257 @@ def l1_dssim_timing(color, target, dev, iters: int = 20):
 
 
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_baseline(wl_name: str, seconds: float):
-    """The CPU oracle on a bounded sample of the workload, scaled to full steps/s."""
+# fp32 operations one contributing (pixel, splat) pair costs in the compositing
+# kernels (fused multiply-adds count 2; the ex2 / reciprocal special functions
+# are not counted): forward 21 (offset, quadratic form, falloff argument,
+# alpha, weight, colour and alpha sums, transmittance), backward 35 (the same
+# recompute, transmittance recovery, the B recursion, colour sums, dL/dalpha
+# and the five moments).
+FWD_FLOPS_PER_PAIR = 21
+BWD_FLOPS_PER_PAIR = 35
+
+
+def oracle_train_run(wl_name: str = "tiny-3k", steps: int = 50):
+    """The reference's training step restated on the CPU (the oracle), run in
+    full for ``steps`` steps: cull -> dense rasterizer forward with the L1
+    loss gradient in the same pass (fp32 torch-CPU on every host thread) ->
+    the trainer's 1e-5 regulariser -> the fused-Adam restatement (C) per group
+    with the reference's clamps and learning-rate schedule -> quaternion
+    renormalisation.  Targets are rendered from the second seeded set, as the
+    GPU runner's are."""
     from mlx_gsplat_b200 import synthetic
     from oracle import adam as oadam
+    from oracle import densify as odens
     from oracle import rendering as orend
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     wl = synthetic.WORKLOADS[wl_name]
     g = synthetic.make_gaussians(wl, seed=0)
-    views, K = synthetic.make_cameras(wl, seed=2, num_views=8)
-    vm = views[0]
-    ids = orend.cull(g["means"], g["opacities"], vm, K, wl.width, wl.height).astype(np.int64)
-    cols = np.concatenate([g["sh0"], g["shN"][:, :9]], 1)
-    rng = np.random.default_rng(0)
-    n_pix = 8
-    t_pix, done_pix = 0.0, 0
+    views, K = synthetic.make_cameras(wl, seed=2)
+    g2 = synthetic.make_gaussians(wl, seed=1)
+    cols2 = np.concatenate([g2["sh0"], g2["shN"]], 1)[:, :12 if wl.sh_degree > 0 else 3]
+    targets = []
+    for vm in views:
+        i2 = orend.cull(g2["means"], g2["opacities"], vm, K, wl.width, wl.height).astype(np.int64)
+        C, _ = orend.rasterize_dense(g2["means"][i2], g2["quats"][i2], g2["scales"][i2], g2["opacities"][i2],
+                                     cols2[i2], vm, K, wl.width, wl.height, wl.width, wl.height, dtype=torch.float32)
+        targets.append(C)
+    P = {"means": g["means"].copy(), "quats": g["quats"].copy(), "scales": g["scales"].copy(),
+         "opacities": g["opacities"].copy(), "colors": np.concatenate([g["sh0"], g["shN"]], 1).astype(np.float32)}
+    M = {k: np.zeros_like(v) for k, v in P.items()}
+    Vv = {k: np.zeros_like(v) for k, v in P.items()}
+    n = P["means"].shape[0]
+    table = np.arange(n, dtype=np.int32)
+    ncol = 12 if wl.sh_degree > 0 else 3
+    reg = np.float32(1e-5)
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds * 0.7:
-        pix = np.sort(rng.choice(wl.pixels, n_pix, replace=False))
-        dC = rng.uniform(-1, 1, (n_pix, 3)) / wl.pixels
+    for step in range(1, steps + 1):
+        vi = (step - 1) % len(views)
+        ids = orend.cull(P["means"], P["opacities"], views[vi], K, wl.width, wl.height).astype(np.int64)
+        _, _, gr = orend.rasterize_dense_vjp(P["means"][ids], P["quats"][ids], P["scales"][ids],
+                                             P["opacities"][ids], P["colors"][ids][:, :ncol], views[vi], K,
+                                             wl.width, wl.height, wl.width, wl.height, dL_dC=None,
+                                             l1_target=targets[vi], dtype=torch.float32, chunk=256)
+        grads = {}
+        for k in ("means", "quats", "scales", "opacities"):
+            gk = np.full_like(P[k], reg)
+            gk[ids] += gr[k].astype(np.float32)
+            grads[k] = gk
+        gc = np.zeros_like(P["colors"])
+        gc[ids, :ncol] = gr["colors"].astype(np.float32) + reg
+        grads["colors"] = gc
+        lr = 1e-3 * (0.01 ** (step / steps))
+        for k in P:
+            lo, hi = oadam.group_clamp(k if k != "colors" else "sh0")
+            oadam.fused_adam_a1(P[k], grads[k], M[k], Vv[k], table, lr=np.float32(lr), beta1=0.9, beta2=0.999,
+                                eps=1e-15, weight_decay=0.0, step=step, a_min=lo, a_max=hi)
+        P["quats"] = odens.quat_renorm(P["quats"])
+    dt = time.perf_counter() - t0
+    return {"workload": wl_name, "steps": steps, "seconds": dt, "value": steps / dt, "unit": "train steps/s",
+            "mpix_per_s": steps * wl.pixels / dt / 1e6, "cores": threads, "kind": "port",
+            "sample": (f"{steps} full training steps of {wl_name} ({n} Gaussians, {len(views)} views at "
+                       f"{wl.width}x{wl.height}, L1, fused Adam) through the CPU oracle, fp32 torch-CPU on "
+                       f"{threads} threads")}
+
+
+class OracleSampler:
+    """A bounded sample of one training step of a full-size workload through
+    the CPU oracle, scaled to the full step.  The dense rasterizer's cost is
+    fitted as ``a + b * pixels`` from calls on two pixel-subset sizes over
+    every Gaussian the view sees (``a`` is the per-view projection of all of
+    them, ``b`` the dense compositing per pixel); Adam is timed on a row slice
+    and scaled by rows."""
+
+    def __init__(self, wl_name: str, pix_small: int = 8, pix_large: int = 40, adam_rows: int = 100_000):
+        from mlx_gsplat_b200 import synthetic
+        from oracle import rendering as orend
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.wl = wl = synthetic.WORKLOADS[wl_name]
+        self.wl_name = wl_name
+        g = synthetic.make_gaussians(wl, seed=0)
+        views, self.K = synthetic.make_cameras(wl, seed=2, num_views=8)
+        self.vm = views[0]
+        ids = orend.cull(g["means"], g["opacities"], self.vm, self.K, wl.width, wl.height).astype(np.int64)
+        cols = np.concatenate([g["sh0"], g["shN"]], 1)[:, :12 if wl.sh_degree > 0 else 3]
+        self.rows = {k: np.ascontiguousarray(g[k][ids]) for k in ("means", "quats", "scales", "opacities")}
+        self.rows["colors"] = np.ascontiguousarray(cols[ids])
+        self.V = len(ids)
+        self.ncols = sum(v.shape[1] for k, v in g.items())
+        self.n_pix = (pix_small, pix_large)
+        self.rng = np.random.default_rng(0)
+        self.adam_rows = adam_rows
+        r = self.rng
+        self.adam = [r.normal(0, 1, (adam_rows, self.ncols)).astype(np.float32),
+                     r.normal(0, 0.1, (adam_rows, self.ncols)).astype(np.float32),
+                     np.zeros((adam_rows, self.ncols), np.float32), np.zeros((adam_rows, self.ncols), np.float32),
+                     np.arange(adam_rows, dtype=np.int32)]
+        self.t_small, self.t_large, self.t_adam, self.samples = 0.0, 0.0, 0.0, 0
+        self.step = 0
+
+    def _raster(self, n_pix: int) -> float:
+        from oracle import rendering as orend
+        wl = self.wl
+        pix = np.sort(self.rng.choice(wl.pixels, n_pix, replace=False))
+        dC = self.rng.uniform(-1, 1, (n_pix, 3)) / wl.pixels
         s = time.perf_counter()
-        orend.rasterize_dense_vjp(g["means"][ids], g["quats"][ids], g["scales"][ids], g["opacities"][ids],
-                                  cols[ids], vm, K, wl.width, wl.height, wl.width, wl.height, dL_dC=dC,
-                                  dtype=torch.float32, chunk=8, pixel_ids=pix)
-        t_pix += time.perf_counter() - s
-        done_pix += n_pix
-    # Adam over a slice of rows (the C restatement, one thread)
-    rows = 200_000
-    th = rng.normal(0, 1, (rows, 59)).astype(np.float32)
-    gg = rng.normal(0, 0.1, (rows, 59)).astype(np.float32)
-    mm = np.zeros_like(th)
-    vv = np.zeros_like(th)
-    idx = np.arange(rows, dtype=np.int32)
-    s = time.perf_counter()
-    oadam.fused_adam_a1(th, gg, mm, vv, idx, 1e-3, 0.9, 0.999, 1e-15, 0.0, 1, -1e10, 1e10)
-    t_adam = (time.perf_counter() - s) * wl.num_gaussians / rows
-    t_step = t_pix / done_pix * wl.pixels + t_adam
-    return {"value": 1.0 / t_step, "unit": "train steps/s", "cores": threads, "kind": "port",
-            "sample": (f"dense oracle fwd+bwd on {done_pix} random pixels x {len(ids)} visible Gaussians "
-                       f"(fp32 torch-CPU, {threads} threads) scaled to {wl.pixels} px, plus the C Adam "
-                       f"restatement on {rows} rows scaled to {wl.num_gaussians}; seconds/step "
-                       f"{t_step:.1f}")}
+        r = self.rows
+        orend.rasterize_dense_vjp(r["means"], r["quats"], r["scales"], r["opacities"], r["colors"], self.vm, self.K,
+                                  wl.width, wl.height, wl.width, wl.height, dL_dC=dC, dtype=torch.float32, chunk=8,
+                                  pixel_ids=pix)
+        return time.perf_counter() - s
+
+    def sample_step(self) -> float:
+        """One sample step; returns its seconds."""
+        from oracle import adam as oadam
+        s0 = time.perf_counter()
+        self.t_small += self._raster(self.n_pix[0])
+        self.t_large += self._raster(self.n_pix[1])
+        self.step += 1
+        th, g, m, v, idx = self.adam
+        s = time.perf_counter()
+        oadam.fused_adam_a1(th, g, m, v, idx, 1e-3, 0.9, 0.999, 1e-15, 0.0, self.step, -1e10, 1e10)
+        self.t_adam += time.perf_counter() - s
+        self.samples += 1
+        return time.perf_counter() - s0
+
+    def full_step_seconds(self) -> float:
+        n = max(self.samples, 1)
+        ps, pl = self.n_pix
+        b = max((self.t_large - self.t_small) / n / (pl - ps), 0.0)
+        a = max(self.t_small / n - b * ps, 0.0)
+        return a + b * self.wl.pixels + self.t_adam / n * self.wl.num_gaussians / self.adam_rows
+
+    def describe(self) -> str:
+        ps, pl = self.n_pix
+        return (f"{self.samples} sample steps of {self.wl_name}: the dense oracle fwd+bwd over all {self.V} visible "
+                f"Gaussians of one view at {ps} and at {pl} random pixels (fp32 torch-CPU, {self.threads} threads), "
+                f"cost fitted as projection + per-pixel compositing and scaled to {self.wl.pixels} pixels, plus the "
+                f"C fused-Adam restatement on {self.adam_rows} rows x {self.ncols} columns scaled to "
+                f"{self.wl.num_gaussians} rows; extrapolated seconds per full step "
+                f"{self.full_step_seconds():.1f}")
+
+
+def cpu_baseline(wl_name: str, seconds: float):
+    """The CPU oracle on the host cores: a bounded sample of the benchmark
+    workload scaled to full steps/s (``value``), and the reference's own
+    CPU-sized workload (3,000 Gaussians at 120x90, 50 steps) measured in full
+    (``config0_measured``)."""
+    sampler = OracleSampler(wl_name)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or sampler.samples < 2:
+        sampler.sample_step()
+    t = sampler.full_step_seconds()
+    return {"value": 1.0 / t, "unit": "train steps/s", "cores": sampler.threads, "kind": "port",
+            "basis": "extrapolated from a bounded sample", "sample": sampler.describe(),
+            "config0_measured": oracle_train_run("tiny-3k", 50)}
+
+
+def workload_config(args, world: int) -> dict:
+    """The ``config`` of the JSON line (both arms print the same one)."""
+    from mlx_gsplat_b200 import synthetic
+    wl = synthetic.WORKLOADS[args.workload]
+    return {"workload": args.workload, "gaussians": args.gaussians or wl.num_gaussians,
+            "image": f"{wl.width}x{wl.height}", "sh_degree": wl.sh_degree, "views": args.views or wl.num_views,
+            "views_per_gpu_per_step": 1, "parallelism": f"views-dp{world}", "loss": "l1",
+            "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v slabs (0.72 GB) and the seen "
+                  "gradient rows every step"}
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the reference's training step restated on the CPU
+    (the oracle; MLX itself cannot be installed here) on the host cores.
+    Each step is a bounded sample of the workload's step (see OracleSampler);
+    ``ms_per_step`` is the measured time of one sample step, ``value`` the
+    full-step rate the samples extrapolate to."""
     if rank != 0:
         return
-    base = cpu_baseline(args.workload, max(5.0, min(args.cpu_seconds, 60.0)))
-    line = {"metric": metric_name(args.workload),
-            "value": base["value"], "unit": "train steps/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": args.workload},
-            "cpu_baseline": base,
-            "e2e": {"value": base["value"], "unit": "train steps/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+    sampler = OracleSampler(args.workload)
+    for _ in range(args.warmup):
+        sampler.sample_step()
+    sampler.t_small = sampler.t_large = sampler.t_adam = 0.0
+    sampler.samples = 0
+    t_samples = 0.0
+    for _ in range(args.steps):
+        t_samples += sampler.sample_step()
+    full = sampler.full_step_seconds()
+    value = 1.0 / full
+    base = {"value": value, "unit": "train steps/s", "cores": sampler.threads, "kind": "port",
+            "basis": "extrapolated from bounded sample steps", "sample": sampler.describe()}
+    if not args.no_cpu_baseline:
+        base["config0_measured"] = oracle_train_run("tiny-3k", 50)
+    line = {"metric": metric_name(args.workload), "value": value, "unit": "train steps/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_samples / args.steps,
+            "ms_per_full_step_extrapolated": 1000.0 * full,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": workload_config(args, world), "cpu_baseline": base,
+            "e2e": {"value": value, "unit": "train steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def fp32_peak(dev) -> dict:
+    """The GPU's fp32 fused multiply-add throughput (``gs_fp32_peak_probe``, paired
+    and scalar forms, best of 5 launches each, CUDA events)."""
+    import ctypes
+    from mlx_gsplat_b200 import _lib
+    lib = _lib.load()
+    blocks, iters = 148 * 16, 4096
+    out = torch.empty(blocks * 256, dtype=torch.float32, device=dev)
+    res = {}
+    for paired in (1, 0):
+        fl = ctypes.c_double()
+        best = None
+        for _ in range(6):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            _lib.check(lib.gs_fp32_peak_probe(out.data_ptr(), out.numel(), blocks, iters, paired, ctypes.byref(fl),
+                                              _lib.stream_ptr(dev)), "fp32 peak probe")
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        res["paired" if paired else "scalar"] = fl.value / (best * 1e-3) / 1e12
+    return {"tflops": max(res.values()), "by_form_tflops": res,
+            "how": "gs_fp32_peak_probe: 16 independent FMA chains per thread, 148x16 CTAs of 256 threads"}
+
+
+def pair_counts(frames, dev) -> float:
+    """Mean number of contributing (pixel, splat) pairs per view (the work both
+    compositing kernels do) over the given step frames (gs_render_pair_count
+    on each frame's staged splats and tile lists)."""
+    from mlx_gsplat_b200 import _lib
+    lib = _lib.load()
+    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    n = 0
+    for f in frames:
+        if f.V > 0:
+            _lib.check(lib.gs_render_pair_count(f.ranges.data_ptr(), _lib.ptr(f.tile_order), f.entry_vals.data_ptr(),
+                                                f.splats.data_ptr(), f.V, f.cam, f.rs, cnt.data_ptr(),
+                                                _lib.stream_ptr(dev)), "pair count")
+        n += 1
+    torch.cuda.synchronize(dev)
+    return float(cnt.item()) / max(n, 1)
 
 
 # ----------------------------------------------------------------------------- main
@@ -357,7 +555,7 @@ def main():
     def view_of(step):
         return (rank + world * step) % nv
 
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, args.clocks_csv.format(rank=local) if args.clocks_csv else None)
     clocks.start()
     step = 0
     for _ in range(args.warmup):
@@ -376,12 +574,14 @@ def main():
     e1 = torch.cuda.Event(enable_timing=True)
     t_start = time.time()
     e0.record()
+    frames = []
     for _ in range(args.steps):
         step += 1
         tm = StepTimer()
         f = runner.train_step(view_of(step), step, target=targets_dev[view_of(step)], timer=tm)
         timers.append(tm)
         stats.append((f.V, f.K))
+        frames = (frames + [f])[-4:]  # the last steps' frames, for the pair count after the timed region
     e1.record()
     torch.cuda.synchronize(dev)
     t_end = time.time()
@@ -421,6 +621,19 @@ def main():
     if "adam" in per:
         roof["adam"] = {"achieved": per["adam"]["gbs"], "frac": per["adam"]["gbs"] / pk["hbm_gbs"],
                         "traffic": measured_traffic("adam", args.workload) if full_size else None}
+    # compute roofline of the compositing kernels: contributing (pixel, splat) pairs
+    # times the fp32 operations per pair, against the measured fp32 throughput
+    pairs = pair_counts(frames, dev)
+    fp = fp32_peak(dev)
+    comp = {"pairs_per_view": pairs, "peak_tflops": fp["tflops"], "peak_by_form_tflops": fp["by_form_tflops"],
+            "peak_how": fp["how"], "flops_per_pair": {"render_fwd": FWD_FLOPS_PER_PAIR,
+                                                      "render_bwd": BWD_FLOPS_PER_PAIR}}
+    for k, fl in (("render_fwd", FWD_FLOPS_PER_PAIR), ("render_bwd", BWD_FLOPS_PER_PAIR)):
+        if k in per:
+            tf = pairs * fl / (per[k]["ms"] * 1e-3) / 1e12
+            comp[k] = {"ms": per[k]["ms"], "gpairs_per_s": pairs / (per[k]["ms"] * 1e-3) / 1e9,
+                       "achieved_tflops": tf, "frac": tf / fp["tflops"]}
+    roof["fp32"] = comp
 
     # ---- end to end through the public API (host target in, loss out)
     e2e = None
@@ -504,15 +717,11 @@ def main():
                 "unit": "train steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic",
-                "config": {"workload": args.workload, "gaussians": wl.num_gaussians, "image": f"{wl.width}x{wl.height}",
-                           "sh_degree": wl.sh_degree, "views": nv, "views_per_gpu_per_step": 1,
-                           "parallelism": f"views-dp{world}", "loss": "l1",
-                           "grad_reduce": ("nvlink multicast sum fused into the sharded adam" if runner.sharded else
-                                           ("nvlink multicast row sum" if runner.fused_reduce is not None else
-                                            ("nccl all-reduce" if world > 1 else "none"))),
-                           "grad_row_floats": runner.g_stride,
-                           "l2": "working set > L2: Adam streams the 1M x 60-float theta/m/v slabs (0.72 GB) and "
-                                 "the seen gradient rows every step"},
+                "config": workload_config(args, world),
+                "grad_reduce": ("nvlink multicast sum fused into the sharded adam" if runner.sharded else
+                                ("nvlink multicast row sum" if runner.fused_reduce is not None else
+                                 ("nccl all-reduce" if world > 1 else "none"))),
+                "grad_row_floats": runner.g_stride,
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,
                 "adam_gbs": per.get("adam", {}).get("gbs"),
                 "kernels_ms": {k: round(v["ms"], 4) for k, v in per.items()},

@@ -226,7 +226,10 @@ int gs_cull(const gs_gaussians* g, int64_t n, const gs_camera* cam, float near_p
  *    GS_ERR_CAPACITY before any work.
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *    before any stream capture.  The address is kept with the id of the
+ *    context it was taken in: after a cudaDeviceReset the next call (which
+ *    then runs in a new context) looks it up again, so that call too should
+ *    come before any stream capture.
  *  - All calls share the one array and each call overwrites it: calls that can
  *    overlap on the GPU (other streams, other host threads on the same device)
  *    race; serialise them. */
@@ -317,6 +320,27 @@ int gs_render_forward(const gs_tile_range* ranges, const int32_t* tile_order, co
                       float* final_T, int32_t* n_contrib, int loss_mode, const void* target, float* loss_partials,
                       gs_stream_t stream);
 
+/* Diagnostic (no reference counterpart): the number of (pixel, splat) pairs
+ * that take part in the compositing of one view — alpha >= alpha_cutoff
+ * while the pixel's transmittance is >= transmittance_min, the pairs both
+ * compositing kernels evaluate — added to ``*pairs`` (device uint64).  Runs
+ * the forward's arithmetic without writing an image; the arguments mean what
+ * they mean for gs_render_forward.  Used to state the compositing kernels'
+ * work in pairs per second. */
+int gs_render_pair_count(const gs_tile_range* ranges, const int32_t* tile_order, const uint32_t* entry_vals,
+                         const float* splats, int64_t num_visible, const gs_camera* cam,
+                         const gs_raster_settings* rs, unsigned long long* pairs, gs_stream_t stream);
+
+/* Diagnostic (no reference counterpart): a kernel of ``blocks`` x 256 threads,
+ * each running 16 independent fused multiply-add chains for ``iters``
+ * iterations — as sm_100 paired (two-lane) instructions when ``paired``, else
+ * scalar — writing one float per thread to ``out``.  ``*flops_per_launch``
+ * receives the floating-point operations the launch performs.  Timed by the
+ * caller, it measures the GPU's fp32 throughput: the denominator of the
+ * compositing kernels' compute roofline. */
+int gs_fp32_peak_probe(float* out, int64_t out_len, int blocks, int iters, int paired, double* flops_per_launch,
+                       gs_stream_t stream);
+
 /* Back-to-front gradient of the compositing: recomputes transmittance from the
  * saved final value and accumulates per visible Gaussian, with warp-reduced
  * atomics, the 12-float record {du, dv, dconic_a, dconic_bc}, {dconic_d,
@@ -403,9 +427,11 @@ int gs_group_barrier(uint32_t* const* peer_pads, int32_t rank, int32_t world, in
  * across all GPUs' copies and stored back to all of them.  Each GPU calls it
  * on a disjoint range between two gs_group_barrier calls (after every GPU
  * wrote its rows; before anyone reads the sums); together the calls leave the
- * same sums in every copy. */
+ * same sums in every copy.  ``error_flag`` (device int32, may be NULL): the
+ * flag the group barriers set when a wait gives up; when it is non-zero the
+ * call reads and writes nothing, so a partial sum is never broadcast. */
 int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, int64_t num_rows, int64_t stride,
-                          gs_stream_t stream);
+                          const int32_t* error_flag, gs_stream_t stream);
 
 /* The slab Adam of one GPU of a views-data-parallel group, fused with the
  * group's gradient sum and parameter broadcast (no reference counterpart: the
@@ -420,13 +446,15 @@ int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, int64_t num_
  * owner until the caller gathers them).  Fused semantics with the approximate
  * step; ``grad_scale`` and ``grad_bias_host`` as in gs_fused_adam_slab.  Call
  * it between two gs_group_barrier calls: after every GPU wrote its gradient
- * rows, before any GPU reads parameters again. */
+ * rows, before any GPU reads parameters again.  ``error_flag`` (device int32,
+ * may be NULL): the flag those barriers set when a wait gives up; when it is
+ * non-zero the update is skipped entirely (no partial sums are applied). */
 int gs_fused_adam_slab_sharded(float* theta, float* theta_multicast, const float* g_multicast, float* m, float* v,
                                const int32_t* indices, int64_t num_active, int ncols, int64_t stride,
                                int64_t g_stride, const float* col_lo, const float* col_hi, int quat_col, double lr,
                                double beta1, double beta2, float eps, float weight_decay, int step, float grad_scale,
                                const float* grad_bias_host, int g_cols, int count_col, const float* count_coef_host,
-                               int rank, int world, int hot_cols, gs_stream_t stream);
+                               int rank, int world, int hot_cols, const int32_t* error_flag, gs_stream_t stream);
 
 /* ------------------------------------------------------------------ pool / densify */
 
@@ -483,6 +511,11 @@ int gs_fill_rows(float* dst, int64_t n_rows, int64_t stride, const float* patter
 /* Sets column ``col`` of rows [0, n_rows) to ``value`` (the periodic opacity
  * reset, mlx_gsplat/trainer.py:416-419). */
 int gs_fill_column(float* dst, int64_t n_rows, int64_t stride, int col, float value, gs_stream_t stream);
+
+/* mask[slots[j]] = value for j < n, skipping slots outside [0, mask_len): the
+ * allocator's active-slot mask updates of allocator.py:209-225 (pruned slots
+ * cleared, child slots set). */
+int gs_mark_slots(int8_t* mask, int64_t mask_len, const int32_t* slots, int64_t n, int value, gs_stream_t stream);
 
 #ifdef __cplusplus
 }

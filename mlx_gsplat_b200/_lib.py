@@ -92,6 +92,10 @@ _SIGS = {
     "gs_render_forward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
                                          ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, c_vp, ctypes.c_int,
                                          c_vp, c_vp, c_vp]),
+    "gs_render_pair_count": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
+                                             ctypes.POINTER(GsRasterSettings), c_vp, c_vp]),
+    "gs_fp32_peak_probe": (ctypes.c_int, [c_vp, i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_double), c_vp]),
     "gs_render_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
                                           ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, ctypes.c_int, c_vp,
                                           c_vp, c_vp, c_vp, c_vp]),
@@ -103,12 +107,12 @@ _SIGS = {
                                         c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "gs_resize_bilinear": (ctypes.c_int, [c_vp, ctypes.c_int, i32, i32, i32, c_vp, i32, i32, c_vp]),
     "gs_group_barrier": (ctypes.c_int, [c_vp, i32, i32, i32, ctypes.c_uint32, c_vp, i64, c_vp]),
-    "gs_rows_sum_multicast": (ctypes.c_int, [c_vp, i64, i64, i64, c_vp]),
+    "gs_rows_sum_multicast": (ctypes.c_int, [c_vp, i64, i64, i64, c_vp, c_vp]),
     "gs_fused_adam_slab_sharded": (ctypes.c_int, [c_vp] * 6 + [i64, ctypes.c_int, i64, i64, c_float_p, c_float_p,
                                                                ctypes.c_int] + [ctypes.c_double] * 3 +
                                    [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_float, c_float_p,
                                     ctypes.c_int, ctypes.c_int, c_float_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                    c_vp]),
+                                    c_vp, c_vp]),
     "gs_compact_flags": (ctypes.c_int, [c_vp, i64, ctypes.c_uint8, ctypes.c_uint8, c_vp, c_vp, c_vp, c_vp,
                                         ctypes.c_size_t, c_vp]),
     "gs_densify_masks": (ctypes.c_int, [ctypes.POINTER(GsGaussians), c_vp, c_vp, i64] + [ctypes.c_float] * 5 +
@@ -119,6 +123,7 @@ _SIGS = {
     "gs_free_pop_reversed": (ctypes.c_int, [c_vp, i64, i64, c_vp, c_vp]),
     "gs_fill_rows": (ctypes.c_int, [c_vp, i64, i64, c_float_p, c_vp]),
     "gs_fill_column": (ctypes.c_int, [c_vp, i64, i64, ctypes.c_int, ctypes.c_float, c_vp]),
+    "gs_mark_slots": (ctypes.c_int, [c_vp, i64, c_vp, i64, ctypes.c_int, c_vp]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None

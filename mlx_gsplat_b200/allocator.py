@@ -122,6 +122,7 @@ class PointerStableChunkedAllocator:
         self.cached_indices_addr = None
         self.grad2d = torch.zeros(self.max_gaussians, dtype=torch.float32, device=self.device)
         self.count = torch.zeros(self.max_gaussians, dtype=torch.float32, device=self.device)
+        self._ws = None  # density-step buffers, allocated at the first density step
 
     # ------------------------------------------------------------------ properties / metrics
     @property
@@ -188,15 +189,36 @@ class PointerStableChunkedAllocator:
     # ------------------------------------------------------------------ split / prune
     FLAG_PRUNE, FLAG_REFINE, FLAG_SPLIT = 1, 2, 4
 
-    def _compact(self, flags: torch.Tensor, n: int, mask: int, value: int, gather: Optional[torch.Tensor]):
+    def workspace(self) -> Dict[str, object]:
+        """Buffers of the density step, sized for the whole pool and allocated
+        once (the first density step): the row flags, the compacted slot and row
+        lists, two indirection-table buffers that alternate (the new table is
+        compacted into the one the current table does not use, and the child
+        slots are popped straight behind its kept entries), the compaction
+        scratch and the counts with their pinned host copy."""
+        if self._ws is None:
+            lib = _lib.lib()
+            M = self.max_gaussians
+            dev = self.device
+
+            def i32(n):
+                return torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+
+            self._ws = {"flags": torch.empty(max(M, 1), dtype=torch.uint8, device=dev),
+                        "prune": i32(M), "split": i32(M), "refine": i32(M), "tables": (i32(M), i32(M)),
+                        "counts": i32(4), "counts_host": torch.empty(4, dtype=torch.int32, pin_memory=True),
+                        "scratch": torch.empty(max(lib.gs_cull_scratch_bytes(M), 16), dtype=torch.uint8,
+                                               device=dev)}
+        return self._ws
+
+    def _compact(self, flags: torch.Tensor, n: int, mask: int, value: int, gather: Optional[torch.Tensor],
+                 out: torch.Tensor, count_at: int) -> None:
         lib = _lib.lib()
-        out = torch.empty(max(n, 1), dtype=torch.int32, device=self.device)
-        cnt = torch.empty(1, dtype=torch.int32, device=self.device)
-        sb = torch.empty(max(lib.gs_cull_scratch_bytes(n), 16), dtype=torch.uint8, device=self.device)
+        ws = self.workspace()
+        sb = ws["scratch"]
         _lib.check(lib.gs_compact_flags(flags.data_ptr(), n, mask, value, None if gather is None else gather.data_ptr(),
-                                        out.data_ptr(), cnt.data_ptr(), sb.data_ptr(), sb.numel(),
+                                        out.data_ptr(), ws["counts"][count_at:].data_ptr(), sb.data_ptr(), sb.numel(),
                                         _lib.stream_ptr(self.device)), "gs_compact_flags")
-        return out, cnt
 
     def apply_flags(self, flags: torch.Tensor, make_children) -> Tuple[int, int]:
         """The realloc-free density step of allocator.py:185-292 driven by
@@ -204,34 +226,44 @@ class PointerStableChunkedAllocator:
         refine_rows, n)`` returns the child rows ``(child1, child2)`` as
         ``[n, stride]`` tensors.  Slot order is the reference's: pruned slots are
         pushed in ascending logical order and children pop from the same end, so
-        a child can land in a just-pruned slot and is then reset by the prune."""
+        a child can land in a just-pruned slot and is then reset by the prune.
+        Every buffer comes from ``workspace()``; the three counts come back to
+        the host in one read."""
         start = time.perf_counter()
         lib = _lib.lib()
         st = _lib.stream_ptr(self.device)
         L = self.layout
+        ws = self.workspace()
         n = self.num_active
         table = self.indirection_table
+        t0, t1 = ws["tables"]
+        dst = t1 if table.data_ptr() == t0.data_ptr() else t0  # the buffer the current table does not use
         P, R = self.FLAG_PRUNE, self.FLAG_REFINE
-        prune_slots, c_p = self._compact(flags, n, P, P, table)
-        split_slots, c_s = self._compact(flags, n, R, R, table)
-        refine_rows, _ = self._compact(flags, n, R, R, None)
-        keep_slots, c_k = self._compact(flags, n, P, 0, table)
-        n_p, n_s, n_keep = [int(x) for x in torch.cat([c_p, c_s, c_k]).tolist()]
+        prune_slots, split_slots, refine_rows = ws["prune"], ws["split"], ws["refine"]
+        self._compact(flags, n, P, P, table, prune_slots, 0)
+        self._compact(flags, n, R, R, table, split_slots, 1)
+        self._compact(flags, n, R, R, None, refine_rows, 3)
+        self._compact(flags, n, P, 0, table, dst, 2)  # kept entries, in order, at the head of the new table
+        host = ws["counts_host"]
+        host.copy_(ws["counts"], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        n_p, n_s, n_keep = [int(x) for x in host[:3].tolist()]
         # 1. prune: slots go back on the free list (allocator.py:209-211)
         if n_p:
             self.free_stack[self.free_top:self.free_top + n_p].copy_(prune_slots[:n_p])
-            self.active_mask[prune_slots[:n_p].long()] = 0
+            _lib.check(lib.gs_mark_slots(self.active_mask.data_ptr(), self.max_gaussians, prune_slots.data_ptr(), n_p,
+                                         0, st), "active mask")
         self.free_top += n_p
-        # 2. children pop from the same end (allocator.py:213-220)
+        # 2. children pop from the same end (allocator.py:213-220), straight behind the kept entries
         if self.free_top < n_s:
             raise MemoryError(f"pool capacity reached: {self.free_top} free slots, {n_s} children requested")
-        children = torch.empty(max(n_s, 1), dtype=torch.int32, device=self.device)
+        children = dst[n_keep:n_keep + n_s]
         _lib.check(lib.gs_free_pop_reversed(self.free_stack.data_ptr(), self.free_top, n_s, children.data_ptr(), st),
                    "free list pop")
         self.free_top -= n_s
-        children = children[:n_s]
         if n_s:
-            self.active_mask[children.long()] = 1
+            _lib.check(lib.gs_mark_slots(self.active_mask.data_ptr(), self.max_gaussians, children.data_ptr(), n_s, 1,
+                                         st), "active mask")
         # 3. rows: child 1 -> parent slot, child 2 -> popped slot, then the prune reset (allocator.py:229-273)
         if n_s:
             child1, child2 = make_children(split_slots[:n_s], refine_rows[:n_s], n_s)
@@ -246,7 +278,7 @@ class PointerStableChunkedAllocator:
                                               _lib.fptr(L.reset_row()), self.grad2d.data_ptr(),
                                               self.count.data_ptr(), st), "prune reset")
         # 4. indirection table: kept entries in order, then the children (allocator.py:275-281)
-        self.indirection_table = torch.cat([keep_slots[:n_keep], children]).contiguous()
+        self.indirection_table = dst[:n_keep + n_s]
         self.allocation_latency_ms = (time.perf_counter() - start) * 1000.0
         self.update_metrics()
         self.update_cached_pointers()
@@ -259,7 +291,9 @@ class PointerStableChunkedAllocator:
                              device=self.device).to(torch.uint8)
         sm = torch.as_tensor(np.asarray(split_mask) if not isinstance(split_mask, torch.Tensor) else split_mask,
                              device=self.device).to(torch.uint8)
-        flags = (pm * self.FLAG_PRUNE + sm * self.FLAG_REFINE).to(torch.uint8).contiguous()
+        n = self.num_active
+        flags = self.workspace()["flags"][:max(n, 1)]
+        flags[:n].copy_(pm * self.FLAG_PRUNE + sm * self.FLAG_REFINE)
         L = self.layout
 
         def make_children(split_slots, refine_rows, n):

@@ -306,7 +306,11 @@ __global__ void __launch_bounds__(256, 4) adam_sharded_kernel(
     float4* __restrict__ theta, float4* __restrict__ theta_mc, const float4* __restrict__ g_mc,
     float4* __restrict__ m, float4* __restrict__ v, const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
     int lane_shift, int g_chunks, int ncols, int quat_chunk, int64_t half, int g_cols, int count_col, int rank,
-    int world, int hot_chunks, AdamScalars s, SlabCols cols) {
+    int world, int hot_chunks, const int32_t* __restrict__ error_flag, AdamScalars s, SlabCols cols) {
+    // a group barrier before this launch gave up waiting for a peer: the
+    // summed rows may be partial, so nothing is read or written (uniform
+    // over the grid: the flag is written only by kernels ordered before this one)
+    if (error_flag && *reinterpret_cast<const volatile int32_t*>(error_flag) != 0) return;
     __shared__ ColsSmem cs;
     if (threadIdx.x < kMaxSlabCols) {
         cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
@@ -510,7 +514,7 @@ extern "C" int gs_fused_adam_slab_sharded(float* theta, float* theta_multicast, 
                                           float weight_decay, int step, float grad_scale,
                                           const float* grad_bias_host, int g_cols, int count_col,
                                           const float* count_coef_host, int rank, int world, int hot_cols,
-                                          gs_stream_t stream) {
+                                          const int32_t* error_flag, gs_stream_t stream) {
     GS_REQUIRE(world >= 1 && rank >= 0 && rank < world, "adam_sharded: bad rank/world");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_sharded: ncols must be in [1, %d]", kMaxSlabCols);
     GS_REQUIRE(stride % 4 == 0 && g_stride % 4 == 0 && stride >= ncols && stride <= 128 && g_stride >= g_cols,
@@ -551,7 +555,7 @@ extern "C" int gs_fused_adam_slab_sharded(float* theta, float* theta_multicast, 
         reinterpret_cast<float4*>(theta), reinterpret_cast<float4*>(theta_multicast),
         reinterpret_cast<const float4*>(g_multicast), reinterpret_cast<float4*>(m), reinterpret_cast<float4*>(v),
         indices, num_active, chunks, shift, (int)(g_stride / 4), ncols, quat_col < 0 ? -1 : quat_col / 4, half,
-        g_cols, g_cols < ncols ? count_col : 0, rank, world, hot_cols / 4, s, cols);
+        g_cols, g_cols < ncols ? count_col : 0, rank, world, hot_cols / 4, error_flag, s, cols);
     return check_launch("adam_sharded_kernel");
 }
 

@@ -5,6 +5,8 @@
 // Pass 2: exclusive scan of the chunk counts.
 // Pass 3: each chunk writes its surviving ids in ascending order.
 // Reads 16 bytes per id (means + opacity), writes 4 bytes per survivor.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -215,9 +217,13 @@ int compact_flags(const uint8_t* flags, int64_t n, uint8_t mask, uint8_t value, 
 // in the file-scope device array below instead of a caller buffer.  It is
 // sized for kNoAllocMaxRows active ids; every device that loads the library
 // holds it until the process exits.  Host code never dereferences the array's
-// name: the device address is taken once per device with
-// cudaGetSymbolAddress.  Each call writes every scratch word before reading
-// it, so nothing has to be cleared between calls.
+// name: the device address is taken with cudaGetSymbolAddress, with the
+// device current, the first time a device's context calls in, and kept per
+// device together with that context's unique id.  A call from a different
+// context on that device (after cudaDeviceReset made a new primary context,
+// where the array may have moved) takes the address again.  Each call writes
+// every scratch word before reading it, so nothing has to be cleared between
+// calls.
 constexpr int64_t kNoAllocMaxRows = int64_t(1) << 23;  // 8,388,608 active ids
 constexpr size_t cx_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
 constexpr int64_t kNoAllocChunks = (kNoAllocMaxRows + kCullChunk - 1) / kCullChunk;
@@ -229,24 +235,61 @@ constexpr size_t kNoAllocScratchBytes = cx_align((size_t)((kNoAllocMaxRows + 31)
 static __device__ __align__(256) unsigned char g_cull_scratch[kNoAllocScratchBytes];
 
 constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocSlot {
+    void* ptr;
+    unsigned long long ctx_id;  // unique id of the context the address belongs to
+};
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+static NoAllocSlot g_noalloc[kNoAllocMaxDevices] = {};
 
-// Device address of g_cull_scratch on the current device (looked up on first use).
+// Unique id of the context current on this thread (cuCtxGetCurrent +
+// cuCtxGetId, reached through the runtime's driver entry points so the
+// library needs no link to the driver library); 0 when no context is
+// current or the driver cannot say, in which case the address is looked up
+// on every call.
+static unsigned long long current_context_id() {
+    using GetCurrentFn = CUresult (*)(CUcontext*);
+    using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetIdFn>(f);
+        cudaGetLastError();  // a missing entry point is not this call's error
+    });
+    if (!get_current || !get_id) return 0;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    unsigned long long id = 0;
+    return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of g_cull_scratch on the current device and context.
 static int noalloc_scratch(void** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "cull_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
     GS_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "cull_noalloc: device %d out of range", dev);
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    NoAllocSlot& slot = g_noalloc[dev];
+    const unsigned long long ctx = current_context_id();
+    if (slot.ptr == nullptr || ctx == 0 || slot.ctx_id != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_cull_scratch);
         if (e != cudaSuccess || p == nullptr)
             return set_error(GS_ERR_CUDA, "cull_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        g_noalloc_ptr[dev] = p;
+        slot.ptr = p;
+        slot.ctx_id = current_context_id();  // the lookup made the device's context current
     }
-    *out = g_noalloc_ptr[dev];
+    *out = slot.ptr;
     return GS_OK;
 }
 

@@ -48,7 +48,10 @@ __global__ void group_barrier_kernel(uint32_t* const* __restrict__ peer_pads, in
 constexpr int kSumUnroll = 4;  // loads in flight per thread before the stores
 
 __global__ void __launch_bounds__(256) rows_sum_multicast_kernel(float4* __restrict__ mc, int64_t begin,
-                                                                 int64_t end) {
+                                                                 int64_t end, const int32_t* __restrict__ error_flag) {
+    // a group barrier before this launch gave up waiting for a peer: some
+    // copies may be incomplete, so no partial sum is formed or broadcast
+    if (error_flag && *reinterpret_cast<const volatile int32_t*>(error_flag) != 0) return;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < end; i0 += kSumUnroll * stride) {
         float4 v[kSumUnroll];
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(256) rows_sum_multicast_kernel(float4* __restr
 using namespace gs;
 
 extern "C" int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, int64_t num_rows, int64_t stride,
-                                     gs_stream_t stream) {
+                                     const int32_t* error_flag, gs_stream_t stream) {
     GS_REQUIRE(multicast_rows && aligned16(multicast_rows), "rows_sum_multicast: 16-byte aligned address needed");
     GS_REQUIRE(first_row >= 0 && num_rows >= 0 && stride > 0 && stride % 4 == 0,
                "rows_sum_multicast: bad rows or stride (a multiple of 4 floats)");
@@ -88,7 +91,7 @@ extern "C" int gs_rows_sum_multicast(float* multicast_rows, int64_t first_row, i
     const int64_t n = end - begin;
     const unsigned blocks = (unsigned)std::min<int64_t>((n + 256 * kSumUnroll - 1) / (256 * kSumUnroll), 148 * 8);
     rows_sum_multicast_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<float4*>(multicast_rows),
-                                                                        begin, end);
+                                                                        begin, end, error_flag);
     return check_launch("rows_sum_multicast_kernel");
 }
 

@@ -65,6 +65,15 @@ __global__ void export_rows_kernel(const float* __restrict__ theta, int64_t stri
     oq[3] = __fdiv_rn(q3, nrm);
 }
 
+// mask[slots[j]] = value for j < n (slots at or past mask_len are skipped).
+__global__ void mark_slots_kernel(int8_t* __restrict__ mask, int64_t mask_len, const int32_t* __restrict__ slots,
+                                  int64_t n, int8_t value) {
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const int32_t s = slots[j];
+    if (s >= 0 && s < mask_len) mask[s] = value;
+}
+
 }  // namespace gs
 
 using namespace gs;
@@ -110,4 +119,13 @@ extern "C" int gs_fill_column(float* dst, int64_t n_rows, int64_t stride, int co
     GS_REQUIRE(dst, "fill_column: null pointer");
     fill_column_kernel<<<grid_for(n_rows, 256), 256, 0, (cudaStream_t)stream>>>(dst, n_rows, stride, col, value);
     return check_launch("fill_column");
+}
+
+extern "C" int gs_mark_slots(int8_t* mask, int64_t mask_len, const int32_t* slots, int64_t n, int value,
+                             gs_stream_t stream) {
+    GS_REQUIRE(n >= 0 && mask_len >= 0, "mark_slots: bad sizes");
+    if (n == 0) return GS_OK;
+    GS_REQUIRE(mask && slots, "mark_slots: null pointer");
+    mark_slots_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(mask, mask_len, slots, n, (int8_t)value);
+    return check_launch("mark_slots_kernel");
 }

@@ -34,8 +34,16 @@ constexpr int kGradRec = 12;  // floats per splat gradient record
 // warp's pixels are reduced with 14 shuffles, added into per-batch
 // shared-memory accumulators, and flushed with one global vector reduction
 // per (tile, splat).
+//
+// Two forms of a splat's step, chosen per (warp, splat), both bit-identical
+// to the forward's alphas:
+//  * fast — the splat's opacity is below 0.98 and its conic is positive
+//    definite, so opacity * g < 0.99 wherever the splat reaches (g <= 1 up
+//    to rounding): the clip is the identity and passes every gradient.  A
+//    pixel that does not take part gets m = +inf, hence g = 0 and alpha = 0.
+//  * general — the 0.99 clip and its gradient mask, for every other splat.
 struct PixelBwd {
-    float T, dr, dg, db, dA, Bv;
+    float T, dr, dg, db, dA;
     int last;
 };
 
@@ -44,7 +52,7 @@ __device__ __forceinline__ void pixel_bwd_init(PixelBwd& s, bool inside, int64_t
                                                int loss_mode, const void* target, const float* dL_dcolor,
                                                const float* dL_dalpha) {
     s.T = 1.f;
-    s.dr = s.dg = s.db = s.dA = s.Bv = 0.f;
+    s.dr = s.dg = s.db = s.dA = 0.f;
     s.last = 0;
     if (!inside) return;
     s.T = final_T[pix];
@@ -83,39 +91,74 @@ struct SplatBwd {
 };
 
 // Backward state of a pixel pair (lanes .x / .y: a thread's pixels 2q and 2q + 1).
+// ``dA`` is carried only when the loss has an alpha cotangent (kDA).
+template <bool kDA>
 struct PairBwd {
+    float2 T, dr, dg, db, Bv;
+    int last0, last1;
+};
+template <>
+struct PairBwd<true> {
     float2 T, dr, dg, db, dA, Bv;
     int last0, last1;
 };
 
-// One splat's step for a pixel pair; v0 / v1 say whether each pixel takes
-// part.  Adds w T dL/dC to the colour sums and dog = dL/dalpha * g (the
+template <bool kDA>
+__device__ __forceinline__ float2 pair_val(const PairBwd<kDA>& s, const SplatBwd& c) {
+    if constexpr (kDA)
+        return __ffma2_rn(s.dr, f2(c.r), __ffma2_rn(s.dg, f2(c.g), __ffma2_rn(s.db, f2(c.b), s.dA)));
+    else
+        return __ffma2_rn(s.dr, f2(c.r), __ffma2_rn(s.dg, f2(c.g), __fmul2_rn(s.db, f2(c.b))));
+}
+
+// One splat's step for a pixel pair, given the pair's alpha ``al`` (0 where a
+// pixel does not take part) and the clip's gradient mask times the falloff
+// ``gi``.  Adds w T dL/dC to the colour sums and dog = dL/dalpha * g (the
 // geometry gradients are linear in it, see the kernel) with its y moments to
-// the pair sums.  Branch-free: a pixel that does not take part gets alpha = 0,
-// which leaves T and B unchanged and zeroes every term.
-__device__ __forceinline__ void pair_bwd_step(PairBwd& s, bool v0, bool v1, float2 m, float2 y, const SplatBwd& c,
-                                              float2& sd, float2& sy, float2& syy, float2& sr, float2& sg,
-                                              float2& sb) {
-    const float2 gv = pair_falloff(m);
-    const float2 og = __fmul2_rn(f2(c.opac), gv);
-    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+// the pair sums.  A pixel with alpha = 0 keeps T and B and adds nothing.
+template <bool kDA>
+__device__ __forceinline__ void pair_bwd_accum(PairBwd<kDA>& s, float2 al, float2 gi, float2 y, const SplatBwd& c,
+                                               float2& sd, float2& sy, float2& syy, float2& sr, float2& sg,
+                                               float2& sb) {
     const float2 oma = __ffma2_rn(al, f2(-1.f), f2(1.f));  // 1 - alpha >= 0.01
     s.T = __fmul2_rn(s.T, make_float2(fast_rcp(oma.x), fast_rcp(oma.y)));  // T_i = T_{i+1} / (1 - alpha_i)
-    const float2 val = __ffma2_rn(s.dr, f2(c.r), __ffma2_rn(s.dg, f2(c.g), __ffma2_rn(s.db, f2(c.b), s.dA)));
+    const float2 val = pair_val<kDA>(s, c);
     const float2 d = __ffma2_rn(s.Bv, f2(-1.f), val);  // val - B
     s.Bv = __ffma2_rn(al, d, s.Bv);                     // = al * val + (1 - al) * B
     const float2 wT = __fmul2_rn(al, s.T);
     sr = __ffma2_rn(wT, s.dr, sr);
     sg = __ffma2_rn(wT, s.dg, sg);
     sb = __ffma2_rn(wT, s.db, sb);
-    // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
-    // (opacity * g > 0 holds for every pixel that takes part: m <= the pair cut)
-    const float2 gi = make_float2(v0 && og.x < 0.99f ? gv.x : 0.f, v1 && og.y < 0.99f ? gv.y : 0.f);
     const float2 dog = __fmul2_rn(__fmul2_rn(s.T, d), gi);
     sd = __fadd2_rn(sd, dog);
     const float2 t = __fmul2_rn(dog, y);
     sy = __fadd2_rn(sy, t);
     syy = __ffma2_rn(t, y, syy);
+}
+
+// General form: the last-entry test, the 0.99 clip and its gradient mask.
+template <bool kDA>
+__device__ __forceinline__ void pair_bwd_step(PairBwd<kDA>& s, bool v0, bool v1, float2 m, float2 y,
+                                              const SplatBwd& c, float2& sd, float2& sy, float2& syy, float2& sr,
+                                              float2& sg, float2& sb) {
+    const float2 gv = pair_falloff(m);
+    const float2 og = __fmul2_rn(f2(c.opac), gv);
+    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+    // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
+    // (opacity * g > 0 holds for every pixel that takes part: m <= the pair cut)
+    const float2 gi = make_float2(v0 && og.x < 0.99f ? gv.x : 0.f, v1 && og.y < 0.99f ? gv.y : 0.f);
+    pair_bwd_accum<kDA>(s, al, gi, y, c, sd, sy, syy, sr, sg, sb);
+}
+
+// Fast form: alpha = opacity * g with g = 0 where the pixel does not take part.
+template <bool kDA>
+__device__ __forceinline__ void pair_bwd_step_fast(PairBwd<kDA>& s, bool v0, bool v1, float2 m, float2 y,
+                                                   const SplatBwd& c, float2& sd, float2& sy, float2& syy,
+                                                   float2& sr, float2& sg, float2& sb) {
+    const float inf = __int_as_float(0x7f800000);
+    const float2 gv = pair_falloff(make_float2(v0 ? m.x : inf, v1 ? m.y : inf));  // ex2(-inf) = 0
+    const float2 al = __fmul2_rn(f2(c.opac), gv);
+    pair_bwd_accum<kDA>(s, al, gv, y, c, sd, sy, syy, sr, sg, sb);
 }
 
 // GS_BWD_MIN_CTAS > 0 asks the register allocator for that many resident CTAs per SM
@@ -124,6 +167,7 @@ __device__ __forceinline__ void pair_bwd_step(PairBwd& s, bool v0, bool v1, floa
 #else
 #define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads)
 #endif
+template <bool kDA>
 __global__ void GS_BWD_BOUNDS render_bwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
@@ -145,7 +189,7 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
 #pragma unroll
         for (int c = 0; c < 9; ++c) acc[j][c] = 0.f;
 
-    PairBwd s[kPairs];
+    PairBwd<kDA> s[kPairs];
     float2 py[kPairs];
     int mylast = 0;
 #pragma unroll
@@ -161,7 +205,7 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
         s[q].dr = make_float2(a.dr, b.dr);
         s[q].dg = make_float2(a.dg, b.dg);
         s[q].db = make_float2(a.db, b.db);
-        s[q].dA = make_float2(a.dA, b.dA);
+        if constexpr (kDA) s[q].dA = make_float2(a.dA, b.dA);
         s[q].Bv = f2(0.f);
         s[q].last0 = a.last;
         s[q].last1 = b.last;
@@ -185,9 +229,14 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             const uint32_t vr = vals[bstart + j];
             const uint32_t vi = vr < (uint64_t)nv ? vr : 0u;
             sv[j] = vi;
-            s0[j] = splats[3 * vi];
-            s1[j] = splats[3 * vi + 1];
-            s2[j] = splats[3 * vi + 2];
+            const float4 a = splats[3 * vi], b = splats[3 * vi + 1];
+            float4 c = splats[3 * vi + 2];
+            // .w (the depth, unused here) becomes the fast-form flag of the splat
+            const float sym = 0.5f * (a.w + b.x);
+            c.w = (b.z < 0.98f && a.z > 0.f && b.y > 0.f && a.z * b.y - sym * sym > 0.f) ? 1.f : 0.f;
+            s0[j] = a;
+            s1[j] = b;
+            s2[j] = c;
         }
         __syncthreads();
         // which staged splats can reach this warp's pixel block (same test as the forward),
@@ -211,6 +260,7 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             const int k = 32 * i + hb;
             const int idx = bstart + k - rg.start;
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
+            const bool fast = q2.w != 0.f;  // uniform over the warp
             const float x = px - q0.x;
             const float ax = q0.z * x, cx = q1.x * x;
             float2 y[kPairs], m[kPairs];
@@ -236,14 +286,20 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             c.b = q2.y;
             c.opac = q1.z;
             float2 sd = f2(0.f), sy = f2(0.f), syy = f2(0.f), sr = f2(0.f), sg = f2(0.f), sb = f2(0.f);
+            if (fast) {
 #pragma unroll
-            for (int q = 0; q < kPairs; ++q) {
-#ifndef GS_BWD_NO_PAIR_SKIP
-                // a pair row of the warp block that the splat misses entirely
-                // contributes exactly nothing (alpha = 0 leaves T and B as they are)
-                if (!__any_sync(kFull, v0[q] | v1[q])) continue;
-#endif
-                pair_bwd_step(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+                for (int q = 0; q < kPairs; ++q) {
+                    // a pair row of the warp block that the splat misses entirely
+                    // contributes exactly nothing (alpha = 0 leaves T and B as they are)
+                    if (!__any_sync(kFull, v0[q] | v1[q])) continue;
+                    pair_bwd_step_fast<kDA>(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < kPairs; ++q) {
+                    if (!__any_sync(kFull, v0[q] | v1[q])) continue;
+                    pair_bwd_step<kDA>(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+                }
             }
             float g[9];
             g[5] = sd.x + sd.y;
@@ -577,10 +633,11 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const int32_t* ti
     GS_REQUIRE(aligned16(splat_grads) && aligned16(splats), "render_backward: records must be 16-byte aligned");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_bwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+    // the alpha cotangent is carried per pixel only when the caller passes one
+    auto kernel = (loss_mode == GS_LOSS_NONE && dL_dalpha) ? render_bwd_kernel<true> : render_bwd_kernel<false>;
+    kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T,
-        n_contrib, loss_mode,
-        target, dL_dcolor, dL_dalpha, splat_grads);
+        n_contrib, loss_mode, target, dL_dcolor, dL_dalpha, splat_grads);
     return check_launch("render_bwd_kernel");
 }
 

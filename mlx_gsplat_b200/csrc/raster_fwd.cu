@@ -499,11 +499,15 @@ __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, i
 #else
 #define GS_FWD_BOUNDS __launch_bounds__(kRenderThreads)
 #endif
+// kCount: the same compositing, but instead of writing the image it adds the
+// number of (pixel, splat) pairs that took part to *pairs (a diagnostic of the
+// work the compositing kernels do; not on the training path).
+template <bool kCount>
 __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, float* __restrict__ out_color, float* __restrict__ out_alpha, float* __restrict__ final_T,
     int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
-    float* __restrict__ loss_partials) {
+    float* __restrict__ loss_partials, unsigned long long* __restrict__ pairs) {
     __shared__ float4 s0[kBatch], s1[kBatch], s2[kBatch];
     __shared__ float red[kRenderThreads / 32];
     const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
@@ -520,6 +524,7 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     // (never written back), so they never take part.
     float2 py[kPairs], T[kPairs], cr[kPairs], cg[kPairs], cb[kPairs], A[kPairs];
     int last[kPx];
+    unsigned npairs = 0;
     const float t_min = p.t_min;
     const float t_out = fminf(-1.f, t_min - 1.f);
 #pragma unroll
@@ -593,6 +598,7 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
                     T[q] = __fmul2_rn(T[q], __ffma2_rn(al, f2(-1.f), f2(1.f)));  // T (1 - alpha)
                     last[2 * q] = v0 ? idx1 : last[2 * q];
                     last[2 * q + 1] = v1 ? idx1 : last[2 * q + 1];
+                    if constexpr (kCount) npairs += (unsigned)v0 + (unsigned)v1;
                 }
             }
             warp_done = __all_sync(kFull, all_dead());
@@ -600,6 +606,11 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
         __syncthreads();
     }
 
+    if constexpr (kCount) {
+        const unsigned long long w = (unsigned long long)__reduce_add_sync(kFull, npairs);
+        if (lane == 0 && w) atomicAdd(pairs, w);
+        return;
+    }
     float lsum = 0.f;
 #pragma unroll
     for (int k = 0; k < kPx; ++k) {
@@ -744,9 +755,23 @@ extern "C" int gs_render_forward(const gs_tile_range* ranges, const int32_t* til
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || target, "render_forward: target required");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_fwd_kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+    render_fwd_kernel<false><<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, out_alpha,
-        final_T, n_contrib,
-        loss_mode, target, loss_partials);
+        final_T, n_contrib, loss_mode, target, loss_partials, nullptr);
     return check_launch("render_fwd_kernel");
+}
+
+extern "C" int gs_render_pair_count(const gs_tile_range* ranges, const int32_t* tile_order,
+                                    const uint32_t* entry_vals, const float* splats, int64_t num_visible,
+                                    const gs_camera* cam, const gs_raster_settings* rs,
+                                    unsigned long long* pairs, gs_stream_t stream) {
+    GS_REQUIRE(cam && ranges && pairs, "render_pair_count: null pointer");
+    GS_REQUIRE(aligned16(splats), "render_pair_count: splats must be 16-byte aligned");
+    GS_REQUIRE(!rs || rs->transmittance_min <= 1.f, "render_pair_count: transmittance_min must be <= 1");
+    const RasterParams p = make_raster_params(*cam, rs);
+    const int tiles = p.tiles_x * p.tiles_y;
+    render_fwd_kernel<true><<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+        ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, nullptr, nullptr,
+        nullptr, nullptr, GS_LOSS_NONE, nullptr, nullptr, pairs);
+    return check_launch("render_fwd_kernel<count>");
 }

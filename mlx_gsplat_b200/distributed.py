@@ -150,14 +150,24 @@ class FusedRowReduce:
         sharded Adam (slot % world == rank)."""
         return (torch.arange(rows, device=self.device) % self.world) == self.rank
 
-    def gather_owned_rows(self, t: torch.Tensor, owned: torch.Tensor) -> None:
+    def gather_owned_rows(self, t: torch.Tensor, owned: torch.Tensor, rows: Optional[slice] = None,
+                          first_col: int = 0) -> None:
         """Every GPU's copy of the slot-indexed rows of ``t`` becomes the owners'
         rows: the rows this GPU does not own are zeroed, then summed over the
         group (an NCCL all-reduce); used before densify, export and
         checkpoints, which read the columns and moments the sharded Adam
-        leaves with the owners."""
-        t[~owned] = 0
-        dist.all_reduce(t, group=self.pg)
+        leaves with the owners.  Only the slot range ``rows`` (default: all)
+        and the columns from ``first_col`` on move: the columns every GPU
+        already holds identically (the broadcast ones) and unused slots need no
+        exchange."""
+        rows = rows if rows is not None else slice(0, t.shape[0])
+        part = t[rows, first_col:]
+        if part.numel() == 0:
+            return
+        buf = part.contiguous()
+        buf.masked_fill_(~owned[rows].unsqueeze(1), 0.0)
+        dist.all_reduce(buf, group=self.pg)
+        part.copy_(buf)
 
     def slice_of(self, n_rows: int):
         """This GPU's rows of the sum: a contiguous 1/world share."""
@@ -171,10 +181,15 @@ class FusedRowReduce:
         first, count = self.slice_of(n_rows)
         lib = self._lib.lib()
         self._lib.check(lib.gs_rows_sum_multicast(self.multicast, first, count, self.rows.shape[1],
-                                                  self._lib.stream_ptr(self.device)), "multicast row sum")
+                                                  self.error.data_ptr(), self._lib.stream_ptr(self.device)),
+                        "multicast row sum")
         self._barrier(1)
 
     def check(self) -> None:
+        """Raises if a group barrier of this GPU gave up waiting for a peer (a
+        host sync).  The row sum and the sharded Adam read the flag and skip
+        their work on that GPU, so no partial sum is applied there, but the
+        replicas are no longer in step and training cannot go on."""
         if int(self.error.item()) != 0:
             raise RuntimeError("multi-GPU barrier timed out (a peer did not arrive)")
 

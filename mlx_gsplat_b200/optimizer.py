@@ -140,12 +140,14 @@ class FusedMLXAdam:
                           m: torch.Tensor, v: torch.Tensor, table: torch.Tensor, num_active: int, ncols: int,
                           col_lo, col_hi, rank: int, world: int, hot_cols: int, quat_col: int = -1,
                           grad_scale: float = 1.0, grad_bias=None, g_cols: Optional[int] = None, count_col: int = 0,
-                          count_coef=None) -> None:
+                          count_coef=None, error_flag: Optional[int] = None) -> None:
         """``step_slab`` for one GPU of a multicast group: the rows whose slot
         this GPU owns (slot % world == rank), their gradient summed over the
         group through the multicast address ``g_multicast``, the first
         ``hot_cols`` columns of the new parameters stored to every GPU through
-        ``theta_multicast`` (``gs_fused_adam_slab_sharded``)."""
+        ``theta_multicast`` (``gs_fused_adam_slab_sharded``).  ``error_flag``:
+        device address of the group barriers' error flag; once a barrier wait
+        has given up the update is skipped on the GPU."""
         self.t += 1
         lib = _lib.lib()
         _lib.check(lib.gs_fused_adam_slab_sharded(theta.data_ptr(), theta_multicast, g_multicast, m.data_ptr(),
@@ -155,4 +157,5 @@ class FusedMLXAdam:
                                                   grad_scale, None if grad_bias is None else _lib.fptr(grad_bias),
                                                   ncols if g_cols is None else int(g_cols), int(count_col),
                                                   None if count_coef is None else _lib.fptr(count_coef), rank, world,
-                                                  hot_cols, _lib.stream_ptr(theta.device)), "sharded fused adam")
+                                                  hot_cols, error_flag, _lib.stream_ptr(theta.device)),
+                   "sharded fused adam")

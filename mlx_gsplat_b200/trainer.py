@@ -228,8 +228,9 @@ class RunnerMLX:
             theta_storage=self.fused_reduce.theta if self.sharded else None)
         self.allocator.set_initial_gaussians(init_params)
         self.optimizer = FusedMLXAdam(lr=cfg.lr, betas=cfg.betas, eps=cfg.eps)
-        # columns every GPU needs each step: what the rasterizer reads
-        self.hot_cols = L.stride if cfg.sh_eval == "full" else (L.color_col + 12 + 3) // 4 * 4
+        # columns every GPU needs each step: what the rasterizer reads (the
+        # geometry and SH <= 1 colour in the reference mode), whole 16-byte chunks
+        self.hot_cols = L.stride if cfg.sh_eval == "full" else min(L.stride, (L.color_col + 12 + 3) // 4 * 4)
         self._owned = self.fused_reduce.owned_slots(cfg.max_gaussians) if self.sharded else None
         if self.fused_reduce is not None:
             self.grad = self.fused_reduce.rows
@@ -251,6 +252,7 @@ class RunnerMLX:
         self.settings = RasterSettings(cfg.alpha_cutoff, cfg.transmittance_min)
         self.scene_scale = scene_scale
         self.last_frame = None
+        self._child_rows = None  # [2, capacity, stride] child rows of the density step
         self.step_count = 0
         self._k_hint = 0  # tile-entry buffer size for the next view (grows with the views seen)
         # How gradient rows of unseen Gaussians are formed: "sparse" (one GPU:
@@ -429,7 +431,8 @@ class RunnerMLX:
                                          al.adam_v, al.indirection_table, N, L.ncols, self.col_lo, self.col_hi,
                                          fr.rank, fr.world, self.hot_cols, quat_col=L.quat_col, grad_scale=scale,
                                          grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
-                                         count_coef=self.count_coef(step) if self.g_cols < L.ncols else None)
+                                         count_coef=self.count_coef(step) if self.g_cols < L.ncols else None,
+                                         error_flag=fr.error.data_ptr())
         fr.barrier(1)
 
     def gather_sharded_state(self, moments: bool = True) -> None:
@@ -440,10 +443,23 @@ class RunnerMLX:
         if not self.sharded:
             return
         al = self.allocator
-        self.fused_reduce.gather_owned_rows(al.theta, self._owned)
+        self.check_group()
+        if al.num_active == 0:
+            return
+        t = al.indirection_table
+        used = slice(int(t.min()), int(t.max()) + 1)  # the slot range in use (the free list pops from the top)
+        # theta: only the columns past the broadcast ones differ between GPUs
+        self.fused_reduce.gather_owned_rows(al.theta, self._owned, used, first_col=self.hot_cols)
         if moments:
-            self.fused_reduce.gather_owned_rows(al.adam_m, self._owned)
-            self.fused_reduce.gather_owned_rows(al.adam_v, self._owned)
+            self.fused_reduce.gather_owned_rows(al.adam_m, self._owned, used)
+            self.fused_reduce.gather_owned_rows(al.adam_v, self._owned, used)
+
+    def check_group(self) -> None:
+        """Raises if a multi-GPU barrier wait gave up (``FusedRowReduce.check``;
+        a host sync).  Called where the host syncs anyway: densify, export,
+        checkpoints, the log lines and the end of ``train``."""
+        if self.fused_reduce is not None:
+            self.fused_reduce.check()
 
     # ------------------------------------------------------------------ densify / prune
     def densify(self, step: int, noise: Optional[Dict[str, torch.Tensor]] = None) -> Tuple[int, int]:
@@ -459,21 +475,25 @@ class RunnerMLX:
         al = self.allocator
         L = self.layout
         N = al.num_active
+        self.check_group()
         self.gather_sharded_state(moments=False)  # children copy whole parent rows
         distributed.reduce_densify_stats(al.grad2d, al.count, self.pg)
         g = self._gaussians(step)
-        flags = torch.empty(max(N, 1), dtype=torch.uint8, device=self.device)
+        flags = al.workspace()["flags"]
         f32 = np.float32
         _lib.check(lib.gs_densify_masks(g, al.grad2d.data_ptr(), al.count.data_ptr(), N, 0.0002,
                                         float(f32(0.01 * self.scene_scale)), float(f32(0.1 * self.scene_scale)),
                                         0.005, 5e-2, int(N >= 80000), flags.data_ptr(), st), "densify masks")
-        self.last_densify = {"flags": flags[:N]}
+        self.last_densify = {"flags": flags[:N]}  # valid until the next density step
 
         def make_children(split_slots, refine_rows, n):
             nz = noise if noise is not None else distributed.densify_noise(step, n, self.device)
             self.last_densify["noise"] = nz
-            c1 = torch.empty((n, L.stride), dtype=torch.float32, device=self.device)
-            c2 = torch.empty_like(c1)
+            # child rows: buffers kept between density steps, grown (with headroom) when a step needs more
+            if self._child_rows is None or self._child_rows.shape[1] < n:
+                cap = min(al.max_gaussians, n + n // 4 + 1024)
+                self._child_rows = torch.empty((2, cap, L.stride), dtype=torch.float32, device=self.device)
+            c1, c2 = self._child_rows[0, :n], self._child_rows[1, :n]
             o = L.offsets
             _lib.check(lib.gs_densify_children(al.theta.data_ptr(), L.stride, L.ncols, split_slots.data_ptr(),
                                                refine_rows.data_ptr(), flags.data_ptr(), nz["means1"].data_ptr(),
@@ -534,6 +554,9 @@ class RunnerMLX:
                                       L.color_col, L.color_cols, out.data_ptr(), cols,
                                       _lib.stream_ptr(self.device)), "export rows")
         rows = out[:n].cpu().numpy()
+        if distributed.rank_of(self.pg) != 0:  # every rank holds the same rows; one writes the file
+            self._group_barrier()
+            return n
         head = [b"ply\n", b"format binary_little_endian 1.0\n", f"element vertex {n}\n".encode()]
         head += [f"property float {p}\n".encode() for p in ("x", "y", "z", "nx", "ny", "nz")]
         head += [f"property float f_dc_{j}\n".encode() for j in range(L.dims["sh0"])]
@@ -545,7 +568,13 @@ class RunnerMLX:
         with open(filepath, "wb") as f:
             f.write(b"".join(head))
             f.write(rows.astype("<f4").tobytes())
+        self._group_barrier()
         return n
+
+    def _group_barrier(self) -> None:
+        """Host barrier of the process group (after rank 0 wrote a file)."""
+        if self.world > 1:
+            torch.distributed.barrier(group=self.pg)
 
     _CKPT_TENSORS = ("theta", "adam_m", "adam_v", "free_stack", "active_mask", "grad2d", "count")
 
@@ -562,7 +591,9 @@ class RunnerMLX:
         state["adam_t"] = np.int64(self.optimizer.t)
         state["step_count"] = np.int64(self.step_count)
         state["layout"] = np.array([al.max_gaussians, al.layout.stride, al.layout.ncols], np.int64)
-        np.savez(filepath, **state)
+        if distributed.rank_of(self.pg) == 0:  # every rank holds the same state; one writes the file
+            np.savez(filepath, **state)
+        self._group_barrier()
 
     def load_checkpoint(self, filepath: str) -> None:
         """Restores a ``save_checkpoint`` state into this runner (same pool size
@@ -603,8 +634,10 @@ class RunnerMLX:
                         print(f"[Step {step:4d} - Densification] Pruned: {n_p} | Split/Duplicated: {n_s} | "
                               f"Active GS: {self.allocator.num_active}")
             if log_every and (step % log_every == 0 or step == 1):
+                self.check_group()
                 print(f"Step {step:5d} | Active: {self.allocator.num_active} | loss {float(self.loss_value()):.5f}")
         torch.cuda.synchronize(self.device)
+        self.check_group()
         elapsed = time.time() - t0
         if log_every:
             print(f"\n[Finished] 3DGS training complete in {elapsed:.2f} seconds.")

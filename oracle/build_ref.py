@@ -7,7 +7,7 @@ into ``oracle/_ref/ref_fused_adam_step.inc`` and compiles it, with
 the driver, into ``oracle/_ref/libref_adam.so``.  Nothing under ``oracle/_ref``
 is committed.  TEST INFRASTRUCTURE ONLY.
 
-Usage: ``python oracle/build_ref.py [REFERENCE_ROOT]`` (default ``/root/reference``).
+Usage: ``python oracle/build_ref.py REFERENCE_ROOT``.
 Returns quietly without building when the reference checkout is absent.
 """
 import os
@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 
 
-def build(ref_root: str = "/root/reference") -> bool:
+def build(ref_root: str) -> bool:
     src = os.path.join(ref_root, "src", "mlx_extensions.cpp")
     if not os.path.exists(src):
         return False
@@ -39,5 +39,7 @@ def build(ref_root: str = "/root/reference") -> bool:
 
 
 if __name__ == "__main__":
-    ok = build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python oracle/build_ref.py REFERENCE_ROOT")
+    ok = build(sys.argv[1])
     print("built oracle/_ref/libref_adam.so" if ok else "reference checkout absent; nothing built")

@@ -275,12 +275,17 @@ def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, 
 
 def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, width, height,
                         render_width, render_height, dL_dC, dL_dA=None, dtype=torch.float64,
-                        chunk: int = 256, pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference"):
+                        chunk: int = 256, pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference",
+                        l1_target=None):
     """Forward plus vector-Jacobian product of the dense rasterizer.
 
     ``dL_dC``/``dL_dA`` are ``[H,W,3]``/``[H,W,1]`` (or ``[P,3]``/``[P,1]`` for
     a pixel subset).  Returns ``(C, A, grads)`` with ``grads`` keyed
     ``means, quats, scales, opacities, colors`` on the gathered rows.
+    With ``l1_target`` ([H,W,3]) the loss is instead the trainer's
+    ``mean(|C - target|)`` (trainer.py:273-275, over all 3 H W values), whose
+    gradient is formed chunk by chunk in the same single pass (``dL_dC`` is
+    ignored).
     """
     leaves = [_as_t(a, dtype).requires_grad_(True) for a in (means, quats, scales, opacities, colors)]
     pg = project(*leaves, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
@@ -292,14 +297,18 @@ def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, wid
     if pixel_ids is not None:
         pix = pix[torch.as_tensor(np.asarray(pixel_ids, np.int64))]
     P = pix.shape[0]
-    gC = _as_t(dL_dC, dtype).reshape(P, 3)
+    tgt = None if l1_target is None else _as_t(l1_target, dtype).reshape(P, 3)
+    gC = None if tgt is not None else _as_t(dL_dC, dtype).reshape(P, 3)
     gA = None if dL_dA is None else _as_t(dL_dA, dtype).reshape(P, 1)
     cs, as_ = [], []
     for s in range(0, P, chunk):
         for k in keys:
             det[k].grad = None
         c_, a_ = composite(det, pix[s:s + chunk])
-        loss = torch.sum(c_ * gC[s:s + chunk])
+        if tgt is not None:
+            loss = torch.sum(torch.abs(c_ - tgt[s:s + chunk])) / (3 * P)
+        else:
+            loss = torch.sum(c_ * gC[s:s + chunk])
         if gA is not None:
             loss = loss + torch.sum(a_ * gA[s:s + chunk])
         gs = torch.autograd.grad(loss, [det[k] for k in keys], allow_unused=True)

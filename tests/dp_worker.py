@@ -9,6 +9,9 @@ parameters and moments on every GPU, before and after a densify step:
 * the multicast row sum, then a replicated Adam — narrow rows;
 * an NCCL all-reduce, then a replicated Adam — narrow rows;
 * an NCCL all-reduce of full-width rows.
+
+Then the same for an SH degree 0 scene (16-float rows, where the broadcast
+columns are the whole row): the sharded Adam against the NCCL all-reduce.
 """
 import os
 import sys
@@ -22,8 +25,9 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from mlx_gsplat_b200 import distributed  # noqa: E402
 from mlx_gsplat_b200.trainer import runner_for_workload  # noqa: E402
 
-CONFIGS = [("sharded", True, True, True), ("multicast sum", True, True, False), ("nccl", False, True, True),
-           ("nccl full rows", False, False, True)]
+CONFIGS = [("outdoor-1m", "sharded", True, True, True), ("outdoor-1m", "multicast sum", True, True, False),
+           ("outdoor-1m", "nccl", False, True, True), ("outdoor-1m", "nccl full rows", False, False, True),
+           ("mid-200k", "sharded sh0", True, True, True), ("mid-200k", "nccl sh0", False, True, True)]
 
 
 def state(r):
@@ -38,15 +42,16 @@ def main():
     rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=120.0)
     dev = torch.device("cuda", local)
     out = {}
-    for name, fused, compact, sharded in CONFIGS:
-        r = runner_for_workload("outdoor-1m", n=20_000, max_steps=100, device=dev, num_views=8, process_group=pg,
+    for wl, name, fused, compact, sharded in CONFIGS:
+        r = runner_for_workload(wl, n=20_000, max_steps=100, device=dev, num_views=8, process_group=pg,
                                 fused_reduce=fused, compact_grad_rows=compact, sharded_adam=sharded,
                                 max_gaussians=60_000)
         if fused and r.fused_reduce is None:
             print("SKIP: no multicast support", flush=True)
             dist.destroy_process_group()
             return
-        assert (r.g_stride == 24) == compact and r.sharded == (fused and sharded)
+        assert wl != "outdoor-1m" or (r.g_stride == 24) == compact
+        assert r.sharded == (fused and sharded)
         for step in range(1, 4):
             r.train_step(distributed.view_for(step, rank, world, 8), step)
         before = state(r)
@@ -61,10 +66,14 @@ def main():
         if r.fused_reduce is not None:
             r.fused_reduce.check()
         out[name] = before + state(r)
-    ref = out["sharded"]
-    err = max(float(np.abs(a - b).max()) for o in out.values() for a, b in zip(ref, o) if a.shape == b.shape)
-    ok = all(len(o) == len(ref) and all(a.shape == b.shape and np.allclose(a, b, rtol=1e-5, atol=1e-6)
-                                        for a, b in zip(ref, o)) for o in out.values())
+    groups = {"sharded": [k for k in out if not k.endswith("sh0")], "sharded sh0": ["nccl sh0"]}
+    err, ok = 0.0, True
+    for refname, others in groups.items():
+        ref = out[refname]
+        for o in (out[k] for k in others):
+            err = max([err] + [float(np.abs(a - b).max()) for a, b in zip(ref, o) if a.shape == b.shape])
+            ok = ok and len(o) == len(ref) and all(a.shape == b.shape and np.allclose(a, b, rtol=1e-5, atol=1e-6)
+                                                   for a, b in zip(ref, o))
     gathered = [None] * world
     dist.all_gather_object(gathered, (bool(ok), float(err), {k: [x.shape for x in v] for k, v in out.items()}),
                            group=pg)

@@ -8,7 +8,7 @@ MLX is not installable here, so ``tests/golden/mlx_shim`` stands in for
 ``.npz`` files committed next to this script; they pin the CPU oracle
 (``tests/test_oracle_golden.py``).  Run from the repository root:
 
-    python tests/golden/gen_golden.py [REFERENCE_ROOT]     # default /root/reference
+    python tests/golden/gen_golden.py REFERENCE_ROOT
 
 The reference checkout is needed only to regenerate; the tests read the
 committed fixtures.
@@ -18,6 +18,7 @@ from __future__ import annotations
 import importlib.util
 import os
 import sys
+import tempfile
 
 import numpy as np
 import torch
@@ -355,15 +356,16 @@ def gen_colmap(ref_root, out):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/gen_golden.py REFERENCE_ROOT")
+    ref_root = sys.argv[1]
     torch.manual_seed(0)
     torch.set_num_threads(1)  # a fixed summation order for the reference's matmuls
     R = load_ref(ref_root, "rendering")
     O = load_ref(ref_root, "optimizer")
     cwd = os.getcwd()
-    tmp = os.path.join(ROOT, "_work", "golden_cwd")
-    os.makedirs(tmp, exist_ok=True)
-    os.chdir(tmp)  # the allocator writes a log next to its own file; keep any stray output out of the repo
+    tmp_dir = tempfile.TemporaryDirectory(prefix="gen_golden_")
+    os.chdir(tmp_dir.name)  # the allocator writes a log next to its own file; keep any stray output out of the repo
     try:
         A = load_ref(ref_root, "allocator")
         gen_cull(R, HERE)
@@ -375,6 +377,7 @@ def main():
         gen_colmap(ref_root, HERE)
     finally:
         os.chdir(cwd)
+        tmp_dir.cleanup()
     print("fixtures written to", HERE)
 
 

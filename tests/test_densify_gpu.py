@@ -159,3 +159,26 @@ def test_densify_rounds_on_the_stress_workload():
         assert_same(al, o, f"round {rnd}")
         refined += n_s
     assert refined > 0  # the rounds exercised the split/clone path
+
+
+def test_opacity_reset_sets_every_slot():
+    """trainer.py:416-419: every slot of the opacity pool (used and free) is set
+    to the logit -4.59; no other column changes.  Then through the training
+    loop: with max_steps <= 3000 the reset falls on every 1000th step, so
+    after a 1000-step run every opacity logit is -4.59."""
+    r = runner_for_workload("tiny-3k", max_steps=50, n=3000, num_views=4, max_gaussians=4096)
+    r.train_step(0, 1)
+    al, L = r.allocator, r.layout
+    before = al.theta.cpu().numpy().copy()
+    al.reset_opacities(-4.59)
+    after = al.theta.cpu().numpy()
+    o = L.offsets["opacities"]
+    np.testing.assert_array_equal(after[:, o], np.full(al.max_gaussians, np.float32(-4.59)))
+    keep = [c for c in range(after.shape[1]) if c != o]
+    np.testing.assert_array_equal(after[:, keep], before[:, keep])
+    # the reset schedule of the training loop
+    r = runner_for_workload("tiny-3k", max_steps=1000, n=3000, num_views=8, max_gaussians=4096, densify=False,
+                            lr=1e-2)
+    r.train(log_every=0)
+    op = r.allocator.physical_pools["opacities"].cpu().numpy()
+    np.testing.assert_array_equal(op, np.full_like(op, np.float32(-4.59)))

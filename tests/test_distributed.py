@@ -205,3 +205,30 @@ def test_narrow_gradient_rows_sum_like_full_rows():
     expanded = np.concatenate([nar[:, :23], nar[:, 23:24] * np.float32(1e-5) * np.ones((1, 36), np.float32)], 1)
     np.testing.assert_allclose(expanded, full[:, :59], rtol=1e-6, atol=0)
     assert nar[:, 23].max() <= 2 and nar[:, 23].sum() > 0
+
+
+def _gather_owned(rank, world):
+    """gather_owned_rows on gloo ranks: each rank holds the true rows of the
+    slots it owns (slot % world == rank) and garbage (NaN included) elsewhere
+    in the columns the owners keep; the broadcast columns are identical."""
+    from mlx_gsplat_b200 import distributed as D
+    rows, cols, hot = 40, 12, 4
+    truth = np.random.default_rng(0).normal(0, 1, (rows, cols)).astype(np.float32)
+    t = torch.from_numpy(truth.copy())
+    owned = (torch.arange(rows) % world) == rank
+    junk = torch.from_numpy(np.random.default_rng(100 + rank).normal(0, 1, (rows, cols)).astype(np.float32))
+    junk[3, 7] = float("nan")
+    t[~owned, hot:] = junk[~owned, hot:]
+    outside = t[:10].clone()
+    fr = D.FusedRowReduce.__new__(D.FusedRowReduce)  # host logic only: no symmetric memory on gloo
+    fr.pg = dist.group.WORLD
+    fr.gather_owned_rows(t, owned, slice(10, rows), first_col=hot)
+    return {"t": t.numpy(), "truth": truth, "outside": outside.numpy()}
+
+
+def test_gather_owned_rows_moves_only_the_used_range_and_owner_columns():
+    a, b = _run(_gather_owned)
+    for r in (a, b):
+        np.testing.assert_array_equal(r["t"][10:], r["truth"][10:])  # used slots: the owners' rows
+        np.testing.assert_array_equal(r["t"][:10], r["outside"])     # outside the range: untouched
+    np.testing.assert_array_equal(a["t"][10:], b["t"][10:])

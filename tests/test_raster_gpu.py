@@ -50,11 +50,12 @@ def test_matches_reference_golden(golden_dir, case):
         assert_grad_close(params[k].grad.cpu().numpy(), p("grad_" + k), what=f"{case} grad {k}")
 
 
-def _oracle_grads(g, cols_vis, ids, vm, K, W, H, dC, dA=None, pixel_ids=None):
+def _oracle_grads(g, cols_vis, ids, vm, K, W, H, dC, dA=None, pixel_ids=None, chunk=None):
     ids64 = ids.astype(np.int64)
+    chunk = chunk or (256 if pixel_ids is None else 16)
     C, A, gr = orend.rasterize_dense_vjp(g["means"][ids64], g["quats"][ids64], g["scales"][ids64],
                                          g["opacities"][ids64], cols_vis, vm, K, W, H, W, H, dL_dC=dC, dL_dA=dA,
-                                         pixel_ids=pixel_ids, chunk=256 if pixel_ids is None else 16)
+                                         pixel_ids=pixel_ids, chunk=chunk)
     full = {}
     for k in ("means", "quats", "scales", "opacities"):
         z = np.zeros_like(g[k], dtype=np.float64)
@@ -109,38 +110,46 @@ def _subset(wl, n_pix, seed):
     return np.sort(rng.choice(wl.pixels, n_pix, replace=False))
 
 
-@pytest.mark.parametrize("wl_name,n,n_pix", [("mid-200k", 200_000, 512), ("outdoor-1m", 1_000_000, 96)])
-def test_full_size_pixel_subset_vs_oracle(wl_name, n, n_pix):
+@pytest.mark.parametrize("wl_name,n,n_pix,view_ids,chunk", [("mid-200k", 200_000, 512, (1,), 16),
+                                                            ("outdoor-1m", 1_000_000, 512, (1, 5), 16),
+                                                            ("large-6m", 6_000_000, 32, (3,), 4)])
+def test_full_size_pixel_subset_vs_oracle(wl_name, n, n_pix, view_ids, chunk):
     """Full-size scenes: the oracle evaluates only a pixel subset (dense over every
-    visible Gaussian); the cotangent is non-zero only there."""
-    wl, g, cols = _scene(wl_name, n, seed=0, sh_dim=12 if wl_name == "outdoor-1m" else 3)
+    visible Gaussian); the cotangent is non-zero only there.  The large scene
+    (6,000,000 Gaussians at 3840x2160, about 2.8 M visible) runs 32 pixels;
+    the outdoor scene two views of 512 pixels each."""
+    sh_dim = 12 if synthetic.WORKLOADS[wl_name].sh_degree > 0 else 3
+    wl, g, cols = _scene(wl_name, n, seed=0, sh_dim=sh_dim)
     views, K = synthetic.make_cameras(wl, seed=2, num_views=8)
-    vm = views[1]
-    params = {"means": _t(g["means"]), "quats": _t(g["quats"]), "scales": _t(g["scales"]),
-              "opacities": _t(g["opacities"])}
-    ids = frustum_culling_mlx(params["means"], None, None, vm, K, wl.width, wl.height,
-                              opacities=params["opacities"])
-    idn = ids.cpu().numpy()
-    cols_vis = cols[idn.astype(np.int64)]
-    for k in params:
-        params[k].requires_grad_(True)
-    params["colors"] = _t(cols_vis).requires_grad_(True)
-    C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
-                                   params["colors"], vm, K, wl.width, wl.height, ids, render_width=wl.width,
-                                   render_height=wl.height)
-    pix = _subset(wl, n_pix, seed=5)
-    rng = np.random.default_rng(2)
-    wsub = rng.uniform(-1, 1, (n_pix, 3)).astype(np.float32)
-    wC = np.zeros((wl.pixels, 3), np.float32)
-    wC[pix] = wsub
-    (torch.sum(C * _t(wC.reshape(wl.height, wl.width, 3)))).backward()
-    Cr, Ar, gr = _oracle_grads(g, cols_vis, idn, vm, K, wl.width, wl.height, wsub, None, pixel_ids=pix)
-    Cg = C.detach().cpu().numpy().reshape(-1, 3)[pix]
-    Ag = A.detach().cpu().numpy().reshape(-1, 1)[pix]
-    assert_image_close(Cg, Cr, what="colors at subset")
-    assert_image_close(Ag, Ar, what="alphas at subset")
-    for k in NAMES:
-        assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what=f"{wl_name} grad {k}")
+    for vi in view_ids:
+        vm = views[vi]
+        params = {"means": _t(g["means"]), "quats": _t(g["quats"]), "scales": _t(g["scales"]),
+                  "opacities": _t(g["opacities"])}
+        ids = frustum_culling_mlx(params["means"], None, None, vm, K, wl.width, wl.height,
+                                  opacities=params["opacities"])
+        idn = ids.cpu().numpy()
+        cols_vis = cols[idn.astype(np.int64)]
+        for k in params:
+            params[k].requires_grad_(True)
+        params["colors"] = _t(cols_vis).requires_grad_(True)
+        C, A = rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                       params["colors"], vm, K, wl.width, wl.height, ids, render_width=wl.width,
+                                       render_height=wl.height)
+        pix = _subset(wl, n_pix, seed=5 + vi)
+        rng = np.random.default_rng(2 + vi)
+        wsub = rng.uniform(-1, 1, (n_pix, 3)).astype(np.float32)
+        wC = np.zeros((wl.pixels, 3), np.float32)
+        wC[pix] = wsub
+        (torch.sum(C * _t(wC.reshape(wl.height, wl.width, 3)))).backward()
+        Cr, Ar, gr = _oracle_grads(g, cols_vis, idn, vm, K, wl.width, wl.height, wsub, None, pixel_ids=pix,
+                                   chunk=chunk)
+        Cg = C.detach().cpu().numpy().reshape(-1, 3)[pix]
+        Ag = A.detach().cpu().numpy().reshape(-1, 1)[pix]
+        assert_image_close(Cg, Cr, what=f"view {vi} colors at subset")
+        assert_image_close(Ag, Ar, what=f"view {vi} alphas at subset")
+        for k in NAMES:
+            assert_grad_close(params[k].grad.cpu().numpy(), gr[k], what=f"{wl_name} view {vi} grad {k}")
+        del params, C, A, gr
 
 
 def test_fused_l1_loss_matches_autograd_path():

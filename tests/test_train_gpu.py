@@ -211,3 +211,56 @@ def test_training_reduces_loss():
         if step % 8 == 1:
             losses.append(float(r.loss_value()))
     assert losses[-1] < 0.8 * losses[0], losses
+
+
+@pytest.mark.parametrize("wl_name,n", [("tiny-3k", 3000), ("outdoor-small", None)])
+def test_grad2d_statistic_matches_oracle(monkeypatch, wl_name, n):
+    """The densification statistic of mlx_gsplat/trainer.py:300-318 over two
+    steps: ``grad2d[slot] += sqrt(sum (dL/dmean + 1e-5)^2 + 1e-8) * |z| / fx``
+    and ``count[slot] += 1`` at the physical slots of the visible Gaussians,
+    accumulated by the projection backward.  Checked two ways each step:
+    within 1e-5 relative of the oracle's ``grad2d_proxy`` evaluated on the
+    GPU's own mean gradients (the formula itself), and within the gradient
+    tolerance of the dense oracle's mean gradients (end to end); the counts
+    exactly."""
+    if wl_name == "outdoor-small":
+        _small_outdoor(monkeypatch)
+    r = runner_for_workload(wl_name, max_steps=50, n=n, num_views=4, lr=1e-3, eps=1e-15)
+    r.row_mode = "dense"  # rows hold dL/dmean + 1e-5 for every Gaussian
+    al, L = r.allocator, r.layout
+    M = al.max_gaussians
+    g2_exact = np.zeros(M, np.float64)
+    g2_e2e = np.zeros(M, np.float64)
+    cnt = np.zeros(M, np.float32)
+    om = L.offsets["means"]
+    for step, view in ((1, 0), (2, 1)):
+        theta0 = al.theta.cpu().numpy().copy()
+        table = al.indirection_table.cpu().numpy()
+        frame = r.train_step(view, step)
+        torch.cuda.synchronize()
+        ids = frame.ids[:frame.V].cpu().numpy().astype(np.int64)
+        assert ids.size > 0
+        vm = r.viewmats[view]
+        fx = float(r.K[0, 0])
+        means = theta0[table][:, om:om + 3]
+        grad = r.full_gradient_rows(step).cpu().numpy()
+        gm_gpu = grad[ids, om:om + 3]
+        slots = table[ids]
+        g2_exact[slots] += odens.grad2d_proxy(gm_gpu, means[ids], vm, fx)
+        # end to end: the dense oracle's own mean gradients (+ the 1e-5 regulariser)
+        act = {k: theta0[table][:, o:o + L.dims[k]] for k, o in L.offsets.items()}
+        colors = np.concatenate([act["sh0"], act["shN"]], 1)[:, :sh_cols_for(step, r.cfg)]
+        C = frame.color.cpu().numpy()
+        tgt = r.targets[view].cpu().numpy()
+        tf = tgt.astype(np.float32) / np.float32(255.0) if tgt.dtype == np.uint8 else tgt
+        dC = np.sign(C.astype(np.float64) - tf) / (3.0 * r.cfg.render_width * r.cfg.render_height)
+        _, _, gr = orend.rasterize_dense_vjp(act["means"][ids], act["quats"][ids], act["scales"][ids],
+                                             act["opacities"][ids], colors[ids], vm, r.K, r.cfg.width,
+                                             r.cfg.height, r.cfg.render_width, r.cfg.render_height, dL_dC=dC)
+        g2_e2e[slots] += odens.grad2d_proxy((gr["means"] + r.cfg.param_reg).astype(np.float32), means[ids], vm, fx)
+        cnt[slots] += 1.0
+        got = al.grad2d.cpu().numpy().astype(np.float64)
+        np.testing.assert_array_equal(al.count.cpu().numpy(), cnt, err_msg=f"step {step} count")
+        np.testing.assert_allclose(got, g2_exact, rtol=1e-5, atol=0, err_msg=f"step {step} grad2d (formula)")
+        assert_grad_close(got, g2_e2e, what=f"step {step} grad2d (end to end)")
+    assert cnt.max() == 2  # some Gaussians were seen by both views: the statistic accumulated
