@@ -83,6 +83,16 @@ def parse():
                          "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
+    ap.add_argument("--allreduce-buckets", type=int, default=4,
+                    help="N > 1 over NCCL: row ranges of the gradient sum, each range's Adam overlapping the later "
+                         "ranges' all-reduce (1: one all-reduce, then Adam)")
+    ap.add_argument("--target-images", type=int, default=None,
+                    help="distinct seeded uint8 target images, cycled over the views (default: one per view, "
+                         "up to ~1 GB of them)")
+    ap.add_argument("--train-run", type=int, default=0,
+                    help="instead of the step benchmark, time a whole training run of this many steps with the "
+                         "trainer's schedule (density steps every 100 steps in its window, opacity resets) and "
+                         "report its steps/s")
     ap.add_argument("--clocks-csv", default=None,
                     help="keep the nvidia-smi clock samples in this file ({rank} is replaced; default: a temp file)")
     return ap.parse_args()
@@ -350,7 +360,7 @@ class OracleSampler:
     them, ``b`` the dense compositing per pixel); Adam is timed on a row slice
     and scaled by rows."""
 
-    def __init__(self, wl_name: str, pix_small: int = 8, pix_large: int = 40, adam_rows: int = 100_000):
+    def __init__(self, wl_name: str, pix_small: int = 8, pix_large: int = 72, adam_rows: int = 100_000):
         from mlx_gsplat_b200 import synthetic
         from oracle import rendering as orend
         self.threads = os.cpu_count() or 1
@@ -522,6 +532,66 @@ def pair_counts(frames, dev) -> float:
     return float(cnt.item()) / max(n, 1)
 
 
+def train_run(args, runner, targets_dev, n_tgt, view_of, world, rank, dev, clocks):
+    """A whole training run with the trainer's schedule (mlx_gsplat/trainer.py:416-425):
+    every step a train step, the opacity reset every 1000 (3000) steps, a density
+    step every ``refine_every`` steps inside the densify window.  Timed end to
+    end with CUDA events (density steps, with their host count read-backs,
+    included); one JSON line."""
+    import torch.distributed as dist
+    from mlx_gsplat_b200 import _lib
+    S = args.train_run
+    runner.cfg.max_steps = S
+    interval = 1000 if S <= 3000 else 3000
+    d0 = 300 if S <= 3000 else 500
+    d1 = 15000 if S >= 30000 else int(S * 0.7)
+    lib = _lib.load()
+    for w in range(args.warmup):  # warm-up on a copy-free path: steps of the first view, then restart the count
+        runner.train_step(view_of(0), 1, target=targets_dev[view_of(0) % n_tgt])
+    runner.allocator.grad2d.zero_()
+    runner.allocator.count.zero_()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    launches0 = lib.gs_kernel_launches()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    t_start = time.time()
+    e0.record()
+    dens = []
+    for step in range(1, S + 1):
+        runner.train_step(view_of(step), step, target=targets_dev[view_of(step) % n_tgt])
+        if step % interval == 0:
+            runner.allocator.reset_opacities(-4.59)
+        if d0 <= step <= d1 and step % runner.cfg.refine_every == 0:
+            t0 = time.perf_counter()
+            n_p, n_s = runner.densify(step)
+            dens.append({"step": step, "pruned": n_p, "refined": n_s, "active": runner.allocator.num_active,
+                         "host_ms": (time.perf_counter() - t0) * 1e3})
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t_end = time.time()
+    barrier(world)
+    clk = clocks.stop(t_start, t_end)
+    runner.check_group()
+    ms = e0.elapsed_time(e1) / S
+    ms_max = max_over_ranks(ms, world)
+    if rank == 0:
+        from mlx_gsplat_b200 import synthetic
+        wl = synthetic.WORKLOADS[args.workload]
+        line = {"metric": f"train steps/s over a {S}-step run incl. densify/prune @ {args.workload}",
+                "value": world * 1000.0 / ms_max, "unit": "train steps/s", "n_gpus": world, "steps": S,
+                "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, world),
+                "pool_slots": runner.allocator.max_gaussians, "density_steps": len(dens),
+                "density_host_ms_mean": float(np.mean([d["host_ms"] for d in dens])) if dens else None,
+                "active_first_last": [dens[0]["active"], dens[-1]["active"]] if dens else None,
+                "densify": dens, "clocks": clk, "gpu_launches": int(lib.gs_kernel_launches() - launches0)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     args = parse()
@@ -545,8 +615,13 @@ def main():
     runner = runner_for_workload(args.workload, max_steps=10_000, device=dev, upload_targets=False, lr=1.6e-4,
                                  eps=1e-15, n=args.gaussians, num_views=nv,
                                  max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2),
-                                 process_group=pg, fused_reduce=args.multicast)
-    targets_host = torch.from_numpy(synthetic.make_uint8_targets(wl, nv, seed=1)).pin_memory()
+                                 process_group=pg, fused_reduce=args.multicast,
+                                 allreduce_buckets=args.allreduce_buckets)
+    # the targets: seeded uint8 images, one per view up to ~1 GB of pinned host memory
+    # per process, cycled over the views beyond that (the large scene's 512 3840x2160
+    # targets alone would take 12.7 GB per process)
+    n_tgt = args.target_images or max(1, min(nv, int(1e9 // (wl.pixels * 3))))
+    targets_host = torch.from_numpy(synthetic.make_uint8_targets(wl, n_tgt, seed=1)).pin_memory()
     targets_dev = targets_host.to(dev)
     L = runner.layout
     P = wl.pixels
@@ -556,11 +631,13 @@ def main():
         return (rank + world * step) % nv
 
     clocks = ClockSampler(local, args.clocks_csv.format(rank=local) if args.clocks_csv else None)
+    if args.train_run:
+        return train_run(args, runner, targets_dev, n_tgt, view_of, world, rank, dev, clocks)
     clocks.start()
     step = 0
     for _ in range(args.warmup):
         step += 1
-        runner.train_step(view_of(step), step, target=targets_dev[view_of(step)])
+        runner.train_step(view_of(step), step, target=targets_dev[view_of(step) % n_tgt])
     torch.cuda.synchronize(dev)
 
     # ---- timed region: inputs resident in HBM
@@ -574,14 +651,12 @@ def main():
     e1 = torch.cuda.Event(enable_timing=True)
     t_start = time.time()
     e0.record()
-    frames = []
     for _ in range(args.steps):
         step += 1
         tm = StepTimer()
-        f = runner.train_step(view_of(step), step, target=targets_dev[view_of(step)], timer=tm)
+        f = runner.train_step(view_of(step), step, target=targets_dev[view_of(step) % n_tgt], timer=tm)
         timers.append(tm)
         stats.append((f.V, f.K))
-        frames = (frames + [f])[-4:]  # the last steps' frames, for the pair count after the timed region
     e1.record()
     torch.cuda.synchronize(dev)
     t_end = time.time()
@@ -623,7 +698,13 @@ def main():
                         "traffic": measured_traffic("adam", args.workload) if full_size else None}
     # compute roofline of the compositing kernels: contributing (pixel, splat) pairs
     # times the fp32 operations per pair, against the measured fp32 throughput
-    pairs = pair_counts(frames, dev)
+    # (on four more steps' frames, after the timed region)
+    pairs = 0.0
+    for _ in range(4):
+        step += 1
+        f = runner.train_step(view_of(step), step, target=targets_dev[view_of(step) % n_tgt])
+        pairs += pair_counts([f], dev) / 4
+        del f
     fp = fp32_peak(dev)
     comp = {"pairs_per_view": pairs, "peak_tflops": fp["tflops"], "peak_by_form_tflops": fp["by_form_tflops"],
             "peak_how": fp["how"], "flops_per_pair": {"render_fwd": FWD_FLOPS_PER_PAIR,
@@ -649,7 +730,7 @@ def main():
             out = []
             for i in range(k):
                 step += 1
-                stage.copy_(targets_host[view_of(step)], non_blocking=True)
+                stage.copy_(targets_host[view_of(step) % n_tgt], non_blocking=True)
                 runner.train_step(view_of(step), step, target=stage)
                 slot = i % 2
                 if i >= 2:
@@ -679,25 +760,34 @@ def main():
         e2e = {"value": world * 1000.0 / ms_e2e, "unit": "train steps/s", "ms_per_step": ms_e2e,
                "h2d_bytes_per_step": int(stage.numel()), "d2h_bytes_per_step": 4}
 
-    # ---- one densify/prune step on this scene (all ranks: the statistics are all-reduced)
+    # ---- three densify/prune steps on this scene, two training steps apart (all ranks:
+    # the statistics are all-reduced); the first also allocates the density-step workspace
     densify_ms = None
     if not args.no_extras:
         al = runner.allocator
-        # statistics with mean 1e-4: about e^-2 = 13.5% of the Gaussians exceed the 2e-4 threshold
+        rounds = []
         gen = torch.Generator(device=dev)
         gen.manual_seed(5)
-        al.grad2d.exponential_(1e4, generator=gen)
-        al.count.fill_(1.0)
-        barrier(world)
-        torch.cuda.synchronize(dev)
-        t0 = time.perf_counter()
         try:
-            n_p, n_s = runner.densify(step + 1)
-            torch.cuda.synchronize(dev)
-            densify_ms = {"ms": (time.perf_counter() - t0) * 1e3, "pruned": n_p, "refined": n_s,
-                          "active_after": al.num_active, "note": "wall clock incl. host count read-backs"}
+            for rnd in range(3):
+                for _ in range(2):
+                    step += 1
+                    runner.train_step(view_of(step), step, target=targets_dev[view_of(step) % n_tgt])
+                # statistics with mean 1e-4: about e^-2 = 13.5% of the Gaussians exceed the 2e-4 threshold
+                al.grad2d.exponential_(1e4, generator=gen)
+                al.count.fill_(1.0)
+                barrier(world)
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                n_p, n_s = runner.densify(step + 1)
+                torch.cuda.synchronize(dev)
+                rounds.append({"ms": (time.perf_counter() - t0) * 1e3, "pruned": n_p, "refined": n_s,
+                               "active_after": al.num_active})
+            densify_ms = {"rounds": rounds, "ms_after_first": float(np.mean([r["ms"] for r in rounds[1:]])),
+                          "note": "wall clock incl. the host count read-back; the first round allocates the "
+                                  "density-step workspace"}
         except MemoryError as e:
-            densify_ms = {"error": str(e)}
+            densify_ms = {"error": str(e), "rounds": rounds}
 
     # ---- the large workload's standalone fused Adam: 6M rows x 59 columns, theta/m/v/g
     # ---- the reference trainer's L1 + D-SSIM image loss (forward + gradient) on this image size

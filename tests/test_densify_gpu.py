@@ -28,6 +28,7 @@ def snapshot(al) -> oalloc.PoolOracle:
     o.free_slots = al.free_slots
     o.grad2d = al.grad2d.cpu().numpy().copy()
     o.count = al.count.cpu().numpy().copy()
+    o.active_mask = al.active_mask.cpu().numpy().astype(np.int8).copy()
     return o
 
 
@@ -182,3 +183,52 @@ def test_opacity_reset_sets_every_slot():
     r.train(log_every=0)
     op = r.allocator.physical_pools["opacities"].cpu().numpy()
     np.testing.assert_array_equal(op, np.full_like(op, np.float32(-4.59)))
+
+
+def test_stress_run_3000_steps_every_round_checked():
+    """The densify/prune stress workload as specified: 300,000 Gaussians in the
+    4,000,000-slot pool at 1920x1080, 3,000 training steps with the trainer's
+    schedule (mlx_gsplat/trainer.py:416-425: opacity reset every 1000 steps,
+    a density step every 100 steps from 300 to 2100).  Every round's decisions
+    (prune, clone/split, split masks) are compared bit for bit with the oracle
+    given the GPU's statistics; three rounds (the first, one in the middle, the
+    last) are checked in full: children, pool rows, moments, table, free list
+    and active mask."""
+    r = runner_for_workload("densify-4m", max_steps=3000, num_views=32)
+    al = r.allocator
+    assert al.max_gaussians == 4_000_000 and al.num_active == 300_000
+    full = {300, 1200, 2100}
+    rounds = 0
+    L = al.layout
+    for step in range(1, 3001):
+        r.train_step((step - 1) % 32, step)
+        if step % odens.opacity_reset_interval(3000) == 0:
+            al.reset_opacities(-4.59)
+        if not odens.is_densify_step(step, 3000):
+            continue
+        torch.cuda.synchronize()
+        N = al.num_active
+        table = al.indirection_table.cpu().numpy()
+        th = al.theta.cpu().numpy()[table]
+        act = {k: th[:, o:o + L.dims[k]] for k, o in L.offsets.items()}
+        g2, cnt = al.grad2d.cpu().numpy()[table], al.count.cpu().numpy()[table]
+        o = snapshot(al) if step in full else None
+        n_p, n_s = r.densify(step)
+        torch.cuda.synchronize()
+        refine, split, prune = odens.densify_masks(g2, cnt, act["scales"], act["opacities"], act["means"],
+                                                   act["quats"], r.scene_scale, N)
+        flags = r.last_densify["flags"].cpu().numpy()
+        np.testing.assert_array_equal((flags & 1) != 0, prune, err_msg=f"step {step} prune")
+        np.testing.assert_array_equal((flags & 2) != 0, refine, err_msg=f"step {step} refine")
+        np.testing.assert_array_equal((flags & 4) != 0, split, err_msg=f"step {step} split")
+        assert (n_p, n_s) == (int(prune.sum()), int(refine.sum())), f"step {step}"
+        if o is not None:
+            nz = {k: v[:n_s].cpu().numpy() for k, v in r.last_densify["noise"].items()}
+            oa = {k: o.active(k) for k in o.pools}
+            sp = odens.child_params(oa, refine, split, nz["means1"], nz["means2"], nz["quats2"])
+            assert o.split_and_prune(prune, refine, sp) == (n_p, n_s)
+            assert_same(al, o, f"step {step}")
+            np.testing.assert_array_equal(al.active_mask.cpu().numpy(), o.active_mask, err_msg=f"step {step} mask")
+        rounds += 1
+    assert rounds == 19
+    assert al.num_active > 300_000
