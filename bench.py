@@ -93,6 +93,9 @@ def parse():
                     help="instead of the step benchmark, time a whole training run of this many steps with the "
                          "trainer's schedule (density steps every 100 steps in its window, opacity resets) and "
                          "report its steps/s")
+    ap.add_argument("--densify-fraction", type=float, default=0.0,
+                    help="--train-run stress knob: before each density step scale the accumulated statistics so "
+                         "that this fraction of the Gaussians crosses the 2e-4 threshold (default: as trained)")
     ap.add_argument("--clocks-csv", default=None,
                     help="keep the nvidia-smi clock samples in this file ({rank} is replaced; default: a temp file)")
     return ap.parse_args()
@@ -564,6 +567,8 @@ def train_run(args, runner, targets_dev, n_tgt, view_of, world, rank, dev, clock
         if step % interval == 0:
             runner.allocator.reset_opacities(-4.59)
         if d0 <= step <= d1 and step % runner.cfg.refine_every == 0:
+            if args.densify_fraction > 0:
+                runner.scale_densify_stats(args.densify_fraction)
             t0 = time.perf_counter()
             n_p, n_s = runner.densify(step)
             dens.append({"step": step, "pruned": n_p, "refined": n_s, "active": runner.allocator.num_active,
@@ -580,6 +585,7 @@ def train_run(args, runner, targets_dev, n_tgt, view_of, world, rank, dev, clock
         from mlx_gsplat_b200 import synthetic
         wl = synthetic.WORKLOADS[args.workload]
         line = {"metric": f"train steps/s over a {S}-step run incl. densify/prune @ {args.workload}",
+                "densify_fraction": args.densify_fraction or "as trained",
                 "value": world * 1000.0 / ms_max, "unit": "train steps/s", "n_gpus": world, "steps": S,
                 "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(args, world),

@@ -541,6 +541,22 @@ class RunnerMLX:
         al.count.zero_()
         return n_p, n_s
 
+    def scale_densify_stats(self, fraction: float, threshold: float = 0.0002) -> float:
+        """Stress knob for the density step (not part of the reference's
+        schedule): scales the accumulated view-space gradients so that the
+        ``fraction`` of active Gaussians with the largest average statistic
+        exceed ``threshold``; returns the factor.  Large renders give small
+        per-pixel gradients, whose statistics may never reach the reference's
+        2e-4 otherwise."""
+        al = self.allocator
+        t = al.indirection_table.long()
+        avg = al.grad2d[t] / al.count[t].clamp(min=1.0)
+        q = float(torch.quantile(avg.float(), 1.0 - fraction)) if avg.numel() <= (1 << 24) else \
+            float(avg.kthvalue(max(1, int(avg.numel() * (1.0 - fraction)))).values)
+        factor = threshold / q * 1.0001 if q > 0 else 1.0
+        al.grad2d.mul_(factor)
+        return factor
+
     def _l1_dssim(self, frame, target: torch.Tensor) -> torch.Tensor:
         """The reference trainer's image loss 0.8 * L1 + 0.2 * (1 - SSIM) / 2
         (trainer.py:276-279) of the rendered frame; returns dL/dC (HWC) and

@@ -193,11 +193,15 @@ def test_stress_run_3000_steps_every_round_checked():
     (prune, clone/split, split masks) are compared bit for bit with the oracle
     given the GPU's statistics; three rounds (the first, one in the middle, the
     last) are checked in full: children, pool rows, moments, table, free list
-    and active mask."""
+    and active mask.  At 1920x1080 the per-pixel loss gradient is small and no
+    Gaussian's statistic reaches the 2e-4 threshold in training, so before the
+    middle and last full rounds the statistics are scaled (the same values go
+    to the oracle) so that the top 5% cross it and the split/clone path runs."""
     r = runner_for_workload("densify-4m", max_steps=3000, num_views=32)
     al = r.allocator
     assert al.max_gaussians == 4_000_000 and al.num_active == 300_000
     full = {300, 1200, 2100}
+    scaled = {1200, 2100}
     rounds = 0
     L = al.layout
     for step in range(1, 3001):
@@ -206,6 +210,8 @@ def test_stress_run_3000_steps_every_round_checked():
             al.reset_opacities(-4.59)
         if not odens.is_densify_step(step, 3000):
             continue
+        if step in scaled:
+            r.scale_densify_stats(0.05)
         torch.cuda.synchronize()
         N = al.num_active
         table = al.indirection_table.cpu().numpy()
@@ -222,13 +228,16 @@ def test_stress_run_3000_steps_every_round_checked():
         np.testing.assert_array_equal((flags & 2) != 0, refine, err_msg=f"step {step} refine")
         np.testing.assert_array_equal((flags & 4) != 0, split, err_msg=f"step {step} split")
         assert (n_p, n_s) == (int(prune.sum()), int(refine.sum())), f"step {step}"
-        if o is not None:
+        assert n_s > 0 if step in scaled else n_s == 0
+        if o is not None and n_s > 0:
             nz = {k: v[:n_s].cpu().numpy() for k, v in r.last_densify["noise"].items()}
             oa = {k: o.active(k) for k in o.pools}
             sp = odens.child_params(oa, refine, split, nz["means1"], nz["means2"], nz["quats2"])
             assert o.split_and_prune(prune, refine, sp) == (n_p, n_s)
             assert_same(al, o, f"step {step}")
             np.testing.assert_array_equal(al.active_mask.cpu().numpy(), o.active_mask, err_msg=f"step {step} mask")
+        elif o is not None:
+            assert_same(al, o, f"step {step} (no change)")
         rounds += 1
     assert rounds == 19
     assert al.num_active > 300_000
