@@ -130,12 +130,18 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int, path: str = None):
-        self.gpu = gpu_index
+    def __init__(self, gpu_indices, path: str = None, period_ms: int = 100):
+        """One nvidia-smi poller for the GPUs ``gpu_indices`` (local rank 0 samples
+        every GPU of the job; the other ranks sample nothing)."""
+        self.gpus = list(gpu_indices)
+        self.gpu = self.gpus[0] if self.gpus else 0
+        self.period_ms = period_ms
         self.proc = None
         self.path = path
 
     def start(self):
+        if not self.gpus:
+            return
         try:
             if self.path is None:
                 import tempfile
@@ -144,15 +150,17 @@ class ClockSampler:
             else:
                 os.makedirs(os.path.dirname(os.path.abspath(self.path)), exist_ok=True)
             self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
-                                         stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", ",".join(str(g) for g in self.gpus),
+                                          f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                                          str(self.period_ms)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
     def stop(self, t0: float = None, t1: float = None):
         """Median SM clock and the active throttle reasons over the samples taken
         between host times t0 and t1 (the timed region)."""
+        if not self.gpus:
+            return None
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -183,7 +191,8 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_median": float(np.median(power)) if power else None}
+                "samples": len(sm), "gpus": self.gpus,
+                "power_w_median": float(np.median(power)) if power else None}
 
 
 # ----------------------------------------------------------------------------- byte model
@@ -636,7 +645,9 @@ def main():
     def view_of(step):
         return (rank + world * step) % nv
 
-    clocks = ClockSampler(local, args.clocks_csv.format(rank=local) if args.clocks_csv else None)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    clocks = ClockSampler(range(local_world) if local == 0 else [],
+                          args.clocks_csv.format(rank=local) if args.clocks_csv else None)
     if args.train_run:
         return train_run(args, runner, targets_dev, n_tgt, view_of, world, rank, dev, clocks)
     clocks.start()
