@@ -116,6 +116,8 @@ typedef struct gs_camera {
 typedef struct gs_raster_settings {
     float alpha_cutoff;      /* e.g. 1e-7 (the default: parity with the dense reference to ~1e-6) */
     float transmittance_min; /* e.g. 1e-6 (parity) */
+    int32_t alpha_mask;      /* 1: the compositing kernels multiply each splat's clipped alpha by the
+                                multiplier gs_apply_sorted_mask stored in its record; 0 (default): none */
 } gs_raster_settings;
 
 /* Per-tile [start, end) ranges into the tile-sorted entry list. */
@@ -322,6 +324,19 @@ int gs_render_forward(const gs_tile_range* ranges, const int32_t* tile_order, co
                       int64_t num_visible, const gs_camera* cam, const gs_raster_settings* rs, float* out_color, float* out_alpha,
                       float* final_T, int32_t* n_contrib, int loss_mode, const void* target, float* loss_partials,
                       gs_stream_t stream);
+
+/* The rasterizer's optional per-Gaussian alpha mask (mlx_gsplat/rendering.py:289-290:
+ * alpha = clip(opacity * g, 0, 0.99) * mask[j]).  As in the reference, mask[j]
+ * belongs to the j-th visible Gaussian in depth order (the reference applies it
+ * after its depth argsort without permuting it), so ``order`` is the depth
+ * sort's permutation (order[j] = visible index of depth rank j, from
+ * gs_radix_sort_pairs on the depth keys).  Writes the multiplier (clamped to
+ * [0, 1]: binning bounds a splat's reach by its unmasked opacity) into the last
+ * float of each splat record and tightens the record's contribution cut to
+ * opacity * mask.  Call it after the depth sort and before the compositing
+ * kernels, which then need gs_raster_settings.alpha_mask = 1. */
+int gs_apply_sorted_mask(float* splats, const int32_t* order, const float* mask, int64_t num_visible,
+                         const gs_raster_settings* rs, gs_stream_t stream);
 
 /* Diagnostic (no reference counterpart): the number of (pixel, splat) pairs
  * that take part in the compositing of one view — alpha >= alpha_cutoff

@@ -53,7 +53,7 @@ class GsCamera(ctypes.Structure):
 
 
 class GsRasterSettings(ctypes.Structure):
-    _fields_ = [("alpha_cutoff", ctypes.c_float), ("transmittance_min", ctypes.c_float)]
+    _fields_ = [("alpha_cutoff", ctypes.c_float), ("transmittance_min", ctypes.c_float), ("alpha_mask", i32)]
 
 
 _SIGS = {
@@ -96,6 +96,7 @@ _SIGS = {
                                              ctypes.POINTER(GsRasterSettings), c_vp, c_vp]),
     "gs_fp32_peak_probe": (ctypes.c_int, [c_vp, i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_double), c_vp]),
+    "gs_apply_sorted_mask": (ctypes.c_int, [c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsRasterSettings), c_vp]),
     "gs_render_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, i64, ctypes.POINTER(GsCamera),
                                           ctypes.POINTER(GsRasterSettings), c_vp, c_vp, c_vp, ctypes.c_int, c_vp,
                                           c_vp, c_vp, c_vp, c_vp]),

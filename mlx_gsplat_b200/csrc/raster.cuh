@@ -18,6 +18,7 @@ struct RasterParams {
     int rw, rh, tiles_x, tiles_y;
     float alpha_cut, t_min;
     float loss_scale;  // 1 / (3 * rw * rh) for the mean-based losses
+    int masked;        // the splat records carry an alpha multiplier (gs_apply_sorted_mask)
 };
 
 inline RasterParams make_raster_params(const gs_camera& c, const gs_raster_settings* rs) {
@@ -41,6 +42,7 @@ inline RasterParams make_raster_params(const gs_camera& c, const gs_raster_setti
     p.alpha_cut = rs ? rs->alpha_cutoff : 1e-7f;
     p.t_min = rs ? rs->transmittance_min : 1e-6f;
     p.loss_scale = (float)(1.0 / (3.0 * (double)c.render_width * (double)c.render_height));
+    p.masked = rs ? (rs->alpha_mask != 0) : 0;
     return p;
 }
 

@@ -136,17 +136,23 @@ __device__ __forceinline__ void pair_bwd_accum(PairBwd<kDA>& s, float2 al, float
     syy = __ffma2_rn(t, y, syy);
 }
 
-// General form: the last-entry test, the 0.99 clip and its gradient mask.
-template <bool kDA>
+// General form: the 0.99 clip and its gradient mask; with kMask the clipped
+// alpha, and with it the gradient through the clip, is scaled by the splat's
+// mask multiplier ``mk`` (alpha = clip(opacity g, 0, 0.99) * mk).
+template <bool kDA, bool kMask = false>
 __device__ __forceinline__ void pair_bwd_step(PairBwd<kDA>& s, bool v0, bool v1, float2 m, float2 y,
                                               const SplatBwd& c, float2& sd, float2& sy, float2& syy, float2& sr,
-                                              float2& sg, float2& sb) {
+                                              float2& sg, float2& sb, float mk = 1.f) {
     const float2 gv = pair_falloff(m);
     const float2 og = __fmul2_rn(f2(c.opac), gv);
-    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+    float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
     // the clip of opacity * g to [0, 0.99] passes the gradient strictly inside
     // (opacity * g > 0 holds for every pixel that takes part: m <= the pair cut)
-    const float2 gi = make_float2(v0 && og.x < 0.99f ? gv.x : 0.f, v1 && og.y < 0.99f ? gv.y : 0.f);
+    float2 gi = make_float2(v0 && og.x < 0.99f ? gv.x : 0.f, v1 && og.y < 0.99f ? gv.y : 0.f);
+    if constexpr (kMask) {
+        al = __fmul2_rn(al, f2(mk));
+        gi = __fmul2_rn(gi, f2(mk));
+    }
     pair_bwd_accum<kDA>(s, al, gi, y, c, sd, sy, syy, sr, sg, sb);
 }
 
@@ -167,7 +173,7 @@ __device__ __forceinline__ void pair_bwd_step_fast(PairBwd<kDA>& s, bool v0, boo
 #else
 #define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads)
 #endif
-template <bool kDA>
+template <bool kDA, bool kMask>
 __global__ void GS_BWD_BOUNDS render_bwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
@@ -231,9 +237,11 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             sv[j] = vi;
             const float4 a = splats[3 * vi], b = splats[3 * vi + 1];
             float4 c = splats[3 * vi + 2];
-            // .w (the depth, unused here) becomes the fast-form flag of the splat
+            // .w (the depth, unused here) becomes the fast-form flag of the splat;
+            // with an alpha mask it keeps the mask multiplier (general form only)
             const float sym = 0.5f * (a.w + b.x);
-            c.w = (b.z < 0.98f && a.z > 0.f && b.y > 0.f && a.z * b.y - sym * sym > 0.f) ? 1.f : 0.f;
+            if constexpr (!kMask)
+                c.w = (b.z < 0.98f && a.z > 0.f && b.y > 0.f && a.z * b.y - sym * sym > 0.f) ? 1.f : 0.f;
             s0[j] = a;
             s1[j] = b;
             s2[j] = c;
@@ -260,7 +268,7 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
             const int k = 32 * i + hb;
             const int idx = bstart + k - rg.start;
             const float4 q0 = s0[k], q1 = s1[k], q2 = s2[k];
-            const bool fast = q2.w != 0.f;  // uniform over the warp
+            const bool fast = !kMask && q2.w != 0.f;  // uniform over the warp
             const float x = px - q0.x;
             const float ax = q0.z * x, cx = q1.x * x;
             float2 y[kPairs], m[kPairs];
@@ -298,7 +306,7 @@ __global__ void GS_BWD_BOUNDS render_bwd_kernel(
 #pragma unroll
                 for (int q = 0; q < kPairs; ++q) {
                     if (!__any_sync(kFull, v0[q] | v1[q])) continue;
-                    pair_bwd_step<kDA>(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb);
+                    pair_bwd_step<kDA, kMask>(s[q], v0[q], v1[q], m[q], y[q], c, sd, sy, syy, sr, sg, sb, q2.w);
                 }
             }
             float g[9];
@@ -634,7 +642,9 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const int32_t* ti
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
     // the alpha cotangent is carried per pixel only when the caller passes one
-    auto kernel = (loss_mode == GS_LOSS_NONE && dL_dalpha) ? render_bwd_kernel<true> : render_bwd_kernel<false>;
+    const bool da = loss_mode == GS_LOSS_NONE && dL_dalpha;
+    auto kernel = p.masked ? (da ? render_bwd_kernel<true, true> : render_bwd_kernel<false, true>)
+                           : (da ? render_bwd_kernel<true, false> : render_bwd_kernel<false, false>);
     kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T,
         n_contrib, loss_mode, target, dL_dcolor, dL_dalpha, splat_grads);

@@ -502,7 +502,9 @@ __device__ __forceinline__ float pixel_loss(int loss_mode, const void* target, i
 // kCount: the same compositing, but instead of writing the image it adds the
 // number of (pixel, splat) pairs that took part to *pairs (a diagnostic of the
 // work the compositing kernels do; not on the training path).
-template <bool kCount>
+// kMask: each splat's clipped alpha is multiplied by the last float of its
+// record (gs_apply_sorted_mask; mlx_gsplat/rendering.py:289-290).
+template <bool kCount, bool kMask>
 __global__ void GS_FWD_BOUNDS render_fwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, float* __restrict__ out_color, float* __restrict__ out_alpha, float* __restrict__ final_T,
@@ -589,7 +591,8 @@ __global__ void GS_FWD_BOUNDS render_fwd_kernel(
                     const float2 m = pair_quad(__fadd2_rn(py[q], f2(-q0.y)), x, ax, cx, q0.w, q1.y);
                     const float2 og = __fmul2_rn(f2(q1.z), pair_falloff(m));
                     const bool v0 = T[q].x >= t_min && m.x <= q2.z, v1 = T[q].y >= t_min && m.y <= q2.z;
-                    const float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+                    float2 al = make_float2(v0 ? fminf(og.x, 0.99f) : 0.f, v1 ? fminf(og.y, 0.99f) : 0.f);
+                    if constexpr (kMask) al = __fmul2_rn(al, f2(q2.w));
                     const float2 w = __fmul2_rn(al, T[q]);
                     cr[q] = __ffma2_rn(w, f2(q1.w), cr[q]);
                     cg[q] = __ffma2_rn(w, f2(q2.x), cg[q]);
@@ -755,7 +758,8 @@ extern "C" int gs_render_forward(const gs_tile_range* ranges, const int32_t* til
     GS_REQUIRE(loss_mode == GS_LOSS_NONE || loss_mode == GS_LOSS_MEAN || target, "render_forward: target required");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_fwd_kernel<false><<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+    auto kernel = p.masked ? render_fwd_kernel<false, true> : render_fwd_kernel<false, false>;
+    kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, out_alpha,
         final_T, n_contrib, loss_mode, target, loss_partials, nullptr);
     return check_launch("render_fwd_kernel");
@@ -770,8 +774,39 @@ extern "C" int gs_render_pair_count(const gs_tile_range* ranges, const int32_t* 
     GS_REQUIRE(!rs || rs->transmittance_min <= 1.f, "render_pair_count: transmittance_min must be <= 1");
     const RasterParams p = make_raster_params(*cam, rs);
     const int tiles = p.tiles_x * p.tiles_y;
-    render_fwd_kernel<true><<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+    auto kernel = p.masked ? render_fwd_kernel<true, true> : render_fwd_kernel<true, false>;
+    kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, nullptr, nullptr,
         nullptr, nullptr, GS_LOSS_NONE, nullptr, nullptr, pairs);
     return check_launch("render_fwd_kernel<count>");
+}
+
+// Record r of depth rank j (r = order[j]) gets mask[j] (clamped to [0, 1]) as
+// its alpha multiplier and the contribution cut of opacity * mask.
+__global__ void apply_sorted_mask_kernel(float4* __restrict__ splats, const int32_t* __restrict__ order,
+                                         const float* __restrict__ mask, int64_t nv, RasterParams p) {
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= nv) return;
+    const int32_t r = order[j];
+    if (r < 0 || r >= nv) return;
+    const float mk = fminf(fmaxf(mask[j], 0.f), 1.f);
+    const float opac = splats[3 * r + 1].z;
+    float4 c = splats[3 * r + 2];
+    c.z = pair_cut(opac * mk, p);
+    c.w = mk;
+    splats[3 * r + 2] = c;
+}
+
+extern "C" int gs_apply_sorted_mask(float* splats, const int32_t* order, const float* mask, int64_t num_visible,
+                                    const gs_raster_settings* rs, gs_stream_t stream) {
+    GS_REQUIRE(num_visible >= 0, "apply_sorted_mask: negative count");
+    if (num_visible == 0) return GS_OK;
+    GS_REQUIRE(splats && order && mask, "apply_sorted_mask: null pointer");
+    GS_REQUIRE(aligned16(splats), "apply_sorted_mask: splats must be 16-byte aligned");
+    gs_camera cam = {};
+    cam.width = cam.height = cam.render_width = cam.render_height = 1;
+    const RasterParams p = make_raster_params(cam, rs);  // only the cutoff is used
+    apply_sorted_mask_kernel<<<grid_for(num_visible, 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<float4*>(splats), order, mask, num_visible, p);
+    return check_launch("apply_sorted_mask_kernel");
 }

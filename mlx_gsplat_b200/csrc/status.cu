@@ -19,5 +19,5 @@ int set_error(int code, const char* fmt, ...) {
 }  // namespace gs
 
 extern "C" const char* gs_last_error(void) { return gs::g_msg; }
-extern "C" int gs_abi_version(void) { return 2; }
+extern "C" int gs_abi_version(void) { return 3; }
 extern "C" unsigned long long gs_kernel_launches(void) { return gs::g_launches.load(std::memory_order_relaxed); }

@@ -40,8 +40,8 @@ class RasterSettings:
     alpha_cutoff: float = 1e-7
     transmittance_min: float = 1e-6
 
-    def cstruct(self) -> GsRasterSettings:
-        return GsRasterSettings(self.alpha_cutoff, self.transmittance_min)
+    def cstruct(self, alpha_mask: bool = False) -> GsRasterSettings:
+        return GsRasterSettings(self.alpha_cutoff, self.transmittance_min, int(alpha_mask))
 
 
 DEFAULT_SETTINGS = RasterSettings()
@@ -206,16 +206,18 @@ class TileFrame:
 def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, settings: RasterSettings,
                    device, loss_mode: int = _lib.GS_LOSS_NONE, target: Optional[torch.Tensor] = None,
                    out_color: Optional[torch.Tensor] = None, timer=None, v_count: Optional[torch.Tensor] = None,
-                   k_hint: int = 0) -> TileFrame:
+                   k_hint: int = 0, mask: Optional[torch.Tensor] = None) -> TileFrame:
     """The forward of one view.  With ``v_count`` (the cull's device count, not
     yet read back) ``V`` is an upper bound of the visible count: every
     per-view buffer is allocated before the count is read, and the tile-entry
     buffers before the entry count is read (``k_hint`` entries, enlarged only
     when a view has more), so the host goes from each read-back straight to
-    the next kernel launch."""
+    the next kernel launch.  ``mask`` (float32 [V] in [0, 1], device): the
+    reference's alpha mask, entry j multiplying the clipped alpha of the j-th
+    visible Gaussian in depth order (mlx_gsplat/rendering.py:289-290)."""
     lib = _lib.lib()
     st = _lib.stream_ptr(device)
-    rs = settings.cstruct()
+    rs = settings.cstruct(alpha_mask=mask is not None)
     RW, RH = cam.render_width, cam.render_height
     tx, ty = num_tiles(RW, RH)
     T = tx * ty
@@ -247,6 +249,9 @@ def render_forward(g: GsGaussians, ids: torch.Tensor, V: int, cam: GsCamera, set
             timer.mark("project_fwd")
         check(lib.gs_radix_sort_pairs(depth_keys.data_ptr(), None, keys_sorted.data_ptr(),
                                       order.data_ptr(), V, 0, 32, sb.data_ptr(), sb.numel(), st), "depth sort")
+        if mask is not None:
+            check(lib.gs_apply_sorted_mask(f.splats.data_ptr(), order.data_ptr(), mask.data_ptr(), V, rs, st),
+                  "gs_apply_sorted_mask")
         check(lib.gs_bin_offsets(order.data_ptr(), tile_counts.data_ptr(), V, offsets.data_ptr(), ob.data_ptr(),
                                  ob.numel(), st), "gs_bin_offsets")
         if timer:
@@ -324,12 +329,13 @@ def render_backward(f: TileFrame, g: GsGaussians, out: GsGaussianGrads, device,
 # ----------------------------------------------------------------------------- autograd entry
 class _RasterizeFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, means, quats, scales, opacities, colors, ids, cam, settings, colors_by_visible, sh_mode):
+    def forward(ctx, means, quats, scales, opacities, colors, ids, cam, settings, colors_by_visible, sh_mode,
+                mask=None):
         device = means.device
         g = gaussians_struct(means, quats, scales, opacities, colors, colors_by_visible=colors_by_visible,
                              sh_mode=sh_mode)
         V = int(ids.shape[0])
-        f = render_forward(g, ids, V, cam, settings, device)
+        f = render_forward(g, ids, V, cam, settings, device, mask=mask)
         ctx.frame = f
         ctx.g = g
         ctx.colors_by_visible = colors_by_visible
@@ -351,7 +357,7 @@ class _RasterizeFn(torch.autograd.Function):
         dC = torch.zeros_like(ctx.frame.color) if dC is None else dC.contiguous()
         dA = None if dA is None else dA.contiguous()
         render_backward(ctx.frame, ctx.g, out, device, dL_dcolor=dC, dL_dalpha=dA)
-        return gm, gq, gsc, go, gc, None, None, None, None, None
+        return gm, gq, gsc, go, gc, None, None, None, None, None, None
 
 
 def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K, width: int, height: int,
@@ -366,13 +372,14 @@ def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K,
     with respect to the five parameter tensors.  ``colors`` is used row per
     visible Gaussian when it has one row per index, otherwise gathered too.
     ``pixel_chunk_size`` is accepted for compatibility (the tiled kernels need
-    no pixel chunking); the per-Gaussian ``mask`` multiplier is not supported.
+    no pixel chunking).  ``mask`` ([V] values in [0, 1]) multiplies clipped
+    alphas as the reference's does: entry j goes to the j-th visible Gaussian in
+    depth order (the reference applies it after its depth sort without
+    permuting it); no gradient flows to it.
     ``sh_mode="full"`` evaluates real spherical harmonics up to the degree the
     colour rows hold (3, 12, 27 or 48 floats: degree 0-3; the reference,
     ``"reference"``, stops at degree 1), with channel ch's coefficients at
     ``colors[:, 3 + k*ch : 3 + k*(ch+1)]``, k = (degree+1)**2 - 1."""
-    if mask is not None:
-        raise NotImplementedError("rasterize_gaussians_mlx: the alpha mask argument is not supported")
     m = means if means_active is None else means_active
     q = quats if quats_active is None else quats_active
     s = scales if scales_active is None else scales_active
@@ -384,5 +391,12 @@ def rasterize_gaussians_mlx(means, quats, scales, opacities, colors, viewmat, K,
                 torch.zeros((render_height, render_width, 1), dtype=torch.float32, device=m.device))
     cam = camera_struct(viewmat, K, width, height, render_width, render_height)
     by_visible = int(colors.shape[0]) == V
+    mk = None
+    if mask is not None:
+        mk = torch.as_tensor(mask, device=m.device).detach().to(torch.float32).reshape(-1).contiguous()
+        if mk.numel() != V:
+            raise ValueError(f"rasterize_gaussians_mlx: mask has {mk.numel()} entries for {V} Gaussians")
+        if bool(((mk < 0) | (mk > 1) | ~torch.isfinite(mk)).any()):
+            raise ValueError("rasterize_gaussians_mlx: mask values must lie in [0, 1]")
     return _RasterizeFn.apply(m, q, s, o, colors, ids, cam, raster_settings or DEFAULT_SETTINGS, by_visible,
-                              sh_mode_code(sh_mode))
+                              sh_mode_code(sh_mode), mk)

@@ -356,7 +356,9 @@ class RunnerMLX:
         # the counts are read back
         frame = render_forward(g, ids, N, cam, self.settings, self.device, loss_mode=loss_mode, target=target,
                                timer=timer, v_count=vcount, k_hint=self._k_hint)
-        self._k_hint = max(self._k_hint, frame.K + frame.K // 8)
+        # 50% headroom: views differ in their entry counts, and a view that exceeds
+        # the hint gets freshly allocated entry buffers
+        self._k_hint = max(self._k_hint, frame.K + frame.K // 2)
         dL_dcolor = self._l1_dssim(frame, target) if ssim_loss else None
         if ssim_loss and timer:
             timer.mark("loss")

@@ -223,7 +223,8 @@ def pixel_centers(width, height, render_width, render_height, dtype) -> torch.Te
 
 
 def composite(pg: Dict[str, torch.Tensor], pix: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """rendering.py:274-300 for one chunk of pixels ``pix [P,2]``."""
+    """rendering.py:274-300 for one chunk of pixels ``pix [P,2]``.  ``pg["mask"]``
+    (optional, depth order) multiplies the clipped alphas (:289-290)."""
     xv = pix[:, None, 0] - pg["u"][None, :]
     yv = pix[:, None, 1] - pg["v"][None, :]
     isx = pg["a"][None, :] * xv + pg["b"][None, :] * yv
@@ -231,6 +232,8 @@ def composite(pg: Dict[str, torch.Tensor], pix: torch.Tensor) -> Tuple[torch.Ten
     mah = xv * isx + yv * isy
     g = torch.exp(-0.5 * mah)
     alpha = _clip(pg["opac"][None, :] * g, 0.0, 0.99)
+    if pg.get("mask") is not None:
+        alpha = alpha * pg["mask"][None, :]
     trans = torch.cumprod(1.0 - alpha, 1)
     T = torch.cat([torch.ones((pix.shape[0], 1), dtype=alpha.dtype), trans[:, :-1]], 1)
     w = alpha * T
@@ -245,14 +248,16 @@ def _as_t(x, dtype):
 
 def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, height,
                     render_width, render_height, dtype=torch.float64, chunk: int = 512,
-                    pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference"):
-    """Forward only.  Inputs are the gathered active rows (numpy or torch).
+                    pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference", mask=None):
+    """Forward only.  Inputs are the gathered active rows (numpy or torch);
+    ``mask`` [V] multiplies the clipped alpha of the j-th Gaussian in depth order.
     Returns ``(colors [H,W,3], alphas [H,W,1])`` as numpy arrays, or
     ``[P,3], [P,1]`` when ``pixel_ids`` selects a subset."""
     with torch.no_grad():
         args = [_as_t(a, dtype) for a in (means, quats, scales, opacities, colors)]
         pg = project(*args, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
                      render_width, render_height, sh_mode=sh_mode)
+        pg["mask"] = None if mask is None else _as_t(mask, dtype).reshape(-1)
         pix = pixel_centers(width, height, render_width, render_height, dtype)
         if pixel_ids is not None:
             pix = pix[torch.as_tensor(np.asarray(pixel_ids, np.int64))]
@@ -276,7 +281,7 @@ def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, 
 def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, width, height,
                         render_width, render_height, dL_dC, dL_dA=None, dtype=torch.float64,
                         chunk: int = 256, pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference",
-                        l1_target=None):
+                        l1_target=None, mask=None):
     """Forward plus vector-Jacobian product of the dense rasterizer.
 
     ``dL_dC``/``dL_dA`` are ``[H,W,3]``/``[H,W,1]`` (or ``[P,3]``/``[P,1]`` for
@@ -285,13 +290,14 @@ def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, wid
     With ``l1_target`` ([H,W,3]) the loss is instead the trainer's
     ``mean(|C - target|)`` (trainer.py:273-275, over all 3 H W values), whose
     gradient is formed chunk by chunk in the same single pass (``dL_dC`` is
-    ignored).
+    ignored).  ``mask`` as in ``rasterize_dense`` (no gradient flows to it).
     """
     leaves = [_as_t(a, dtype).requires_grad_(True) for a in (means, quats, scales, opacities, colors)]
     pg = project(*leaves, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
                  render_width, render_height, sh_mode=sh_mode)
     keys = ["u", "v", "a", "b", "c", "d", "opac", "rgb"]
     det = {k: pg[k].detach().clone().requires_grad_(True) for k in keys}
+    det["mask"] = None if mask is None else _as_t(mask, dtype).reshape(-1)
     acc = {k: torch.zeros_like(det[k]) for k in keys}
     pix = pixel_centers(width, height, render_width, render_height, dtype)
     if pixel_ids is not None:

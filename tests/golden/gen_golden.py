@@ -127,6 +127,51 @@ def gen_raster(R, out):
     np.savez_compressed(os.path.join(out, "raster.npz"), **res)
 
 
+def gen_raster_mask(R, out):
+    """The rasterizer's alpha mask (rendering.py:289-290), one case with
+    colours of SH degree 1: mask values uniform in [0, 1] with a fifth of them
+    exactly 0 and a fifth exactly 1; ``raster_mask.npz``."""
+    W, H, RW, RH, seed = 48, 36, 48, 36, 21
+    wl = synthetic.WORKLOADS["tiny-3k"]
+    g, colors = small_scene(160, seed, sh_dim=12)
+    views, _ = synthetic.make_cameras(wl, seed=2, num_views=3)
+    vm = views[seed % 3]
+    K = np.array([[W * 0.9, 0, W / 2.0], [0, W * 0.9, H / 2.0], [0, 0, 1]], np.float32)
+    ids = R.frustum_culling_mlx(mx.array(g["means"]), mx.array(g["quats"]), mx.array(g["scales"]),
+                                mx.array(vm), mx.array(K), W, H, opacities=mx.array(g["opacities"]))
+    ids = mx.array(np.array(ids), dtype=mx.int32)
+    V = int(np.array(ids).shape[0])
+    rng = np.random.default_rng(seed + 7)
+    mask = rng.uniform(0, 1, V).astype(np.float32)
+    pick = rng.permutation(V)
+    mask[pick[:V // 5]] = 0.0
+    mask[pick[V // 5:2 * (V // 5)]] = 1.0
+    target = rng.uniform(0, 1, (RH, RW, 3)).astype(np.float32)
+    wA = rng.uniform(-1, 1, (RH, RW, 1)).astype(np.float32)
+    tgt, wa, mk = mx.array(target), mx.array(wA), mx.array(mask)
+    col_vis = colors[np.array(ids).astype(np.int64)]
+
+    def loss_fn(p):
+        c, a = R.rasterize_gaussians_mlx(p["means"], p["quats"], p["scales"], p["opacities"], p["colors"],
+                                         mx.array(vm), mx.array(K), W, H, ids, render_width=RW, render_height=RH,
+                                         pixel_chunk_size=512, mask=mk)
+        return mx.mean(mx.abs(c - tgt)) + mx.mean(a * wa)
+
+    params = {"means": mx.array(g["means"]), "quats": mx.array(g["quats"]), "scales": mx.array(g["scales"]),
+              "opacities": mx.array(g["opacities"]), "colors": mx.array(col_vis)}
+    c, a = R.rasterize_gaussians_mlx(params["means"], params["quats"], params["scales"], params["opacities"],
+                                     params["colors"], mx.array(vm), mx.array(K), W, H, ids, render_width=RW,
+                                     render_height=RH, mask=mk)
+    loss, grads = mx.value_and_grad(loss_fn)(params)
+    res = {"means": g["means"], "quats": g["quats"], "scales": g["scales"], "opacities": g["opacities"],
+           "colors": col_vis, "viewmat": vm, "K": K, "dims": np.array([W, H, RW, RH], np.int32),
+           "ids": np.array(ids).astype(np.int32), "mask": mask, "target": target, "wA": wA,
+           "out_colors": np.array(c), "out_alphas": np.array(a), "loss": np.array(loss)}
+    for k, v in grads.items():
+        res["grad_" + k] = np.array(v)
+    np.savez_compressed(os.path.join(out, "raster_mask.npz"), **res)
+
+
 def gen_adam(O, out):
     rng = np.random.default_rng(5)
     dims = {"means": 3, "scales": 3, "quats": 4, "opacities": 1, "sh0": 3, "shN": 9}
@@ -356,9 +401,10 @@ def gen_colmap(ref_root, out):
 
 
 def main():
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/gen_golden.py REFERENCE_ROOT")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/gen_golden.py REFERENCE_ROOT [fixture ...]")
     ref_root = sys.argv[1]
+    only = set(sys.argv[2:])  # e.g. raster_mask: regenerate only those fixtures
     torch.manual_seed(0)
     torch.set_num_threads(1)  # a fixed summation order for the reference's matmuls
     R = load_ref(ref_root, "rendering")
@@ -368,13 +414,13 @@ def main():
     os.chdir(tmp_dir.name)  # the allocator writes a log next to its own file; keep any stray output out of the repo
     try:
         A = load_ref(ref_root, "allocator")
-        gen_cull(R, HERE)
-        gen_raster(R, HERE)
-        gen_adam(O, HERE)
-        gen_alloc(A, HERE)
-        gen_ssim(ref_root, HERE)
-        gen_resize(R, HERE)
-        gen_colmap(ref_root, HERE)
+        gens = {"cull": lambda: gen_cull(R, HERE), "raster": lambda: gen_raster(R, HERE),
+                "raster_mask": lambda: gen_raster_mask(R, HERE), "adam_pure": lambda: gen_adam(O, HERE),
+                "allocator": lambda: gen_alloc(A, HERE), "ssim": lambda: gen_ssim(ref_root, HERE),
+                "resize": lambda: gen_resize(R, HERE), "colmap": lambda: gen_colmap(ref_root, HERE)}
+        for name, gen in gens.items():
+            if not only or name in only:
+                gen()
     finally:
         os.chdir(cwd)
         tmp_dir.cleanup()

@@ -39,7 +39,7 @@ def test_bindings_cover_header():
 @pytest.mark.skipif(not os.path.exists(_lib.LIB_PATH), reason="library not built")
 def test_cpu_only_calls():
     lib = _lib.load()
-    assert lib.gs_abi_version() == 2
+    assert lib.gs_abi_version() == 3
     assert lib.gs_clear_buffer_cache() == 0
     assert lib.gs_radix_sort_scratch_bytes(1000) > 8000
     assert lib.gs_cull_scratch_bytes(5000) > 0

@@ -63,6 +63,35 @@ def test_dense_raster_matches_reference(golden_dir, case):
         assert err < 1e-4, (k, err)
 
 
+def test_dense_raster_with_alpha_mask_matches_reference(golden_dir):
+    """rendering.py:289-290: the reference multiplies the clipped alphas by
+    mask[j], j the depth-sorted position (the mask is not permuted by the
+    sort).  The golden ran the reference's own rasterizer with a mask."""
+    d = _load(golden_dir, "raster_mask.npz")
+    W, H, RW, RH = [int(x) for x in d["dims"]]
+    ids = d["ids"].astype(np.int64)
+    args = (d["means"][ids], d["quats"][ids], d["scales"][ids], d["opacities"][ids], d["colors"],
+            d["viewmat"], d["K"], W, H, RW, RH)
+    C, A = orend.rasterize_dense(*args, dtype=torch.float32, mask=d["mask"])
+    np.testing.assert_allclose(C, d["out_colors"], atol=2e-6)
+    np.testing.assert_allclose(A, d["out_alphas"], atol=2e-6)
+    # the mask must go by depth rank: applied by visible position instead, the image differs
+    pg_order = orend.project(*[torch.as_tensor(np.asarray(a)) for a in args[:5]], torch.as_tensor(d["viewmat"]),
+                             torch.as_tensor(d["K"]), W, H, RW, RH)["order"].numpy()
+    C_wrong, _ = orend.rasterize_dense(*args, dtype=torch.float32, mask=d["mask"][pg_order])
+    assert np.abs(C_wrong - d["out_colors"]).max() > 1e-3
+    P = RW * RH
+    dC = np.sign(C.astype(np.float64) - d["target"]) / (3.0 * P)
+    _, _, g = orend.rasterize_dense_vjp(*args, dL_dC=dC, dL_dA=d["wA"] / P, dtype=torch.float64, mask=d["mask"])
+    for k in ("means", "quats", "scales", "opacities", "colors"):
+        ref = d["grad_" + k]
+        got = g[k] if k == "colors" else np.zeros_like(ref)
+        if k != "colors":
+            got[ids] = g[k]
+        err = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+        assert err < 1e-4, (k, err)
+
+
 def test_adam_pure_matches_reference(golden_dir):
     d = _load(golden_dir, "adam_pure.npz")
     names = ["means", "scales", "quats", "opacities", "sh0", "shN"]
