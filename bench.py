@@ -742,13 +742,19 @@ def main():
         loss_host = torch.empty(2, dtype=torch.float32, pin_memory=True)
         loss_ready = [torch.cuda.Event(), torch.cuda.Event()]
 
+        # the same camera views as the timed loop above (views differ in their
+        # visible and tile-entry counts, so a different sample of views would
+        # measure different work)
+        timed_views = [view_of(s) for s in range(args.warmup + 1, args.warmup + 1 + args.steps)]
+
         def e2e_steps(k):
             nonlocal step
             out = []
             for i in range(k):
                 step += 1
-                stage.copy_(targets_host[view_of(step) % n_tgt], non_blocking=True)
-                runner.train_step(view_of(step), step, target=stage)
+                v = timed_views[i % len(timed_views)]
+                stage.copy_(targets_host[v % n_tgt], non_blocking=True)
+                runner.train_step(v, step, target=stage)
                 slot = i % 2
                 if i >= 2:
                     loss_ready[slot].synchronize()

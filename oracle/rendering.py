@@ -122,6 +122,18 @@ def cull(means: np.ndarray, opacities: Optional[np.ndarray], viewmat: np.ndarray
     return ids
 
 
+def depth_order_f32(means: np.ndarray, viewmat: np.ndarray) -> np.ndarray:
+    """The depth order a float32 renderer gets: camera z as in ``cull``
+    (float32, left to right, every product and sum rounded), stable argsort
+    (ties by input position).  Rasterizers that rank depths in float64 can
+    order nearly equal depths differently."""
+    f32 = np.float32
+    m = np.asarray(means, f32)
+    v = np.asarray(viewmat, f32)
+    z = ((m[:, 0] * v[2, 0] + m[:, 1] * v[2, 1]) + m[:, 2] * v[2, 2]) + v[2, 3]
+    return np.argsort(z, kind="stable")
+
+
 # ----------------------------------------------------------------------------- projection
 def _gt(x, c):
     """MLX ``maximum(x, c)`` with its gradient rule (to ``x`` only where ``x > c``)."""
@@ -240,6 +252,20 @@ def composite(pg: Dict[str, torch.Tensor], pix: torch.Tensor) -> Tuple[torch.Ten
     return w @ pg["rgb"], torch.sum(w, 1, keepdim=True)
 
 
+def _sorted_mask(mask, mask_order, pg_order, dtype):
+    """The alpha mask in this projection's depth order.  ``mask[j]`` belongs to
+    the j-th Gaussian of ``mask_order`` (default: this projection's own depth
+    order, the reference's rule)."""
+    if mask is None:
+        return None
+    mk = _as_t(mask, dtype).reshape(-1)
+    if mask_order is None:
+        return mk
+    by_gaussian = torch.zeros_like(mk)
+    by_gaussian[torch.as_tensor(np.asarray(mask_order, np.int64))] = mk
+    return by_gaussian[pg_order]
+
+
 def _as_t(x, dtype):
     if isinstance(x, torch.Tensor):
         return x.detach().to(dtype)
@@ -248,16 +274,18 @@ def _as_t(x, dtype):
 
 def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, height,
                     render_width, render_height, dtype=torch.float64, chunk: int = 512,
-                    pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference", mask=None):
+                    pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference", mask=None,
+                    mask_order=None):
     """Forward only.  Inputs are the gathered active rows (numpy or torch);
-    ``mask`` [V] multiplies the clipped alpha of the j-th Gaussian in depth order.
+    ``mask`` [V] multiplies the clipped alpha of the j-th Gaussian in depth order
+    (of ``mask_order`` when given, e.g. ``depth_order_f32``).
     Returns ``(colors [H,W,3], alphas [H,W,1])`` as numpy arrays, or
     ``[P,3], [P,1]`` when ``pixel_ids`` selects a subset."""
     with torch.no_grad():
         args = [_as_t(a, dtype) for a in (means, quats, scales, opacities, colors)]
         pg = project(*args, _as_t(viewmat, dtype), _as_t(K, dtype), width, height,
                      render_width, render_height, sh_mode=sh_mode)
-        pg["mask"] = None if mask is None else _as_t(mask, dtype).reshape(-1)
+        pg["mask"] = _sorted_mask(mask, mask_order, pg["order"], dtype)
         pix = pixel_centers(width, height, render_width, render_height, dtype)
         if pixel_ids is not None:
             pix = pix[torch.as_tensor(np.asarray(pixel_ids, np.int64))]
@@ -281,7 +309,7 @@ def rasterize_dense(means, quats, scales, opacities, colors, viewmat, K, width, 
 def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, width, height,
                         render_width, render_height, dL_dC, dL_dA=None, dtype=torch.float64,
                         chunk: int = 256, pixel_ids: Optional[np.ndarray] = None, sh_mode: str = "reference",
-                        l1_target=None, mask=None):
+                        l1_target=None, mask=None, mask_order=None):
     """Forward plus vector-Jacobian product of the dense rasterizer.
 
     ``dL_dC``/``dL_dA`` are ``[H,W,3]``/``[H,W,1]`` (or ``[P,3]``/``[P,1]`` for
@@ -297,7 +325,7 @@ def rasterize_dense_vjp(means, quats, scales, opacities, colors, viewmat, K, wid
                  render_width, render_height, sh_mode=sh_mode)
     keys = ["u", "v", "a", "b", "c", "d", "opac", "rgb"]
     det = {k: pg[k].detach().clone().requires_grad_(True) for k in keys}
-    det["mask"] = None if mask is None else _as_t(mask, dtype).reshape(-1)
+    det["mask"] = _sorted_mask(mask, mask_order, pg["order"], dtype)
     acc = {k: torch.zeros_like(det[k]) for k in keys}
     pix = pixel_centers(width, height, render_width, render_height, dtype)
     if pixel_ids is not None:

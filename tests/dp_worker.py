@@ -12,6 +12,14 @@ parameters and moments on every GPU, before and after a densify step:
 
 Then the same for an SH degree 0 scene (16-float rows, where the broadcast
 columns are the whole row): the sharded Adam against the NCCL all-reduce.
+
+Finally one data-parallel step (the NCCL path, as the bench runs it) against
+the CPU oracle's single-process step: every rank renders its own view of a
+small SH-3 outdoor scene; after the step, Adam's first moment (0.1 times the
+gradient Adam applied) must equal 0.1 times the oracle's mean over both views
+of the dense rasterizer's gradients plus the regulariser, within the gradient
+tolerance (the L1 cotangent is taken from each rank's rendered image, as the
+single-GPU parity tests do).
 """
 import os
 import sys
@@ -21,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from mlx_gsplat_b200 import distributed  # noqa: E402
 from mlx_gsplat_b200.trainer import runner_for_workload  # noqa: E402
@@ -36,6 +45,61 @@ def state(r):
     torch.cuda.synchronize(r.device)
     t = al.indirection_table.cpu().numpy()
     return [al.theta.cpu().numpy()[t], al.adam_m.cpu().numpy()[t], al.adam_v.cpu().numpy()[t]]
+
+
+def oracle_step_check(rank, world, dev, pg):
+    """Returns (ok, worst relative error) of the data-parallel step against the oracle."""
+    import dataclasses
+    from gsutil import GRAD_RTOL
+    from mlx_gsplat_b200 import synthetic
+    from mlx_gsplat_b200.trainer import sh_cols_for
+    from oracle import rendering as orend
+    wl = dataclasses.replace(synthetic.WORKLOADS["outdoor-1m"], name="outdoor-small", num_gaussians=8000,
+                             width=216, height=140, focal=1150.0 / 6)
+    synthetic.WORKLOADS[wl.name] = wl
+    r = runner_for_workload(wl.name, max_steps=50, device=dev, num_views=8, lr=1e-3, eps=1e-15, process_group=pg)
+    al, L = r.allocator, r.layout
+    theta0 = al.theta.cpu().numpy().copy()
+    table = al.indirection_table.cpu().numpy()
+    view = distributed.view_for(1, rank, world, 8)
+    frame = r.train_step(view, 1)
+    torch.cuda.synchronize(dev)
+    mine = (view, frame.color.cpu().numpy(), frame.ids[:frame.V].cpu().numpy().astype(np.int64))
+    views = [None] * world
+    dist.all_gather_object(views, mine, group=pg)
+    m_after = al.adam_m.cpu().numpy()[table]
+    if rank != 0:
+        return True, 0.0
+    N, reg = table.shape[0], r.cfg.param_reg
+    act = {k: theta0[table][:, o:o + L.dims[k]] for k, o in L.offsets.items()}
+    ncols = sh_cols_for(1, r.cfg)
+    colors = np.concatenate([act["sh0"], act["shN"]], 1)[:, :ncols]
+    G = np.zeros((N, L.ncols), np.float64)
+    P = wl.pixels
+    for v, C, ids in views:
+        tf = r.targets[v].cpu().numpy().astype(np.float32) / np.float32(255.0)
+        dC = np.sign(C.astype(np.float64) - tf) / (3.0 * P)
+        _, _, gr = orend.rasterize_dense_vjp(act["means"][ids], act["quats"][ids], act["scales"][ids],
+                                             act["opacities"][ids], colors[ids], r.viewmats[v], r.K, wl.width,
+                                             wl.height, wl.width, wl.height, dL_dC=dC)
+        for k in ("means", "quats", "scales", "opacities"):
+            o = L.offsets[k]
+            G[:, o:o + L.dims[k]] += reg
+            G[ids, o:o + L.dims[k]] += gr[k]
+        G[ids, L.color_col:L.color_col + ncols] += gr["colors"] + reg
+    G /= world
+    worst, ok = 0.0, True
+    for k, o in L.offsets.items():
+        d = L.dims[k]
+        got = m_after[:, o:o + d].astype(np.float64) / 0.1
+        ref = G[:, o:o + d]
+        nref = np.linalg.norm(ref)
+        rel = np.linalg.norm(got - ref) / nref if nref > 0 else np.abs(got).max()
+        floor = 1e-4 * np.abs(ref).max()
+        bad = np.abs(got - ref) > GRAD_RTOL * np.abs(ref) + floor
+        worst = max(worst, float(rel))
+        ok = ok and rel <= GRAD_RTOL and not bad.any()
+    return ok, worst
 
 
 def main():
@@ -74,9 +138,11 @@ def main():
             err = max([err] + [float(np.abs(a - b).max()) for a, b in zip(ref, o) if a.shape == b.shape])
             ok = ok and len(o) == len(ref) and all(a.shape == b.shape and np.allclose(a, b, rtol=1e-5, atol=1e-6)
                                                    for a, b in zip(ref, o))
+    ok_oracle, err_oracle = oracle_step_check(rank, world, dev, pg)
+    ok = ok and ok_oracle
     gathered = [None] * world
-    dist.all_gather_object(gathered, (bool(ok), float(err), {k: [x.shape for x in v] for k, v in out.items()}),
-                           group=pg)
+    dist.all_gather_object(gathered, (bool(ok), float(err), ("oracle", bool(ok_oracle), float(err_oracle)),
+                                      {k: [x.shape for x in v] for k, v in out.items()}), group=pg)
     if rank == 0:
         print("RESULT", gathered, flush=True)
     dist.barrier(group=pg)

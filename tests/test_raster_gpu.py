@@ -72,7 +72,10 @@ def test_alpha_mask_matches_reference_golden(golden_dir):
 def test_alpha_mask_full_image_vs_oracle():
     """A mask over the 3,000-Gaussian scene (values in [0, 1], some exactly 0
     and 1), whole image and every gradient against the dense oracle; and the
-    mask's bounds are checked."""
+    mask's bounds are checked.  The mask goes by depth rank, and among 3,000
+    Gaussians some depths are closer than float32 resolution: the oracle
+    (float64) is told the depth order the float32 kernels rank by
+    (``depth_order_f32``) to assign the mask values, and composites in its own."""
     wl, g, cols = _scene("tiny-3k", 3000, seed=3, sh_dim=12)
     views, K = synthetic.make_cameras(wl, seed=2)
     vm = views[5]
@@ -97,7 +100,8 @@ def test_alpha_mask_full_image_vs_oracle():
     ids64 = idn.astype(np.int64)
     Cr, Ar, gr = orend.rasterize_dense_vjp(g["means"][ids64], g["quats"][ids64], g["scales"][ids64],
                                            g["opacities"][ids64], cols_vis, vm, K, wl.width, wl.height, wl.width,
-                                           wl.height, dL_dC=wC, chunk=256, mask=mask)
+                                           wl.height, dL_dC=wC, chunk=256, mask=mask,
+                                           mask_order=orend.depth_order_f32(g["means"][ids64], vm))
     assert_image_close(C.detach().cpu().numpy(), Cr, what="masked colors")
     assert_image_close(A.detach().cpu().numpy(), Ar, what="masked alphas")
     for k in ("means", "quats", "scales", "opacities"):
