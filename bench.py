@@ -736,7 +736,15 @@ def main():
     # ---- end to end through the public API (host target in, loss out)
     e2e = None
     if not args.no_e2e:
-        stage = torch.empty_like(targets_dev[0])
+        # Each step's target comes from pinned host memory into one of two device
+        # staging buffers on a copy stream, issued one step ahead so that the
+        # upload overlaps the previous step's compute (the compute stream waits
+        # for the copy; the copy into a buffer waits until the step two back,
+        # which read it, is done).
+        stages = [torch.empty_like(targets_dev[0]) for _ in range(2)]
+        copy_stream = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        consumed = [torch.cuda.Event(), torch.cuda.Event()]
         # every step's loss is copied to pinned host memory and read by the host
         # two steps later (two slots), so the read does not idle the GPU
         loss_host = torch.empty(2, dtype=torch.float32, pin_memory=True)
@@ -747,14 +755,27 @@ def main():
         # measure different work)
         timed_views = [view_of(s) for s in range(args.warmup + 1, args.warmup + 1 + args.steps)]
 
+        def upload(i, first):
+            b = i % 2
+            with torch.cuda.stream(copy_stream):
+                if not first:
+                    copy_stream.wait_event(consumed[b])
+                stages[b].copy_(targets_host[timed_views[i % len(timed_views)] % n_tgt], non_blocking=True)
+                copied[b].record(copy_stream)
+
         def e2e_steps(k):
             nonlocal step
             out = []
+            upload(0, True)
             for i in range(k):
                 step += 1
                 v = timed_views[i % len(timed_views)]
-                stage.copy_(targets_host[v % n_tgt], non_blocking=True)
-                runner.train_step(v, step, target=stage)
+                b = i % 2
+                if i + 1 < k:
+                    upload(i + 1, i < 1)  # the next step's target, behind this one's compute
+                torch.cuda.current_stream(dev).wait_event(copied[b])
+                runner.train_step(v, step, target=stages[b])
+                consumed[b].record()
                 slot = i % 2
                 if i >= 2:
                     loss_ready[slot].synchronize()
@@ -781,7 +802,8 @@ def main():
         barrier(world)
         ms_e2e = max_over_ranks(a0.elapsed_time(a1) / args.steps, world)
         e2e = {"value": world * 1000.0 / ms_e2e, "unit": "train steps/s", "ms_per_step": ms_e2e,
-               "h2d_bytes_per_step": int(stage.numel()), "d2h_bytes_per_step": 4}
+               "h2d_bytes_per_step": int(stages[0].numel()), "d2h_bytes_per_step": 4,
+               "h2d": "pinned host -> device on a copy stream, one step ahead of the compute"}
 
     # ---- three densify/prune steps on this scene, two training steps apart (all ranks:
     # the statistics are all-reduced); the first also allocates the density-step workspace

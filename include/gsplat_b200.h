@@ -144,9 +144,6 @@ int gs_clear_buffer_cache(void);
 #define GS_ADAM_FUSED 0 /* the Metal kernel's semantics (scrub + clamp, float32 bias corrections) */
 #define GS_ADAM_PURE 1  /* mlx_gsplat/optimizer.py:146-175: lr_scale, float64 bias corrections, no scrub/clamp */
 #define GS_ADAM_EXACT 0x100 /* OR into gs_fused_adam_slab's mode: IEEE-rounded sqrt and division in the step */
-#define GS_ADAM_ZERO_GRAD 0x200 /* OR into gs_fused_adam_slab's mode: every gradient-row chunk read is then set to
-                                   zero (rows of [0, num_active) start the next step cleared; not with
-                                   visible_words) */
 
 /* One parameter group with explicit row strides (pools whose rows are views
  * into a wider slab).  ``grad_scale`` multiplies g first (1/world_size after

@@ -15,7 +15,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libgsplat_b200.so")
 
 GS_OK, GS_ERR_INVALID, GS_ERR_CUDA, GS_ERR_CAPACITY = 0, 1, 2, 3
-GS_ADAM_FUSED, GS_ADAM_PURE, GS_ADAM_EXACT, GS_ADAM_ZERO_GRAD = 0, 1, 0x100, 0x200
+GS_ADAM_FUSED, GS_ADAM_PURE, GS_ADAM_EXACT = 0, 1, 0x100
 GS_LOSS_NONE, GS_LOSS_L1_U8, GS_LOSS_L1_F32, GS_LOSS_MEAN = 0, 1, 2, 3
 GS_SH_REFERENCE, GS_SH_FULL = 0, 1
 GS_ROWS_ALL, GS_ROWS_SEEN, GS_ROWS_UNSEEN = 0, 1, 2

@@ -193,8 +193,8 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
                                                         const int32_t* __restrict__ idx, int64_t n_rows, int chunks,
                                                         int lane_shift, int g_chunks, int ncols, int quat_chunk,
                                                         int64_t half, const uint32_t* __restrict__ vis,
-                                                        int g_cols, int count_col, int row_select, bool zero_g,
-                                                        AdamScalars s, SlabCols cols) {
+                                                        int g_cols, int count_col, int row_select, AdamScalars s,
+                                                        SlabCols cols) {
     __shared__ ColsSmem cs;
     if (threadIdx.x < kMaxSlabCols) {
         cs.step[threadIdx.x] = cols.step_size[threadIdx.x];
@@ -248,13 +248,6 @@ __global__ void __launch_bounds__(256, 4) adam_slab_kernel(float4* __restrict__ 
     const bool load_g = !kNarrow || 4 * c4 < g_cols || c4 == (count_col >> 2);
     if (ga_seen && load_g) ga = __ldcs(g + ra * g_chunks + c4);
     if (gb_seen && load_g) gb = __ldcs(g + rb * g_chunks + c4);
-    if (zero_g) {
-        // the gradient rows start the next step at zero: each chunk read is cleared
-        float4* gz = const_cast<float4*>(g);
-        const float4 z0 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ga_seen && load_g) __stcs(gz + ra * g_chunks + c4, z0);
-        if (gb_seen && load_g) __stcs(gz + rb * g_chunks + c4, z0);
-    }
     if (kNarrow) {
         const int src = count_col >> 2, k = count_col & 3, width = 1 << lane_shift;
         const float cnt_a = __shfl_sync(kFull, float4_comp(ga, k), src, width);
@@ -462,11 +455,8 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
                                   int count_col, const float* count_coef_host, int row_select,
                                   gs_stream_t stream) {
     const bool exact = (mode & GS_ADAM_EXACT) != 0;
-    const bool zero_g = (mode & GS_ADAM_ZERO_GRAD) != 0;
-    mode &= ~(GS_ADAM_EXACT | GS_ADAM_ZERO_GRAD);
+    mode &= ~GS_ADAM_EXACT;
     GS_REQUIRE(mode == GS_ADAM_FUSED || mode == GS_ADAM_PURE, "adam_slab: unknown mode %d", mode);
-    GS_REQUIRE(!zero_g || !visible_words, "adam_slab: GS_ADAM_ZERO_GRAD clears the rows it reads; "
-               "it cannot be combined with visible_words");
     GS_REQUIRE(!visible_words || unseen_grad_host, "adam_slab: visible_words needs unseen_grad_host");
     GS_REQUIRE(ncols > 0 && ncols <= kMaxSlabCols, "adam_slab: ncols must be in [1, %d]", kMaxSlabCols);
     GS_REQUIRE(g_cols > 0 && g_cols <= ncols, "adam_slab: g_cols must be in [1, ncols]");
@@ -513,7 +503,7 @@ extern "C" int gs_fused_adam_slab(float* theta, const float* g, float* m, float*
         reinterpret_cast<float4*>(theta), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), indices, num_active, chunks, shift, (int)(g_stride / 4), ncols,
         quat_col < 0 ? -1 : quat_col / 4, half, visible_words, g_cols, g_cols < ncols ? count_col : 0, row_select,
-        zero_g, s, cols);
+        s, cols);
     return check_launch("adam_slab_kernel");
 }
 

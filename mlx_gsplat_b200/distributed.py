@@ -72,10 +72,9 @@ class FusedRowReduce:
     GPU has written (barrier), sums this GPU's 1/world slice of the rows across
     all copies and stores the sums to all of them (``multimem.ld_reduce`` +
     ``multimem.st``: one writer per element, so every replica gets the same
-    bits), and waits until every slice is done (barrier).  Adam then clears each
-    row of this GPU's copy as it reads it (with the sharded Adam each GPU
-    zeroes its own copy after the step); the next step's first barrier keeps
-    peers from summing before that.  Barrier waits are bounded; a timeout sets ``error``
+    bits), and waits until every slice is done (barrier).  After Adam each GPU
+    zeroes its own copy; the next step's first barrier keeps peers from
+    summing before that.  Barrier waits are bounded; a timeout sets ``error``
     (``check`` raises), it never stalls the GPU.
 
     Use ``available`` first: it needs NCCL, more than one GPU and multicast

@@ -107,8 +107,7 @@ class FusedMLXAdam:
                   table: torch.Tensor, num_active: int, ncols: int, col_lo, col_hi, quat_col: int = -1,
                   grad_scale: float = 1.0, pure: bool = False, col_lr_scale=None, visible_words: Optional[int] = None,
                   unseen_grad=None, exact: bool = False, grad_bias=None, g_cols: Optional[int] = None,
-                  count_col: int = 0, count_coef=None, row_select: int = 0, advance: bool = True,
-                  zero_grad: bool = False) -> None:
+                  count_col: int = 0, count_coef=None, row_select: int = 0, advance: bool = True) -> None:
         """One launch over every group of a ``[max, stride]`` slab (fused semantics).
         With ``visible_words`` (device address of the cull's visibility bitmask) rows
         the bitmask marks unseen take ``unseen_grad`` (ncols floats) as their gradient
@@ -120,9 +119,7 @@ class FusedMLXAdam:
         count_coef[c]`` (the regulariser of each view that saw the row).
         ``row_select`` (with ``visible_words``) updates only the seen
         (``GS_ROWS_SEEN``) or unseen (``GS_ROWS_UNSEEN``) rows; the second
-        launch of such a pair passes ``advance=False`` to keep the step count.
-        ``zero_grad`` clears every gradient row it reads (the rows then start
-        the next step at zero without a separate fill)."""
+        launch of such a pair passes ``advance=False`` to keep the step count."""
         if advance:
             self.t += 1
         lib = _lib.lib()
@@ -132,8 +129,7 @@ class FusedMLXAdam:
                                           None if col_lr_scale is None else _lib.fptr(col_lr_scale), quat_col,
                                           self.lr, self.beta1, self.beta2, self.eps, self.weight_decay, self.t,
                                           grad_scale, (_lib.GS_ADAM_PURE if pure else _lib.GS_ADAM_FUSED) |
-                                          (_lib.GS_ADAM_EXACT if exact else 0) |
-                                          (_lib.GS_ADAM_ZERO_GRAD if zero_grad else 0),
+                                          (_lib.GS_ADAM_EXACT if exact else 0),
                                           visible_words, None if unseen_grad is None else _lib.fptr(unseen_grad),
                                           None if grad_bias is None else _lib.fptr(grad_bias),
                                           ncols if g_cols is None else int(g_cols), int(count_col),

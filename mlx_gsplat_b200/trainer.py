@@ -94,6 +94,7 @@ class MLXConfig:
     export_ply_on_finish: bool = False
     # NCCL path across GPUs: the gradient rows are summed in this many row
     # ranges, each range's Adam running while the later ranges are reduced
+    # (1: one all-reduce, then Adam)
     allreduce_buckets: int = 4
 
 
@@ -381,10 +382,6 @@ class RunnerMLX:
         bias = None
         sparse = mode == "sparse"
         vis = (cull_scratch.data_ptr() + 255) // 256 * 256 if sparse else None
-        # Across GPUs Adam clears each gradient row it reads (the rows start the
-        # next step at zero; with the multicast sum the peers are past this
-        # step's sum: the next step's first barrier orders the rest)
-        zero = mode == "summed"
         if mode == "summed":
             scale = 1.0 / self.world
             bias = [self.world * r for r in self._reg_pattern(self.layout.ncols)]
@@ -404,12 +401,12 @@ class RunnerMLX:
                     timer.mark("allreduce")
         if not self.sharded and not (mode == "summed" and not fused and cfg.allreduce_buckets > 1 and
                                      self.world > 1):
-            self._adam_rows(0, N, step, scale, bias, vis=vis, zero=zero)
+            self._adam_rows(0, N, step, scale, bias, vis=vis)
             if timer:
                 timer.mark("adam")
-        if self.sharded:
-            # this GPU's rows for the next step (the sharded Adam reads every
-            # copy through the multicast address, so each GPU clears its own)
+        if mode == "summed":
+            # this GPU's rows for the next step (with the multicast sum the
+            # peers are past it: the next step's first barrier orders the rest)
             self.grad[:N].zero_()
             if timer:
                 timer.mark("zero_rows")
@@ -417,7 +414,7 @@ class RunnerMLX:
         self.step_count += 1
         return frame
 
-    def _adam_rows(self, r0: int, r1: int, step: int, scale: float, bias, vis=None, zero: bool = False,
+    def _adam_rows(self, r0: int, r1: int, step: int, scale: float, bias, vis=None,
                    advance: bool = True) -> None:
         """The slab Adam over the gradient rows (active ids) [r0, r1)."""
         L, al = self.layout, self.allocator
@@ -425,22 +422,21 @@ class RunnerMLX:
                                  r1 - r0, L.ncols, self.col_lo, self.col_hi, quat_col=L.quat_col, grad_scale=scale,
                                  visible_words=vis, unseen_grad=self._reg_pattern(L.ncols) if vis is not None else None,
                                  grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
-                                 count_coef=self.count_coef(step) if self.g_cols < L.ncols else None, advance=advance,
-                                 zero_grad=zero)
+                                 count_coef=self.count_coef(step) if self.g_cols < L.ncols else None, advance=advance)
 
     def _bucketed_allreduce_adam(self, N: int, step: int, scale: float, bias, timer=None) -> None:
         """The sum of the gradient rows over GPUs pipelined with Adam: the rows
         are cut into ``cfg.allreduce_buckets`` ranges, every range's NCCL
         all-reduce is queued at once on NCCL's stream, and Adam updates range b
-        (and clears its rows) as soon as range b is summed, while the later
-        ranges are still being reduced."""
+        as soon as range b is summed, while the later ranges are still being
+        reduced."""
         nb = max(1, min(self.cfg.allreduce_buckets, N))
         edges = [N * b // nb for b in range(nb + 1)]
         works = [torch.distributed.all_reduce(self.grad[edges[b]:edges[b + 1]], group=self.pg, async_op=True)
                  for b in range(nb)]
         for b in range(nb):
             works[b].wait()  # this stream waits for bucket b's sum
-            self._adam_rows(edges[b], edges[b + 1], step, scale, bias, zero=True, advance=b == 0)
+            self._adam_rows(edges[b], edges[b + 1], step, scale, bias, advance=b == 0)
         if timer:
             timer.mark("allreduce+adam")
 
