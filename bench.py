@@ -694,6 +694,18 @@ def main():
     Vm = float(np.mean([s[0] for s in stats]))
     Km = float(np.mean([s[1] for s in stats]))
     N = runner.allocator.num_active
+    # the part of each step before the gradient sum, per rank: the sum waits for
+    # the slowest rank's view, so the spread is part of the collective's phase
+    pre = ("cull", "project_fwd", "depth_sort+offsets", "bin+tile_sort", "render_fwd", "render_bwd", "project_bwd")
+    pre_steps = [sum(tm.durations().get(k, 0.0) for k in pre) for tm in timers]
+    per_rank = {"mean_ms": float(np.mean(pre_steps))}
+    if world > 1:
+        import torch.distributed as dist
+        allr = [None] * world
+        dist.all_gather_object(allr, pre_steps)
+        arr = np.array(allr)  # [rank, step]
+        per_rank = {"mean_ms_by_rank": [round(float(x), 4) for x in arr.mean(1)],
+                    "mean_over_steps_of_max_minus_mean_ms": float(np.mean(arr.max(0) - arr.mean(0)))}
     kernels = ["render_fwd", "render_bwd", "project_bwd", "project_fwd", "adam", "cull", "grad_init"]
     per = {}
     for k in kernels:
@@ -857,6 +869,7 @@ def main():
                                 ("nvlink multicast row sum" if runner.fused_reduce is not None else
                                  ("nccl all-reduce" if world > 1 else "none"))),
                 "grad_row_floats": runner.g_stride,
+                "before_sum_ms": per_rank,
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,
                 "adam_gbs": per.get("adam", {}).get("gbs"),
                 "kernels_ms": {k: round(v["ms"], 4) for k, v in per.items()},
