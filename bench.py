@@ -2,8 +2,9 @@
 """Benchmark of the 3DGS training hot path on B200.
 
 One *step* = one camera view per GPU: cull -> tile rasterizer forward with the
-L1 loss fused in -> rasterizer backward -> (N > 1: NCCL all-reduce of the
-gradient rows) -> one fused Adam launch over the pooled slab.  Workload: the
+L1 loss fused in -> rasterizer backward -> (N > 1: NCCL reduce-scatter of the
+gradient rows) -> one fused Adam launch over the pooled slab (N > 1: over this
+GPU's block of rows, then an all-gather of the columns the rasterizer reads).  Workload: the
 ``outdoor-1m`` scene (1,000,000 Gaussians, SH degree 3, 160 ring views at
 1297x840, fx = fy = 1150, seeded uint8 targets).
 
@@ -83,6 +84,9 @@ def parse():
                          "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
+    ap.add_argument("--replicated-adam", action="store_true",
+                    help="N > 1 over NCCL: all-reduce the gradient rows and run Adam on every GPU (default: "
+                         "reduce-scatter, Adam on each GPU's block of rows, all-gather of the rasterizer's columns)")
     ap.add_argument("--allreduce-buckets", type=int, default=4,
                     help="N > 1 over NCCL: row ranges of the gradient sum, each range's Adam overlapping the later "
                          "ranges' all-reduce (1: one all-reduce, then Adam)")
@@ -631,7 +635,8 @@ def main():
                                  eps=1e-15, n=args.gaussians, num_views=nv,
                                  max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2),
                                  process_group=pg, fused_reduce=args.multicast,
-                                 allreduce_buckets=args.allreduce_buckets)
+                                 allreduce_buckets=args.allreduce_buckets,
+                                 nccl_sharded_adam=not args.replicated_adam)
     # the targets: seeded uint8 images, one per view up to ~1 GB of pinned host memory
     # per process, cycled over the views beyond that (the large scene's 512 3840x2160
     # targets alone would take 12.7 GB per process)
@@ -867,7 +872,10 @@ def main():
                 "config": workload_config(args, world),
                 "grad_reduce": ("nvlink multicast sum fused into the sharded adam" if runner.sharded else
                                 ("nvlink multicast row sum" if runner.fused_reduce is not None else
-                                 ("nccl all-reduce" if world > 1 else "none"))),
+                                 ("nccl reduce-scatter, adam on 1/N of the rows, all-gather of the rasterizer's "
+                                  "columns" if runner.sharded_nccl else
+                                  (f"nccl all-reduce in {runner.cfg.allreduce_buckets} row ranges, pipelined with "
+                                   "the replicated adam" if world > 1 else "none")))),
                 "grad_row_floats": runner.g_stride,
                 "before_sum_ms": per_rank,
                 "mpix_per_s": value * P / 1e6, "visible_mean": Vm, "entries_mean": Km,

@@ -527,6 +527,14 @@ int gs_fill_rows(float* dst, int64_t n_rows, int64_t stride, const float* patter
  * reset, mlx_gsplat/trainer.py:416-419). */
 int gs_fill_column(float* dst, int64_t n_rows, int64_t stride, int col, float value, gs_stream_t stream);
 
+/* Row gather/scatter (no reference counterpart; the sharded multi-GPU Adam
+ * packs and unpacks the parameter columns the rasterizer reads): for j < n,
+ * dst row (dst_idx ? dst_idx[j] : j) gets the first ``cols`` floats of src row
+ * (src_idx ? src_idx[j] : j).  Strides in floats; cols and both strides
+ * multiples of 4, bases 16-byte aligned.  Destination rows must be distinct. */
+int gs_copy_rows(const float* src, int64_t src_stride, const int32_t* src_idx, float* dst, int64_t dst_stride,
+                 const int32_t* dst_idx, int64_t n, int cols, gs_stream_t stream);
+
 /* mask[slots[j]] = value for j < n, skipping slots outside [0, mask_len): the
  * allocator's active-slot mask updates of allocator.py:209-225 (pruned slots
  * cleared, child slots set). */

@@ -125,6 +125,7 @@ _SIGS = {
     "gs_fill_rows": (ctypes.c_int, [c_vp, i64, i64, c_float_p, c_vp]),
     "gs_fill_column": (ctypes.c_int, [c_vp, i64, i64, ctypes.c_int, ctypes.c_float, c_vp]),
     "gs_mark_slots": (ctypes.c_int, [c_vp, i64, c_vp, i64, ctypes.c_int, c_vp]),
+    "gs_copy_rows": (ctypes.c_int, [c_vp, i64, c_vp, c_vp, i64, c_vp, i64, ctypes.c_int, c_vp]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None

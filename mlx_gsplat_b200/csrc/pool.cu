@@ -74,6 +74,20 @@ __global__ void mark_slots_kernel(int8_t* __restrict__ mask, int64_t mask_len, c
     if (s >= 0 && s < mask_len) mask[s] = value;
 }
 
+// dst row (dst_idx ? dst_idx[j] : j) gets the first ``cols`` floats of src row
+// (src_idx ? src_idx[j] : j), for j < n; 16 bytes at a time (the caller
+// guarantees 16-byte rows and cols % 4 == 0).
+__global__ void copy_rows_v4_kernel(const float4* __restrict__ src, int64_t src_q, const int32_t* __restrict__ src_idx,
+                                    float4* __restrict__ dst, int64_t dst_q, const int32_t* __restrict__ dst_idx,
+                                    int64_t n, int chunks) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n * chunks) return;
+    const int64_t j = t / chunks;
+    const int c = (int)(t - j * chunks);
+    const int64_t rs = src_idx ? (int64_t)src_idx[j] : j, rd = dst_idx ? (int64_t)dst_idx[j] : j;
+    dst[rd * dst_q + c] = src[rs * src_q + c];
+}
+
 }  // namespace gs
 
 using namespace gs;
@@ -128,4 +142,19 @@ extern "C" int gs_mark_slots(int8_t* mask, int64_t mask_len, const int32_t* slot
     GS_REQUIRE(mask && slots, "mark_slots: null pointer");
     mark_slots_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(mask, mask_len, slots, n, (int8_t)value);
     return check_launch("mark_slots_kernel");
+}
+
+extern "C" int gs_copy_rows(const float* src, int64_t src_stride, const int32_t* src_idx, float* dst,
+                            int64_t dst_stride, const int32_t* dst_idx, int64_t n, int cols, gs_stream_t stream) {
+    GS_REQUIRE(n >= 0 && cols > 0 && cols % 4 == 0 && src_stride % 4 == 0 && dst_stride % 4 == 0 &&
+                   cols <= src_stride && cols <= dst_stride,
+               "copy_rows: cols must be a positive multiple of 4 within both row strides (multiples of 4)");
+    if (n == 0) return GS_OK;
+    GS_REQUIRE(src && dst, "copy_rows: null pointer");
+    GS_REQUIRE(aligned16(src) && aligned16(dst), "copy_rows: bases must be 16-byte aligned");
+    const int chunks = cols / 4;
+    copy_rows_v4_kernel<<<grid_for(n * chunks, 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const float4*>(src), src_stride / 4, src_idx, reinterpret_cast<float4*>(dst), dst_stride / 4,
+        dst_idx, n, chunks);
+    return check_launch("copy_rows_v4_kernel");
 }

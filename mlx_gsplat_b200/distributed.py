@@ -152,22 +152,8 @@ class FusedRowReduce:
 
     def gather_owned_rows(self, t: torch.Tensor, owned: torch.Tensor, rows: Optional[slice] = None,
                           first_col: int = 0) -> None:
-        """Every GPU's copy of the slot-indexed rows of ``t`` becomes the owners'
-        rows: the rows this GPU does not own are zeroed, then summed over the
-        group (an NCCL all-reduce); used before densify, export and
-        checkpoints, which read the columns and moments the sharded Adam
-        leaves with the owners.  Only the slot range ``rows`` (default: all)
-        and the columns from ``first_col`` on move: the columns every GPU
-        already holds identically (the broadcast ones) and unused slots need no
-        exchange."""
-        rows = rows if rows is not None else slice(0, t.shape[0])
-        part = t[rows, first_col:]
-        if part.numel() == 0:
-            return
-        buf = part.contiguous()
-        buf.masked_fill_(~owned[rows].unsqueeze(1), 0.0)
-        dist.all_reduce(buf, group=self.pg)
-        part.copy_(buf)
+        """``gather_owned_rows`` over this group."""
+        gather_owned_rows(t, owned, self.pg, rows, first_col)
 
     def slice_of(self, n_rows: int):
         """This GPU's rows of the sum: a contiguous 1/world share."""
@@ -192,6 +178,34 @@ class FusedRowReduce:
         replicas are no longer in step and training cannot go on."""
         if int(self.error.item()) != 0:
             raise RuntimeError("multi-GPU barrier timed out (a peer did not arrive)")
+
+
+def gather_owned_rows(t: torch.Tensor, owned: torch.Tensor, pg, rows: Optional[slice] = None,
+                      first_col: int = 0) -> None:
+    """Every rank's copy of the slot-indexed rows of ``t`` becomes the owners'
+    rows: the rows this rank does not own are zeroed, then summed over the
+    group (an all-reduce).  The sharded Adams leave some columns and the
+    moments current only on the rank that owns a slot; densify, export and
+    checkpoints call this first.  Only the slot range ``rows`` (default: all)
+    and the columns from ``first_col`` on move: the columns every rank already
+    holds identically (the broadcast ones) and unused slots need no exchange."""
+    rows = rows if rows is not None else slice(0, t.shape[0])
+    part = t[rows, first_col:]
+    if part.numel() == 0:
+        return
+    buf = part.contiguous()
+    buf.masked_fill_(~owned[rows].unsqueeze(1), 0.0)
+    dist.all_reduce(buf, group=pg)
+    part.copy_(buf)
+
+
+def block_of(n_rows: int, rank: int, world: int):
+    """The contiguous block of rows [first, first + count) rank ``rank`` owns when
+    ``n_rows`` rows are cut into ``world`` equal blocks of ``per`` rows (the
+    last ones padded): returns (first, count, per)."""
+    per = -(-n_rows // world) if n_rows > 0 else 0
+    first = min(rank * per, n_rows)
+    return first, max(0, min(per, n_rows - first)), per
 
 
 def init_from_env(backend: str = "nccl", timeout_s: float = 180.0):

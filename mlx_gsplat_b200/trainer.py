@@ -92,7 +92,11 @@ class MLXConfig:
     # write ``<scene>_mlx_custom_3dgs.ply`` when train() finishes, as the
     # reference's train() does (trainer.py:566-568)
     export_ply_on_finish: bool = False
-    # NCCL path across GPUs: the gradient rows are summed in this many row
+    # NCCL path across GPUs: the gradient rows are reduce-scattered, each GPU
+    # runs Adam for its contiguous block of active ids and the columns the
+    # rasterizer reads are all-gathered (else: an all-reduce and a replicated Adam)
+    nccl_sharded_adam: bool = True
+    # replicated-Adam NCCL path: the gradient rows are summed in this many row
     # ranges, each range's Adam running while the later ranges are reduced
     # (1: one all-reduce, then Adam)
     allreduce_buckets: int = 4
@@ -222,6 +226,7 @@ class RunnerMLX:
         # columns the rasterizer reads (``hot_cols``) to every GPU.
         self.fused_reduce = None
         self.sharded = False
+        self.sharded_nccl = False
         if fused_reduce and distributed.FusedRowReduce.available(self.device, process_group):
             self.sharded = bool(cfg.sharded_adam)
             self.fused_reduce = distributed.FusedRowReduce(cfg.max_gaussians, self.g_stride, self.device,
@@ -236,10 +241,21 @@ class RunnerMLX:
         # geometry and SH <= 1 colour in the reference mode), whole 16-byte chunks
         self.hot_cols = L.stride if cfg.sh_eval == "full" else min(L.stride, (L.color_col + 12 + 3) // 4 * 4)
         self._owned = self.fused_reduce.owned_slots(cfg.max_gaussians) if self.sharded else None
+        # NCCL across GPUs with a sharded Adam: rank r updates the active ids of
+        # block r (distributed.block_of); the row buffers have room for the
+        # padding of the last block
+        self.sharded_nccl = self.world > 1 and self.fused_reduce is None and bool(cfg.nccl_sharded_adam)
         if self.fused_reduce is not None:
             self.grad = self.fused_reduce.rows
         else:
-            self.grad = torch.zeros((cfg.max_gaussians, self.g_stride), dtype=torch.float32, device=self.device)
+            pad = self.world if self.sharded_nccl else 0
+            self.grad = torch.zeros((cfg.max_gaussians + pad, self.g_stride), dtype=torch.float32,
+                                    device=self.device)
+        if self.sharded_nccl:
+            rows = cfg.max_gaussians + self.world
+            self._grad_shard = torch.empty((-(-rows // self.world), self.g_stride), dtype=torch.float32,
+                                           device=self.device)
+            self._hot_rows = torch.empty((rows, self.hot_cols), dtype=torch.float32, device=self.device)
         lo, hi = L.col_bounds()
         self.col_lo, self.col_hi = lo.tolist(), hi.tolist()
         self.viewmats = np.asarray(viewmats, np.float32)
@@ -393,14 +409,16 @@ class RunnerMLX:
                 self.fused_reduce.sum_rows(N)
                 if timer:
                     timer.mark("row_sum")
+            elif self.sharded_nccl:
+                self._nccl_sharded_adam(N, step, scale, bias, timer)
             elif cfg.allreduce_buckets > 1 and self.world > 1:
                 self._bucketed_allreduce_adam(N, step, scale, bias, timer)
             else:
                 distributed.reduce_gradient_rows(self.grad[:N], self.pg)
                 if timer:
                     timer.mark("allreduce")
-        if not self.sharded and not (mode == "summed" and not fused and cfg.allreduce_buckets > 1 and
-                                     self.world > 1):
+        if not self.sharded and not self.sharded_nccl and not (mode == "summed" and not fused and
+                                                               cfg.allreduce_buckets > 1 and self.world > 1):
             self._adam_rows(0, N, step, scale, bias, vis=vis)
             if timer:
                 timer.mark("adam")
@@ -415,14 +433,62 @@ class RunnerMLX:
         return frame
 
     def _adam_rows(self, r0: int, r1: int, step: int, scale: float, bias, vis=None,
-                   advance: bool = True) -> None:
-        """The slab Adam over the gradient rows (active ids) [r0, r1)."""
+                   advance: bool = True, g: Optional[torch.Tensor] = None) -> None:
+        """The slab Adam over the active ids [r0, r1), their gradient rows
+        ``g`` (default: rows [r0, r1) of the gradient slab)."""
         L, al = self.layout, self.allocator
-        self.optimizer.step_slab(al.theta, self.grad[r0:r1], al.adam_m, al.adam_v, al.indirection_table[r0:r1],
+        if r1 <= r0:
+            if advance:
+                self.optimizer.t += 1  # every rank keeps the same step count
+            return
+        g = self.grad[r0:r1] if g is None else g
+        self.optimizer.step_slab(al.theta, g, al.adam_m, al.adam_v, al.indirection_table[r0:r1],
                                  r1 - r0, L.ncols, self.col_lo, self.col_hi, quat_col=L.quat_col, grad_scale=scale,
                                  visible_words=vis, unseen_grad=self._reg_pattern(L.ncols) if vis is not None else None,
                                  grad_bias=bias, g_cols=self.g_cols, count_col=self.count_col,
                                  count_coef=self.count_coef(step) if self.g_cols < L.ncols else None, advance=advance)
+
+    def _nccl_sharded_adam(self, N: int, step: int, scale: float, bias, timer=None) -> None:
+        """The gradient rows reduce-scattered over the GPUs (NCCL), Adam on this
+        GPU's block of active ids only, then the columns the rasterizer reads
+        (``hot_cols``) of every block all-gathered and written into every GPU's
+        parameter slab.  The same bytes cross NVLink as with an all-reduce, and
+        Adam's HBM traffic is 1/N of a replicated one.  The other parameter
+        columns and the moments are current only on the block's owner until
+        ``gather_sharded_state``."""
+        import torch.distributed as dist
+        lib = _lib.lib()
+        st = _lib.stream_ptr(self.device)
+        al, L = self.allocator, self.layout
+        W, r = self.world, distributed.rank_of(self.pg)
+        first, count, per = distributed.block_of(N, r, W)
+        shard = self._grad_shard[:per]
+        dist.reduce_scatter_tensor(shard, self.grad[:per * W], op=dist.ReduceOp.SUM, group=self.pg)
+        if timer:
+            timer.mark("reduce_scatter")
+        self._adam_rows(first, first + count, step, scale, bias, g=shard[:count])
+        if timer:
+            timer.mark("adam")
+        hot, hc = self._hot_rows, self.hot_cols
+        tab = al.indirection_table
+        if count:
+            _lib.check(lib.gs_copy_rows(al.theta.data_ptr(), L.stride, tab[first:].data_ptr(),
+                                        hot[first:].data_ptr(), hc, None, count, hc, st), "pack columns")
+        # rank r's block is its slice of the gathered rows (in place)
+        dist.all_gather_into_tensor(hot[:per * W], hot[r * per:(r + 1) * per], group=self.pg)
+        _lib.check(lib.gs_copy_rows(hot.data_ptr(), hc, None, al.theta.data_ptr(), L.stride, tab.data_ptr(), N, hc,
+                                    st), "unpack columns")
+        if timer:
+            timer.mark("all_gather")
+
+    def _owned_slots_of_block(self) -> torch.Tensor:
+        """Boolean mask of the pool slots whose rows this GPU's sharded NCCL Adam
+        updates (the slots of its block of active ids)."""
+        al = self.allocator
+        first, count, _ = distributed.block_of(al.num_active, distributed.rank_of(self.pg), self.world)
+        owned = torch.zeros(al.max_gaussians, dtype=torch.bool, device=self.device)
+        owned[al.indirection_table[first:first + count].long()] = True
+        return owned
 
     def _bucketed_allreduce_adam(self, N: int, step: int, scale: float, bias, timer=None) -> None:
         """The sum of the gradient rows over GPUs pipelined with Adam: the rows
@@ -472,7 +538,7 @@ class RunnerMLX:
         moments are current only on the GPU that owns each slot: every GPU's
         copy becomes the owners' (the parameters, and ``moments`` too).  The
         densify step, the PLY export and checkpoints call it first."""
-        if not self.sharded:
+        if not (self.sharded or self.sharded_nccl):
             return
         al = self.allocator
         self.check_group()
@@ -480,11 +546,12 @@ class RunnerMLX:
             return
         t = al.indirection_table
         used = slice(int(t.min()), int(t.max()) + 1)  # the slot range in use (the free list pops from the top)
+        owned = self._owned if self.sharded else self._owned_slots_of_block()
         # theta: only the columns past the broadcast ones differ between GPUs
-        self.fused_reduce.gather_owned_rows(al.theta, self._owned, used, first_col=self.hot_cols)
+        distributed.gather_owned_rows(al.theta, owned, self.pg, used, first_col=self.hot_cols)
         if moments:
-            self.fused_reduce.gather_owned_rows(al.adam_m, self._owned, used)
-            self.fused_reduce.gather_owned_rows(al.adam_v, self._owned, used)
+            distributed.gather_owned_rows(al.adam_m, owned, self.pg, used)
+            distributed.gather_owned_rows(al.adam_v, owned, self.pg, used)
 
     def check_group(self) -> None:
         """Raises if a multi-GPU barrier wait gave up (``FusedRowReduce.check``;
@@ -508,7 +575,9 @@ class RunnerMLX:
         L = self.layout
         N = al.num_active
         self.check_group()
-        self.gather_sharded_state(moments=False)  # children copy whole parent rows
+        # children copy whole parent rows; with blocks of active ids the blocks
+        # move when the table changes, so the moments are gathered as well
+        self.gather_sharded_state(moments=self.sharded_nccl)
         distributed.reduce_densify_stats(al.grad2d, al.count, self.pg)
         g = self._gaussians(step)
         flags = al.workspace()["flags"]

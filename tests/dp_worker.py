@@ -1,20 +1,22 @@
 """Worker for the multi-GPU parity test (run under torch.distributed.run, one
 process per GPU).  From the same start, trains a few steps of the outdoor
-scene (SH degree 3 stored) four ways and checks that all give the same
+scene (SH degree 3 stored) five ways and checks that all give the same
 parameters and moments on every GPU, before and after a densify step:
 
-* the sharded Adam: each GPU updates the pool slots it owns, fused with the
-  gradient sum (multimem.ld_reduce) and the broadcast of the rasterizer's
-  columns (multimem.st) — narrow gradient rows;
+* the multicast sharded Adam: each GPU updates the pool slots it owns, fused
+  with the gradient sum (multimem.ld_reduce) and the broadcast of the
+  rasterizer's columns (multimem.st) — narrow gradient rows;
 * the multicast row sum, then a replicated Adam — narrow rows;
 * an NCCL all-reduce, then a replicated Adam — narrow rows;
-* an NCCL all-reduce of full-width rows.
+* an NCCL all-reduce of full-width rows;
+* the NCCL sharded Adam (the default): a reduce-scatter of the rows, Adam on
+  each GPU's block of active ids, an all-gather of the rasterizer's columns.
 
 Then the same for an SH degree 0 scene (16-float rows, where the broadcast
-columns are the whole row): the sharded Adam against the NCCL all-reduce.
+columns are the whole row): both sharded Adams against the NCCL all-reduce.
 
-Finally one data-parallel step (the NCCL path, as the bench runs it) against
-the CPU oracle's single-process step: every rank renders its own view of a
+Finally one data-parallel step of the default path against the CPU oracle's
+single-process step: every rank renders its own view of a
 small SH-3 outdoor scene; after the step, Adam's first moment (0.1 times the
 gradient Adam applied) must equal 0.1 times the oracle's mean over both views
 of the dense rasterizer's gradients plus the regulariser, within the gradient
@@ -34,9 +36,13 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 from mlx_gsplat_b200 import distributed  # noqa: E402
 from mlx_gsplat_b200.trainer import runner_for_workload  # noqa: E402
 
-CONFIGS = [("outdoor-1m", "sharded", True, True, True), ("outdoor-1m", "multicast sum", True, True, False),
-           ("outdoor-1m", "nccl", False, True, True), ("outdoor-1m", "nccl full rows", False, False, True),
-           ("mid-200k", "sharded sh0", True, True, True), ("mid-200k", "nccl sh0", False, True, True)]
+# workload, name, multicast, narrow rows, multicast sharded Adam, NCCL sharded Adam
+CONFIGS = [("outdoor-1m", "sharded", True, True, True, False),
+           ("outdoor-1m", "multicast sum", True, True, False, False),
+           ("outdoor-1m", "nccl", False, True, True, False), ("outdoor-1m", "nccl full rows", False, False, True, False),
+           ("outdoor-1m", "nccl sharded", False, True, False, True),
+           ("mid-200k", "sharded sh0", True, True, True, False), ("mid-200k", "nccl sh0", False, True, True, False),
+           ("mid-200k", "nccl sharded sh0", False, True, False, True)]
 
 
 def state(r):
@@ -67,6 +73,7 @@ def oracle_step_check(rank, world, dev, pg):
     mine = (view, frame.color.cpu().numpy(), frame.ids[:frame.V].cpu().numpy().astype(np.int64))
     views = [None] * world
     dist.all_gather_object(views, mine, group=pg)
+    r.gather_sharded_state()  # the sharded Adam leaves each block's moments with its owner
     m_after = al.adam_m.cpu().numpy()[table]
     if rank != 0:
         return True, 0.0
@@ -106,16 +113,16 @@ def main():
     rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=120.0)
     dev = torch.device("cuda", local)
     out = {}
-    for wl, name, fused, compact, sharded in CONFIGS:
+    for wl, name, fused, compact, sharded, nccl_sharded in CONFIGS:
         r = runner_for_workload(wl, n=20_000, max_steps=100, device=dev, num_views=8, process_group=pg,
                                 fused_reduce=fused, compact_grad_rows=compact, sharded_adam=sharded,
-                                max_gaussians=60_000)
+                                nccl_sharded_adam=nccl_sharded, max_gaussians=60_000)
         if fused and r.fused_reduce is None:
             print("SKIP: no multicast support", flush=True)
             dist.destroy_process_group()
             return
         assert wl != "outdoor-1m" or (r.g_stride == 24) == compact
-        assert r.sharded == (fused and sharded)
+        assert r.sharded == (fused and sharded) and r.sharded_nccl == nccl_sharded
         for step in range(1, 4):
             r.train_step(distributed.view_for(step, rank, world, 8), step)
         before = state(r)
@@ -130,7 +137,7 @@ def main():
         if r.fused_reduce is not None:
             r.fused_reduce.check()
         out[name] = before + state(r)
-    groups = {"sharded": [k for k in out if not k.endswith("sh0")], "sharded sh0": ["nccl sh0"]}
+    groups = {"sharded": [k for k in out if not k.endswith("sh0")], "sharded sh0": ["nccl sh0", "nccl sharded sh0"]}
     err, ok = 0.0, True
     for refname, others in groups.items():
         ref = out[refname]

@@ -220,9 +220,7 @@ def _gather_owned(rank, world):
     junk[3, 7] = float("nan")
     t[~owned, hot:] = junk[~owned, hot:]
     outside = t[:10].clone()
-    fr = D.FusedRowReduce.__new__(D.FusedRowReduce)  # host logic only: no symmetric memory on gloo
-    fr.pg = dist.group.WORLD
-    fr.gather_owned_rows(t, owned, slice(10, rows), first_col=hot)
+    D.gather_owned_rows(t, owned, dist.group.WORLD, slice(10, rows), first_col=hot)
     return {"t": t.numpy(), "truth": truth, "outside": outside.numpy()}
 
 
@@ -232,3 +230,15 @@ def test_gather_owned_rows_moves_only_the_used_range_and_owner_columns():
         np.testing.assert_array_equal(r["t"][10:], r["truth"][10:])  # used slots: the owners' rows
         np.testing.assert_array_equal(r["t"][:10], r["outside"])     # outside the range: untouched
     np.testing.assert_array_equal(a["t"][10:], b["t"][10:])
+
+
+def test_row_blocks_cover_every_row_once():
+    from mlx_gsplat_b200 import distributed as D
+    for n in (0, 1, 7, 8, 9, 1000, 1001):
+        for w in (1, 2, 3, 8):
+            seen = []
+            for r in range(w):
+                first, count, per = D.block_of(n, r, w)
+                assert count <= per and per * w >= n
+                seen += list(range(first, first + count))
+            assert seen == list(range(n)), (n, w)

@@ -24,6 +24,7 @@ def test_multicast_row_sum_matches_allreduce():
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29533",
            os.path.join(HERE, "dp_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    print(r.stdout[-4000:])
     tail = (r.stdout + r.stderr)[-3000:]
     if "SKIP: no multicast support" in r.stdout:
         pytest.skip("no NVLink multicast on this machine")
