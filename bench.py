@@ -2,9 +2,9 @@
 """Benchmark of the 3DGS training hot path on B200.
 
 One *step* = one camera view per GPU: cull -> tile rasterizer forward with the
-L1 loss fused in -> rasterizer backward -> (N > 1: NCCL reduce-scatter of the
-gradient rows) -> one fused Adam launch over the pooled slab (N > 1: over this
-GPU's block of rows, then an all-gather of the columns the rasterizer reads).  Workload: the
+L1 loss fused in -> rasterizer backward -> (N > 1: NCCL all-reduce of the
+gradient rows in four row ranges) -> the fused Adam over the pooled slab (N > 1:
+one launch per row range, each as soon as its range is summed).  Workload: the
 ``outdoor-1m`` scene (1,000,000 Gaussians, SH degree 3, 160 ring views at
 1297x840, fx = fy = 1150, seeded uint8 targets).
 
@@ -84,9 +84,10 @@ def parse():
                          "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
-    ap.add_argument("--replicated-adam", action="store_true",
-                    help="N > 1 over NCCL: all-reduce the gradient rows and run Adam on every GPU (default: "
-                         "reduce-scatter, Adam on each GPU's block of rows, all-gather of the rasterizer's columns)")
+    ap.add_argument("--sharded-adam", action="store_true",
+                    help="N > 1 over NCCL: reduce-scatter the gradient rows, run Adam on each GPU's block of rows "
+                         "and all-gather the rasterizer's columns (default: an all-reduce pipelined with a "
+                         "replicated Adam)")
     ap.add_argument("--allreduce-buckets", type=int, default=4,
                     help="N > 1 over NCCL: row ranges of the gradient sum, each range's Adam overlapping the later "
                          "ranges' all-reduce (1: one all-reduce, then Adam)")
@@ -636,7 +637,7 @@ def main():
                                  max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2),
                                  process_group=pg, fused_reduce=args.multicast,
                                  allreduce_buckets=args.allreduce_buckets,
-                                 nccl_sharded_adam=not args.replicated_adam)
+                                 nccl_sharded_adam=args.sharded_adam)
     # the targets: seeded uint8 images, one per view up to ~1 GB of pinned host memory
     # per process, cycled over the views beyond that (the large scene's 512 3840x2160
     # targets alone would take 12.7 GB per process)

@@ -94,8 +94,9 @@ class MLXConfig:
     export_ply_on_finish: bool = False
     # NCCL path across GPUs: the gradient rows are reduce-scattered, each GPU
     # runs Adam for its contiguous block of active ids and the columns the
-    # rasterizer reads are all-gathered (else: an all-reduce and a replicated Adam)
-    nccl_sharded_adam: bool = True
+    # rasterizer reads are all-gathered (default: an all-reduce pipelined with
+    # a replicated Adam, measured faster on two GPUs)
+    nccl_sharded_adam: bool = False
     # replicated-Adam NCCL path: the gradient rows are summed in this many row
     # ranges, each range's Adam running while the later ranges are reduced
     # (1: one all-reduce, then Adam)

@@ -9,14 +9,14 @@ parameters and moments on every GPU, before and after a densify step:
 * the multicast row sum, then a replicated Adam — narrow rows;
 * an NCCL all-reduce, then a replicated Adam — narrow rows;
 * an NCCL all-reduce of full-width rows;
-* the NCCL sharded Adam (the default): a reduce-scatter of the rows, Adam on
-  each GPU's block of active ids, an all-gather of the rasterizer's columns.
+* the NCCL sharded Adam: a reduce-scatter of the rows, Adam on each GPU's
+  block of active ids, an all-gather of the rasterizer's columns.
 
 Then the same for an SH degree 0 scene (16-float rows, where the broadcast
 columns are the whole row): both sharded Adams against the NCCL all-reduce.
 
-Finally one data-parallel step of the default path against the CPU oracle's
-single-process step: every rank renders its own view of a
+Finally one data-parallel step of each NCCL path (the default all-reduce and
+the sharded Adam) against the CPU oracle's single-process step: every rank renders its own view of a
 small SH-3 outdoor scene; after the step, Adam's first moment (0.1 times the
 gradient Adam applied) must equal 0.1 times the oracle's mean over both views
 of the dense rasterizer's gradients plus the regulariser, within the gradient
@@ -53,7 +53,7 @@ def state(r):
     return [al.theta.cpu().numpy()[t], al.adam_m.cpu().numpy()[t], al.adam_v.cpu().numpy()[t]]
 
 
-def oracle_step_check(rank, world, dev, pg):
+def oracle_step_check(rank, world, dev, pg, nccl_sharded):
     """Returns (ok, worst relative error) of the data-parallel step against the oracle."""
     import dataclasses
     from gsutil import GRAD_RTOL
@@ -63,7 +63,8 @@ def oracle_step_check(rank, world, dev, pg):
     wl = dataclasses.replace(synthetic.WORKLOADS["outdoor-1m"], name="outdoor-small", num_gaussians=8000,
                              width=216, height=140, focal=1150.0 / 6)
     synthetic.WORKLOADS[wl.name] = wl
-    r = runner_for_workload(wl.name, max_steps=50, device=dev, num_views=8, lr=1e-3, eps=1e-15, process_group=pg)
+    r = runner_for_workload(wl.name, max_steps=50, device=dev, num_views=8, lr=1e-3, eps=1e-15, process_group=pg,
+                            nccl_sharded_adam=nccl_sharded)
     al, L = r.allocator, r.layout
     theta0 = al.theta.cpu().numpy().copy()
     table = al.indirection_table.cpu().numpy()
@@ -145,7 +146,10 @@ def main():
             err = max([err] + [float(np.abs(a - b).max()) for a, b in zip(ref, o) if a.shape == b.shape])
             ok = ok and len(o) == len(ref) and all(a.shape == b.shape and np.allclose(a, b, rtol=1e-5, atol=1e-6)
                                                    for a, b in zip(ref, o))
-    ok_oracle, err_oracle = oracle_step_check(rank, world, dev, pg)
+    ok_oracle, err_oracle = True, 0.0
+    for nccl_sharded in (False, True):
+        o, e = oracle_step_check(rank, world, dev, pg, nccl_sharded)
+        ok_oracle, err_oracle = ok_oracle and o, max(err_oracle, e)
     ok = ok and ok_oracle
     gathered = [None] * world
     dist.all_gather_object(gathered, (bool(ok), float(err), ("oracle", bool(ok_oracle), float(err_oracle)),
