@@ -2,9 +2,11 @@
 """Benchmark of the 3DGS training hot path on B200.
 
 One *step* = one camera view per GPU: cull -> tile rasterizer forward with the
-L1 loss fused in -> rasterizer backward -> (N > 1: NCCL all-reduce of the
-gradient rows in four row ranges) -> the fused Adam over the pooled slab (N > 1:
-one launch per row range, each as soon as its range is summed).  Workload: the
+L1 loss fused in -> rasterizer backward -> the fused Adam over the pooled slab.
+Across GPUs the gradient rows are summed over NCCL: from 4 GPUs up by a
+reduce-scatter, Adam over each GPU's block of rows and an all-gather of the
+columns the rasterizer reads; on 2 GPUs by an all-reduce in four row ranges,
+each range's replicated Adam launched as soon as the range is summed.  Workload: the
 ``outdoor-1m`` scene (1,000,000 Gaussians, SH degree 3, 160 ring views at
 1297x840, fx = fy = 1150, seeded uint8 targets).
 
@@ -86,8 +88,9 @@ def parse():
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
     ap.add_argument("--sharded-adam", action="store_true",
                     help="N > 1 over NCCL: reduce-scatter the gradient rows, run Adam on each GPU's block of rows "
-                         "and all-gather the rasterizer's columns (default: an all-reduce pipelined with a "
-                         "replicated Adam)")
+                         "and all-gather the rasterizer's columns (the default from 4 GPUs up)")
+    ap.add_argument("--replicated-adam", action="store_true",
+                    help="N > 1 over NCCL: an all-reduce pipelined with a replicated Adam (the default on 2 GPUs)")
     ap.add_argument("--allreduce-buckets", type=int, default=4,
                     help="N > 1 over NCCL: row ranges of the gradient sum, each range's Adam overlapping the later "
                          "ranges' all-reduce (1: one all-reduce, then Adam)")
@@ -637,7 +640,8 @@ def main():
                                  max_gaussians=max(wl.capacity or 0, (3 * n_init) // 2),
                                  process_group=pg, fused_reduce=args.multicast,
                                  allreduce_buckets=args.allreduce_buckets,
-                                 nccl_sharded_adam=args.sharded_adam)
+                                 nccl_sharded_adam=(True if args.sharded_adam else
+                                                    (False if args.replicated_adam else None)))
     # the targets: seeded uint8 images, one per view up to ~1 GB of pinned host memory
     # per process, cycled over the views beyond that (the large scene's 512 3840x2160
     # targets alone would take 12.7 GB per process)

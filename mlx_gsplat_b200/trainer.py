@@ -92,11 +92,12 @@ class MLXConfig:
     # write ``<scene>_mlx_custom_3dgs.ply`` when train() finishes, as the
     # reference's train() does (trainer.py:566-568)
     export_ply_on_finish: bool = False
-    # NCCL path across GPUs: the gradient rows are reduce-scattered, each GPU
-    # runs Adam for its contiguous block of active ids and the columns the
-    # rasterizer reads are all-gathered (default: an all-reduce pipelined with
-    # a replicated Adam, measured faster on two GPUs)
-    nccl_sharded_adam: bool = False
+    # NCCL path across GPUs: True — the gradient rows are reduce-scattered, each
+    # GPU runs Adam for its contiguous block of active ids and the columns the
+    # rasterizer reads are all-gathered; False — an all-reduce pipelined with a
+    # replicated Adam; None (default) — the sharded Adam from 4 GPUs up (measured
+    # faster there; on two GPUs the replicated Adam is)
+    nccl_sharded_adam: Optional[bool] = None
     # replicated-Adam NCCL path: the gradient rows are summed in this many row
     # ranges, each range's Adam running while the later ranges are reduced
     # (1: one all-reduce, then Adam)
@@ -245,7 +246,8 @@ class RunnerMLX:
         # NCCL across GPUs with a sharded Adam: rank r updates the active ids of
         # block r (distributed.block_of); the row buffers have room for the
         # padding of the last block
-        self.sharded_nccl = self.world > 1 and self.fused_reduce is None and bool(cfg.nccl_sharded_adam)
+        want = cfg.nccl_sharded_adam if cfg.nccl_sharded_adam is not None else self.world >= 4
+        self.sharded_nccl = self.world > 1 and self.fused_reduce is None and bool(want)
         if self.fused_reduce is not None:
             self.grad = self.fused_reduce.rows
         else:
