@@ -217,6 +217,32 @@ __global__ void __launch_bounds__(kBigThreads) bin_emit_big_kernel(const float4*
     }
 }
 
+// A lane counts the tiles of its own box when the box has at most
+// kLaneTiles tiles (most splats): the same exact test per tile, in the same
+// row-major order, so count and mask equal warp_bin's; larger boxes go
+// through the warp-cooperative loop.  On the 1 M-Gaussian outdoor scene
+// this took the projection kernel from 0.141 to 0.093 ms (limits of 4, 8,
+// 16, 32 and 64 tiles measured: 16 was fastest there and on the 200k scene).
+#ifndef GS_LANE_TILES
+#define GS_LANE_TILES 16
+#endif
+constexpr int kLaneTiles = GS_LANE_TILES;
+static_assert(kLaneTiles <= kMaskTiles, "a lane-counted box must fit the tile mask");
+
+__device__ __forceinline__ uint32_t lane_bin(const TileBox& tb, float u, float v, float ca, float cd,
+                                             const RasterParams& p, uint64_t& mask) {
+    uint32_t cnt = 0;
+    mask = 0;
+    int t = 0;
+    for (int ty = tb.y0; ty <= tb.y1; ++ty)
+        for (int tx = tb.x0; tx <= tb.x1; ++tx, ++t)
+            if (splat_hits_tile(u, v, ca, cd, tb, tx, ty, p)) {
+                ++cnt;
+                mask |= 1ull << t;
+            }
+    return cnt;
+}
+
 // ---------------------------------------------------------------- projection + tile count
 template <bool kSlab, int kDeg>
 __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids,
@@ -253,8 +279,14 @@ __global__ void __launch_bounds__(128) project_fwd_kernel(gs_gaussians g, const 
         ca = s.ca;
         cd = s.cd;
     }
-    uint64_t mask;
-    const uint32_t cnt = warp_bin<false>(has, tb, u, v, ca, cd, p, 0u, 0u, 0u, false, 0u, nullptr, nullptr, mask);
+    const bool small = has && (tb.x1 - tb.x0 + 1) * (tb.y1 - tb.y0 + 1) <= kLaneTiles;
+    uint64_t mask, lane_mask = 0;
+    const uint32_t lane_cnt = small ? lane_bin(tb, u, v, ca, cd, p, lane_mask) : 0u;
+    uint32_t cnt = warp_bin<false>(has && !small, tb, u, v, ca, cd, p, 0u, 0u, 0u, false, 0u, nullptr, nullptr, mask);
+    if (small) {
+        cnt = lane_cnt;
+        mask = lane_mask;
+    }
     if (active) {
         tile_counts[vi] = cnt;
         if (use_bs) bs.masks[vi] = mask;
