@@ -59,8 +59,10 @@ def test_cull_through_indirection_table_and_strided_rows():
     np.testing.assert_array_equal(ids[:V].cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("n", [1, 7, 2048, 2049, 100_003, 3_000_000])
+@pytest.mark.parametrize("n", [1, 7, 2048, 2049, 4096, 4097, 8193, 100_003, 3_000_000])
 def test_scan_exact(n):
+    """Exclusive scan with the total at out[n]: the one-CTA path (up to 4,096
+    values) and the three-kernel path."""
     lib = _lib.lib()
     rng = np.random.default_rng(n)
     x = rng.integers(0, 50, n).astype(np.int32)
