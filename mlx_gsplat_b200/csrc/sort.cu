@@ -4,8 +4,9 @@
 // digit-major; (2) a device-wide exclusive scan of those counts, which gives
 // every (digit, tile) its global output offset; (3) per tile, a stable local
 // rank of each key within its digit — warps own contiguous runs of keys and
-// rank them 32 at a time with __match_any_sync plus per-warp digit counters in
-// shared memory, then a cross-warp prefix — the tile staged in shared memory
+// rank them 32 at a time (the lanes sharing a digit found with one ballot per
+// digit bit) plus per-warp digit counters in shared memory, then a cross-warp
+// prefix — the tile staged in shared memory
 // in sorted order, and written out in that order to offset + rank, so each
 // digit's run of keys is stored by consecutive threads.
 // There is no inter-CTA waiting (reduce-then-scan), so no kernel can spin.
@@ -37,7 +38,33 @@ __global__ void __launch_bounds__(kSortThreads) radix_upsweep(const uint32_t* __
     counts[(int64_t)threadIdx.x * n_tiles + blockIdx.x] = hist[threadIdx.x];
 }
 
-__global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* __restrict__ keys_in,
+// Lanes of the warp whose keys have the same digit (``bits`` low bits of d)
+// and the same validity: one ballot per digit bit.  The warp-wide
+// match.any instruction does the same on the address-divergence pipe, which
+// limited this kernel (that pipe 67 % busy; with ballots and 5 resident CTAs
+// per SM the 3.6 M-entry tile sort of the 1 M-Gaussian step took 12 us less).
+#ifndef GS_SORT_BALLOT_MATCH
+#define GS_SORT_BALLOT_MATCH 1
+#endif
+__device__ __forceinline__ unsigned digit_peers(int d, bool valid, int bits) {
+#if GS_SORT_BALLOT_MATCH
+    const unsigned vb = __ballot_sync(kFull, valid);
+    unsigned peers = valid ? vb : ~vb;
+    for (int b = 0; b < bits; ++b) {
+        const bool on = (d >> b) & 1;
+        const unsigned bal = __ballot_sync(kFull, on);
+        peers &= on ? bal : ~bal;
+    }
+    return peers;
+#else
+    return __match_any_sync(kFull, valid ? d : kBins);
+#endif
+}
+
+#ifndef GS_SORT_MIN_CTAS
+#define GS_SORT_MIN_CTAS 5
+#endif
+__global__ void __launch_bounds__(kSortThreads, GS_SORT_MIN_CTAS) radix_downsweep(const uint32_t* __restrict__ keys_in,
                                                                 const uint32_t* __restrict__ vals_in,
                                                                 uint32_t* __restrict__ keys_out,
                                                                 uint32_t* __restrict__ vals_out, int64_t n, int shift,
@@ -58,6 +85,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
     const int64_t tbase = (int64_t)blockIdx.x * kSortTile;
     const int64_t wbase = tbase + (int64_t)warp * (32 * kSortItems);
     const unsigned lt = lanemask_lt();
+    const int bits = __popc(mask);
     uint32_t key[kSortItems], val[kSortItems], rank[kSortItems];
     int dig[kSortItems];
 #pragma unroll
@@ -68,7 +96,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep(const uint32_t* 
         val[r] = valid ? (vals_in ? vals_in[i] : (uint32_t)i) : 0u;  // no values: the input positions
         const int d = valid ? (int)((key[r] >> shift) & mask) : kBins;  // invalid lanes form their own group
         dig[r] = d;
-        const unsigned peers = __match_any_sync(kFull, d);
+        const unsigned peers = digit_peers(d, valid, bits);
         const uint32_t before = __popc(peers & lt);
         const uint32_t prior = valid ? wcnt[warp][d] : 0u;
         __syncwarp();
