@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -42,6 +43,26 @@ inline int check_launch(const char* what, int launched = 1) {
     } while (0)
 
 inline unsigned grid_for(int64_t n, int block) { return (unsigned)((n + block - 1) / block); }
+
+// Streaming multiprocessors of the current device (queried once per device).
+inline int sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = 0;
+    }
+    std::atomic<int>* c = dev >= 0 && dev < 64 ? &cache[dev] : nullptr;
+    int n = c ? c->load(std::memory_order_relaxed) : 0;
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        if (c) c->store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 
 // Programmatic dependent launch (sm_90+): a kernel launched with launch_pdl may
 // be scheduled as soon as every block of the previous kernel in its stream has

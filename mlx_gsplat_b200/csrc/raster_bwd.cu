@@ -5,21 +5,23 @@
 
 namespace gs {
 
-// Compositing layout (CompositeLayout): pixels per thread, batch and register budget.
-#ifndef GS_BWD_PX
-#define GS_BWD_PX 4
-#endif
-#ifndef GS_BWD_MIN_CTAS
-#define GS_BWD_MIN_CTAS 16
-#endif
-#ifndef GS_BWD_BATCH
-#define GS_BWD_BATCH 128
-#endif
-using Layout = CompositeLayout<GS_BWD_PX>;
-constexpr int kRenderThreads = Layout::threads;
-constexpr int kPairs = Layout::pairs;
-constexpr int kBatch = GS_BWD_BATCH;  // splats staged in shared memory per batch
-static_assert(kBatch % kRenderThreads == 0 && kBatch % 32 == 0, "batch must tile the CTA");
+// Compositing layouts (CompositeLayout), chosen per launch: 4 pixels per
+// thread (64-thread CTAs, 16 per SM at 64 registers) when the image has at
+// least one full wave of tiles; 2 pixels per thread (128-thread CTAs, 10 per
+// SM at 48 registers) below that, where twice the warps per tile keep the
+// SMs busy.  Measured: 2 pixels per thread took the 200k-Gaussian 648x420
+// step's backward from 0.427 to 0.375 ms (1,161 tiles), and the 1 M-Gaussian
+// 1297x840 one's from 1.263 to 1.491 ms (4,346 tiles).
+constexpr int kBwdMinCtas4 = 16, kBwdMinCtas2 = 10;
+template <int P>
+struct BwdLayout {
+    using L = CompositeLayout<P>;
+    static constexpr int threads = L::threads, pairs = L::pairs;
+    static constexpr int min_ctas = P == 4 ? kBwdMinCtas4 : kBwdMinCtas2;
+};
+constexpr int kBatch = 128;  // splats staged in shared memory per batch
+static_assert(kBatch % BwdLayout<2>::threads == 0 && kBatch % BwdLayout<4>::threads == 0 && kBatch % 32 == 0,
+              "batch must tile the CTA");
 
 constexpr int kGradRec = 12;  // floats per splat gradient record
 
@@ -167,18 +169,14 @@ __device__ __forceinline__ void pair_bwd_step_fast(PairBwd<kDA>& s, bool v0, boo
     pair_bwd_accum<kDA>(s, al, gv, y, c, sd, sy, syy, sr, sg, sb);
 }
 
-// GS_BWD_MIN_CTAS > 0 asks the register allocator for that many resident CTAs per SM
-#if GS_BWD_MIN_CTAS > 0
-#define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads, GS_BWD_MIN_CTAS)
-#else
-#define GS_BWD_BOUNDS __launch_bounds__(kRenderThreads)
-#endif
-template <bool kDA, bool kMask>
-__global__ void GS_BWD_BOUNDS render_bwd_kernel(
+template <int P, bool kDA, bool kMask>
+__global__ void __launch_bounds__(BwdLayout<P>::threads, BwdLayout<P>::min_ctas) render_bwd_kernel(
     const gs_tile_range* __restrict__ ranges, const int32_t* __restrict__ tile_order, const uint32_t* __restrict__ vals, const float4* __restrict__ splats,
     int64_t nv, RasterParams p, const float* __restrict__ out_color, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, int loss_mode, const void* __restrict__ target,
     const float* __restrict__ dL_dcolor, const float* __restrict__ dL_dalpha, float* __restrict__ splat_grads) {
+    using Layout = typename BwdLayout<P>::L;
+    constexpr int kRenderThreads = BwdLayout<P>::threads, kPairs = BwdLayout<P>::pairs;
     __shared__ float4 s0[kBatch], s1[kBatch], s2[kBatch];
     __shared__ uint32_t sv[kBatch];
     __shared__ float acc[kBatch][9];  // per-batch CTA sums of the splat gradients
@@ -643,9 +641,15 @@ extern "C" int gs_render_backward(const gs_tile_range* ranges, const int32_t* ti
     const int tiles = p.tiles_x * p.tiles_y;
     // the alpha cotangent is carried per pixel only when the caller passes one
     const bool da = loss_mode == GS_LOSS_NONE && dL_dalpha;
-    auto kernel = p.masked ? (da ? render_bwd_kernel<true, true> : render_bwd_kernel<false, true>)
-                           : (da ? render_bwd_kernel<true, false> : render_bwd_kernel<false, false>);
-    kernel<<<tiles, kRenderThreads, 0, (cudaStream_t)stream>>>(
+    // fewer tiles than one wave of 4-pixel CTAs: the 2-pixel layout
+    const bool px2 = tiles < sm_count() * kBwdMinCtas4;
+#define GS_RBWD(P)                                                                                        \
+    (p.masked ? (da ? render_bwd_kernel<P, true, true> : render_bwd_kernel<P, false, true>)             \
+              : (da ? render_bwd_kernel<P, true, false> : render_bwd_kernel<P, false, false>))
+    auto kernel = px2 ? GS_RBWD(2) : GS_RBWD(4);
+#undef GS_RBWD
+    const int threads = px2 ? BwdLayout<2>::threads : BwdLayout<4>::threads;
+    kernel<<<tiles, threads, 0, (cudaStream_t)stream>>>(
         ranges, tile_order, entry_vals, reinterpret_cast<const float4*>(splats), num_visible, p, out_color, final_T,
         n_contrib, loss_mode, target, dL_dcolor, dL_dalpha, splat_grads);
     return check_launch("render_bwd_kernel");
