@@ -369,8 +369,12 @@ inline bool slab_grad_rows(const gs_gaussian_grads& o) {
            (reinterpret_cast<uintptr_t>(o.quats) & 15u) == 0;
 }
 
+// Degree <= 1 colour (the reference's SH mode): 8 resident CTAs per SM (64
+// registers, a few spilled) instead of 4 at 105 registers took the 1 M-Gaussian
+// step's projection backward from 0.069 to 0.057 ms; the degree 2-3 kernels
+// spill hundreds of bytes at that budget and keep the default.
 template <bool kSlabIn, bool kSlabOut, int kDeg>
-__global__ void __launch_bounds__(128) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
+__global__ void __launch_bounds__(128, kDeg == 1 ? 8 : 1) project_bwd_kernel(gs_gaussians g, const int32_t* __restrict__ ids, int64_t nv,
                                                           RasterParams p, const float* __restrict__ splat_grads,
                                                           gs_gaussian_grads o, float* __restrict__ grad2d,
                                                           float* __restrict__ count) {
