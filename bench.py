@@ -86,11 +86,13 @@ def parse():
                          "broadcast, instead of an NCCL all-reduce and a replicated Adam")
     ap.add_argument("--gaussians", type=int, default=None, help="override the workload's Gaussian count (profiling)")
     ap.add_argument("--views", type=int, default=None, help="override the workload's view count (profiling)")
-    ap.add_argument("--sharded-adam", action="store_true",
-                    help="N > 1 over NCCL: reduce-scatter the gradient rows, run Adam on each GPU's block of rows "
-                         "and all-gather the rasterizer's columns (the default from 4 GPUs up)")
-    ap.add_argument("--replicated-adam", action="store_true",
-                    help="N > 1 over NCCL: an all-reduce pipelined with a replicated Adam (the default on 2 GPUs)")
+    nccl_path = ap.add_mutually_exclusive_group()
+    nccl_path.add_argument("--sharded-adam", action="store_true",
+                           help="N > 1 over NCCL: reduce-scatter the gradient rows, run Adam on each GPU's block of "
+                                "rows and all-gather the rasterizer's columns (the default from 4 GPUs up)")
+    nccl_path.add_argument("--replicated-adam", action="store_true",
+                           help="N > 1 over NCCL: an all-reduce pipelined with a replicated Adam (the default on 2 "
+                                "GPUs)")
     ap.add_argument("--allreduce-buckets", type=int, default=4,
                     help="N > 1 over NCCL: row ranges of the gradient sum, each range's Adam overlapping the later "
                          "ranges' all-reduce (1: one all-reduce, then Adam)")

@@ -208,6 +208,22 @@ def block_of(n_rows: int, rank: int, world: int):
     return first, max(0, min(per, n_rows - first)), per
 
 
+SHARDED_NCCL_ADAM_MIN_WORLD = 4
+
+
+def use_sharded_nccl_adam(setting, world: int, multicast: bool = False) -> bool:
+    """Which NCCL path sums the gradient rows of a group of ``world`` GPUs:
+    True — reduce-scatter, Adam on this GPU's block of rows, all-gather of the
+    rasterizer's columns; False — an all-reduce with a replicated Adam.
+    ``setting`` True / False forces one; None picks the sharded Adam from
+    SHARDED_NCCL_ADAM_MIN_WORLD GPUs up (on 2 GPUs the replicated Adam measured
+    faster, 705 against 682 steps/s; on 4 the sharded one, 1387 against 1354).
+    Neither runs on one GPU or with the NVLink multicast sum."""
+    if world <= 1 or multicast:
+        return False
+    return bool(setting) if setting is not None else world >= SHARDED_NCCL_ADAM_MIN_WORLD
+
+
 def init_from_env(backend: str = "nccl", timeout_s: float = 180.0):
     """Initialise the default process group from torchrun's environment
     (RANK, WORLD_SIZE, LOCAL_RANK, MASTER_ADDR/PORT); returns (rank, world,

@@ -246,8 +246,8 @@ class RunnerMLX:
         # NCCL across GPUs with a sharded Adam: rank r updates the active ids of
         # block r (distributed.block_of); the row buffers have room for the
         # padding of the last block
-        want = cfg.nccl_sharded_adam if cfg.nccl_sharded_adam is not None else self.world >= 4
-        self.sharded_nccl = self.world > 1 and self.fused_reduce is None and bool(want)
+        self.sharded_nccl = distributed.use_sharded_nccl_adam(cfg.nccl_sharded_adam, self.world,
+                                                              multicast=self.fused_reduce is not None)
         if self.fused_reduce is not None:
             self.grad = self.fused_reduce.rows
         else:

@@ -242,3 +242,14 @@ def test_row_blocks_cover_every_row_once():
                 assert count <= per and per * w >= n
                 seen += list(range(first, first + count))
             assert seen == list(range(n)), (n, w)
+
+
+def test_nccl_path_choice():
+    """The NCCL gradient path: the replicated Adam on 2 GPUs, the sharded one
+    from 4 up, either forced by the setting, neither on one GPU or with the
+    NVLink multicast sum."""
+    from mlx_gsplat_b200 import distributed as D
+    assert [D.use_sharded_nccl_adam(None, w) for w in (1, 2, 3, 4, 8)] == [False, False, False, True, True]
+    assert D.use_sharded_nccl_adam(True, 2) and not D.use_sharded_nccl_adam(False, 8)
+    assert not D.use_sharded_nccl_adam(True, 1)
+    assert not D.use_sharded_nccl_adam(None, 8, multicast=True) and not D.use_sharded_nccl_adam(True, 4, True)
